@@ -1,0 +1,243 @@
+/*
+ * nvmoe_b200 — C ABI of the B200 (sm_100a) routed-expert FFN over a VRAM expert-slot cache.
+ *
+ * Plain pointers and sizes only.  Every entry point returns an int status (NVMOE_OK == 0,
+ * negative on error) and never aborts the process.  Device pointers are CUDA device (or
+ * managed) addresses; "stream" arguments are cudaStream_t values passed as void*.
+ * Kernels that detect bad data on the device (an expert id out of range, more distinct ids
+ * than slots) write a status word the host reads back (see nvmoe_miss_list.counts).
+ *
+ * Reference interfaces these entry points replace (paths inside Waltarb/nvmoe):
+ *   - llama.cpp engine: `static bool eval_cb(ggml_tensor*, bool ask, void*)`
+ *       scripts/moe_cache_probe.cpp:439-997  (remap, host tier, H2D fill, id rewrite)
+ *   - Python engine hook `NvmeOffloadMoeCache` (nvme-moe-bench/nvme_offload_cache.py:441):
+ *       ensure_experts :1366, copy_missing :1684, bank_views :954, and the GEMM call
+ *       `_expert_gemm(cache, hidden, topk_weights, slot_ids, views, n, alphas, is_prefill)`
+ *       :1989-1998 / :2165-2174.
+ */
+#ifndef NVMOE_B200_H
+#define NVMOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define NVMOE_OK 0
+#define NVMOE_ERR_INVALID_ARG -1    /* bad pointer / size / enum on the host side */
+#define NVMOE_ERR_BAD_EXPERT_ID -2  /* an id outside [0, n_expert) reached the remap */
+#define NVMOE_ERR_CACHE_OVERFLOW -3 /* more distinct ids in one call than slots */
+#define NVMOE_ERR_CUDA -4           /* a CUDA runtime call failed (see nvmoe_last_error) */
+#define NVMOE_ERR_WORKSPACE -5      /* workspace pointer null or too small */
+#define NVMOE_ERR_UNSUPPORTED -6    /* shape / format combination not built */
+#define NVMOE_ERR_HOST_LOAD -7      /* the host-tier loader callback reported a failure */
+#define NVMOE_ERR_BAD_SLOT -8       /* a slot id outside [0, n_slots) reached the FFN */
+#define NVMOE_ERR_NO_TABLES -9      /* IQ2_XXS grid table not registered */
+
+typedef void* nvmoe_stream_t; /* cudaStream_t */
+typedef void* nvmoe_event_t;  /* cudaEvent_t  */
+
+/* Weight formats of the slot pool.  NVMOE_Q_NVFP4 is the FTW bank layout of the Python
+ * engine (nvme_offload_cache.py:824-835): codes [rows, K/2] u8 with w[2b] in the low nibble
+ * of byte b, one E4M3 scale per 16 values [rows, K/16], one fp32 global per slot and matrix.
+ * NVMOE_Q_Q2_K / NVMOE_Q_IQ2_XXS are ggml super-blocks of 256 values (84 / 66 bytes). */
+enum nvmoe_quant {
+    NVMOE_Q_NVFP4 = 0,
+    NVMOE_Q_Q2_K = 1,
+    NVMOE_Q_IQ2_XXS = 2,
+};
+
+/* ---------------------------------------------------------------- error text */
+/* Text of the last CUDA error seen by this thread inside the library (static storage). */
+const char* nvmoe_last_error(void);
+/* Library version string, e.g. "nvmoe_b200 0.1.0 sm_100a". */
+const char* nvmoe_version(void);
+
+/* ================================================================ R1: router top-k
+ * Replaces the router epilogue in front of the expert cache:
+ *   llama.cpp softmax -> argsort_top_k -> get_rows -> sum/div  (scripts/test_sched_chain_shrink.cpp:108-121)
+ *   GLM sigmoid + e_score_correction_bias -> topk -> gather -> normalize -> * routed_scaling_factor
+ *     (nvme-moe-bench/nvme_offload_cache.py:3044-3089)
+ * mode NVMOE_ROUTER_SOFTMAX: ids = top_k of logits (ties -> lower expert id);
+ *   weights = softmax restricted to the chosen logits (the renormalised softmax top-k),
+ *   or the full-softmax probabilities when norm_topk == 0.
+ * mode NVMOE_ROUTER_SIGMOID_BIAS: s = sigmoid(logit); ids = top_k of s + bias[e];
+ *   weights = s[ids] (/ (sum + 1e-20) when norm_topk) * routed_scaling.
+ * Ids come out in descending key order.  n_expert <= 1024, top_k <= 32. */
+enum nvmoe_router_mode {
+    NVMOE_ROUTER_SOFTMAX = 0,
+    NVMOE_ROUTER_SIGMOID_BIAS = 1,
+};
+int nvmoe_router_topk(const float* logits, int64_t logits_row_stride, int n_tok, int n_expert,
+                      int top_k, int mode, const float* bias, int norm_topk, float routed_scaling,
+                      int32_t* out_ids, int64_t ids_row_stride, float* out_weights,
+                      int64_t weights_row_stride, nvmoe_stream_t stream);
+
+/* ================================================================ R2/R3/R6: slot remap
+ * Device-resident slot tables of one slot pool (one layer in the llama.cpp engine:
+ * layer_cache.slot_of_real / real_in_slot / slot_last_used / current_step,
+ * scripts/moe_cache_probe.cpp:237-241).  All arrays are device memory owned by the caller. */
+typedef struct nvmoe_slot_table {
+    int32_t* slot_of_real;    /* [n_expert]   slot holding expert e, -1 = not resident   */
+    int32_t* real_in_slot;    /* [cache_size] expert in slot s, -1 = empty               */
+    uint32_t* slot_last_used; /* [cache_size] step of the last use of slot s             */
+    uint32_t* current_step;   /* [1]          incremented once per remap call            */
+    int32_t n_expert;         /* ids are valid in [0, n_expert)                          */
+    int32_t cache_size;       /* number of slots                                         */
+    int32_t pinned_k;         /* decode calls look for victims in [pinned_k, cache_size) first */
+    int32_t id_base;          /* added to every id before the lookup (global pools: layer*E) */
+} nvmoe_slot_table;
+
+/* Outputs of one remap call (device memory, capacity >= n_tok*top_k entries each). */
+typedef struct nvmoe_miss_list {
+    int32_t* unique_ids;  /* distinct ids in first-occurrence order                     */
+    int32_t* unique_slot; /* slot of each distinct id after the call                    */
+    uint8_t* unique_hit;  /* 1 = the id was resident before the call                    */
+    int32_t* miss_ids;    /* ids that were not resident, in first-occurrence order      */
+    int32_t* miss_slots;  /* slot chosen for each miss                                  */
+    int32_t* evicted_ids; /* previous occupant (as stored: id_base + id), -1 = was empty */
+    int32_t* counts;      /* [4]: n_unique, n_miss, status (NVMOE_OK or error), n_ids   */
+    int32_t capacity;     /* entries allocated in each list                             */
+} nvmoe_miss_list;
+
+/* One remap call == the GPU-tier part of eval_cb (scripts/moe_cache_probe.cpp:627-753,
+ * 955-970): distinct ids in first-occurrence order; hits refresh slot_last_used; each miss,
+ * in order, takes the first empty slot of [start, cache_size), else the slot with the oldest
+ * slot_last_used (ties -> lowest slot) whose occupant is not among this call's ids, where
+ * start = pinned_k for decode calls and 0 otherwise, falling back to [0, start); finally every
+ * id is rewritten to its slot.  ids are read with a row stride in bytes (ggml nb[1]); out may
+ * alias ids.  On a bad id or overflow nothing is modified and counts[2] holds the error. */
+int nvmoe_remap(const nvmoe_slot_table* table, const int32_t* ids, int64_t ids_row_stride_bytes,
+                int top_k, int n_tok, int is_decode, int32_t* out_slots,
+                int64_t out_row_stride_bytes, const nvmoe_miss_list* misses,
+                nvmoe_stream_t stream);
+
+/* ================================================================ R8: dequant to memory
+ * Bit-exact dequantisation (fp32 out) used by the parity tests and loaders.
+ * NVFP4 (FTW banks): out[r, c] = (e2m1(code) * e4m3(scale[r, c/16])) * global  (global may be NULL = 1).
+ * Q2_K / IQ2_XXS: ggml block formats, 256 values per block, same operation order as ggml's
+ * dequantize_row_* (fp32 products, two roundings for Q2_K: d*sc*q - dmin*m). */
+int nvmoe_dequant_nvfp4(const uint8_t* codes, const uint8_t* scales, const float* global_scale,
+                        int64_t n_rows, int64_t n_cols, float* out, nvmoe_stream_t stream);
+int nvmoe_dequant_q2_k(const void* blocks, int64_t n_blocks, float* out, nvmoe_stream_t stream);
+int nvmoe_dequant_iq2_xxs(const void* blocks, int64_t n_blocks, float* out,
+                          nvmoe_stream_t stream);
+
+/* Registers the IQ2_XXS codebook (256 entries x 8 magnitudes, bytes) on the current device.
+ * The grid is ggml's iq2xxs_grid; callers pass the copy shipped with gguf-py (or ggml). */
+int nvmoe_set_iq2xxs_grid(const uint8_t* grid_256x8);
+
+/* ================================================================ R7/R9: routed-expert FFN
+ * One quantised matrix bank of a slot pool: slot s of the matrix starts at
+ * base + s * slot_stride bytes; its rows are row_stride bytes apart.  For NVFP4 the codes,
+ * e4m3 scales and fp32 global are three separate banks (FTW layout); for Q2_K / IQ2_XXS
+ * scale/global are NULL. */
+typedef struct nvmoe_matrix_bank {
+    const void* data;
+    int64_t slot_stride; /* bytes between slots                      */
+    int64_t row_stride;  /* bytes between rows of one slot           */
+    const void* scale;   /* NVFP4: e4m3 [rows, K/16] per slot         */
+    int64_t scale_slot_stride;
+    int64_t scale_row_stride;
+    const float* global_scale; /* NVFP4: [n_slots] fp32 (stride global_stride), may be NULL */
+    int64_t global_stride;     /* in floats                                                 */
+} nvmoe_matrix_bank;
+
+/* The three matrices of one expert pool: gate [I, H], up [I, H], down [H, I].
+ * FTW fused banks (gate_up_packed [S, 2I, H/2]): gate = rows [0, I), up = rows [I, 2I) of the
+ * same bank, i.e. up.data = gate.data + I*row_stride with the same slot stride. */
+typedef struct nvmoe_expert_pool {
+    int32_t quant;  /* enum nvmoe_quant                         */
+    int32_t hidden; /* H                                        */
+    int32_t inter;  /* I                                        */
+    int32_t n_slots;
+    nvmoe_matrix_bank gate, up, down;
+} nvmoe_expert_pool;
+
+/* Arguments of one FFN call.  y[t] = sum_j w[t,j] * down_s( silu(gate_s x[t]) * up_s x[t] ),
+ * s = slot_ids[t, j]; plus, when `shared` is set, the always-on shared expert (slot 0 of that
+ * pool) with weight 1, or sigmoid(x[t] . shared_gate) when shared_gate (bf16 [H]) is set
+ * (nvme_offload_cache.py:2115-2123).  fp32 accumulation, bf16 in / out. */
+typedef struct nvmoe_ffn_args {
+    const nvmoe_expert_pool* pool;   /* routed experts                       */
+    const nvmoe_expert_pool* shared; /* may be NULL                          */
+    const uint16_t* shared_gate;     /* bf16 [H], may be NULL                */
+    const uint16_t* x;               /* bf16 [n_tok, H]                      */
+    int64_t x_row_stride;            /* elements                             */
+    const int32_t* slot_ids;         /* [n_tok, top_k] slot ids              */
+    int64_t ids_row_stride;          /* elements                             */
+    const float* weights;            /* [n_tok, top_k] combine weights       */
+    int64_t weights_row_stride;      /* elements                             */
+    int32_t top_k;
+    int32_t n_tok;
+    uint16_t* y;          /* bf16 [n_tok, H]                                  */
+    int64_t y_row_stride; /* elements                                         */
+    void* workspace;      /* device scratch, >= nvmoe_moe_ffn_workspace_size  */
+    size_t workspace_bytes;
+    int32_t* status;      /* optional device int: NVMOE_ERR_BAD_SLOT on a bad slot id */
+} nvmoe_ffn_args;
+
+size_t nvmoe_moe_ffn_workspace_size(int n_tok, int top_k, int hidden, int inter, int n_slots);
+int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
+
+/* ================================================================ R4: host tier (SLRU)
+ * Segmented LRU of the pinned host tier (nvme_offload_cache.py:333-409;
+ * scripts/segmented_host_lru.hpp:85-160): probation queue for first references, protected
+ * queue (capacity max(1, floor(capacity*ratio)), first capacity hint wins) for keys touched
+ * again; eviction drains probation's LRU end first.  Keys are int64. */
+typedef struct nvmoe_slru nvmoe_slru;
+nvmoe_slru* nvmoe_slru_create(double protected_ratio);
+void nvmoe_slru_destroy(nvmoe_slru* lru);
+void nvmoe_slru_set_capacity_hint(nvmoe_slru* lru, int64_t capacity);
+void nvmoe_slru_insert_new(nvmoe_slru* lru, int64_t key);
+void nvmoe_slru_touch(nvmoe_slru* lru, int64_t key);
+int nvmoe_slru_contains(const nvmoe_slru* lru, int64_t key);
+int64_t nvmoe_slru_size(const nvmoe_slru* lru);
+/* Pops probation's LRU key, else protected's; returns 0 and the key, or -1 when empty. */
+int nvmoe_slru_pop_lru(nvmoe_slru* lru, int64_t* key_out);
+/* Pops the least recent key not in protect[0..n) (probation first, then protected); when every
+ * key is protected falls back to nvmoe_slru_pop_lru (segmented_host_lru.hpp:130-141). */
+int nvmoe_slru_pop_lru_excluding(nvmoe_slru* lru, const int64_t* protect, int n_protect,
+                                 int64_t* key_out);
+void nvmoe_slru_discard(nvmoe_slru* lru, int64_t key);
+
+/* ================================================================ R5: pinned-host refill
+ * One bank of an expert row in both tiers: slot s of the device pool starts at
+ * dst + s*dst_slot_stride, host slot h of the pinned tier at src + h*src_slot_stride; each
+ * copy moves row_bytes.  (gpu_fill_from_host_async, scripts/moe_cache_probe.cpp:377-404;
+ * fast_index_copy_multi_jit plan, nvme_offload_cache.py:930-949.) */
+typedef struct nvmoe_refill_bank {
+    void* dst;
+    const void* src;
+    int64_t dst_slot_stride;
+    int64_t src_slot_stride;
+    int64_t row_bytes;
+} nvmoe_refill_bank;
+
+/* Issues one cudaMemcpyAsync per (bank, run of consecutive slot pairs) on copy_stream (host
+ * arrays gpu_slots / host_slots of length n).  When compute_stream and done are given, `done`
+ * is first recorded on compute_stream and waited on by copy_stream (an evicted slot may still
+ * be read by FFN work queued there), then recorded on copy_stream after the copies and waited
+ * on by compute_stream.  Bounds-checked against n_gpu_slots / n_host_slots; host memory must
+ * be pinned for the copies to be asynchronous.  compute_stream / done may be NULL. */
+int nvmoe_refill_async(const nvmoe_refill_bank* banks, int n_banks, const int32_t* gpu_slots,
+                       const int32_t* host_slots, int n, int32_t n_gpu_slots,
+                       int32_t n_host_slots, nvmoe_stream_t copy_stream,
+                       nvmoe_stream_t compute_stream, nvmoe_event_t done);
+
+/* Device-driven variant for graph capture: reads n_miss = counts[1], miss_slots[] and the
+ * host slot of each miss (host_slot_of_id[miss_ids[m]]) from device memory and copies with
+ * an SM kernel from mapped pinned host memory (src pointers must be device-accessible
+ * mappings).  Misses whose host slot is negative are skipped and reported in counts[2]. */
+int nvmoe_refill_gather(const nvmoe_refill_bank* banks, int n_banks, const nvmoe_miss_list* misses,
+                        const int32_t* host_slot_of_id, int32_t n_gpu_slots,
+                        nvmoe_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* NVMOE_B200_H */

@@ -1,0 +1,300 @@
+"""Torch-facing wrappers over the C ABI (device tensors in, device tensors out).
+
+Every function launches the sm_100a kernels of libnvmoe_b200.so on the current CUDA stream and
+raises NvmoeError on a non-zero status; nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .formats import ExpertWeights, QuantMatrix
+
+_QUANT = {"nvfp4": _lib.NVMOE_Q_NVFP4, "q2_k": _lib.NVMOE_Q_Q2_K, "iq2_xxs": _lib.NVMOE_Q_IQ2_XXS}
+
+
+def _stream(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("nvmoe_b200 ops take CUDA tensors (there is no CPU path)")
+
+
+# ------------------------------------------------------------------ R1 router
+def router_topk(logits: torch.Tensor, top_k: int, mode: str = "softmax",
+                bias: torch.Tensor | None = None, norm_topk: bool = True,
+                routed_scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """ids int32 [n, k] and combine weights fp32 [n, k] from fp32 logits [n, E]."""
+    _require_cuda(logits, bias)
+    assert logits.dtype == torch.float32 and logits.dim() == 2 and logits.stride(1) == 1
+    n, E = logits.shape
+    ids = torch.empty((n, top_k), dtype=torch.int32, device=logits.device)
+    w = torch.empty((n, top_k), dtype=torch.float32, device=logits.device)
+    m = _lib.NVMOE_ROUTER_SOFTMAX if mode == "softmax" else _lib.NVMOE_ROUTER_SIGMOID_BIAS
+    if bias is not None:
+        bias = bias.float().contiguous()
+    check(lib().nvmoe_router_topk(logits.data_ptr(), logits.stride(0), n, E, top_k, m,
+                                  _ptr(bias), int(norm_topk), float(routed_scaling),
+                                  ids.data_ptr(), top_k, w.data_ptr(), top_k, _stream()),
+          "nvmoe_router_topk")
+    return ids, w
+
+
+# ------------------------------------------------------------------ R2/R3/R6 remap
+@dataclass
+class SlotTableGPU:
+    """Device slot tables of one pool (llama.cpp engine layer_cache, moe_cache_probe.cpp:237-241).
+    For a global pool (Python engine) pass n_expert = L*E and use id_base = layer*E."""
+    n_expert: int
+    cache_size: int
+    device: torch.device | str = "cuda"
+    pinned_k: int = 0
+    slot_of_real: torch.Tensor = field(init=False)
+    real_in_slot: torch.Tensor = field(init=False)
+    last_used: torch.Tensor = field(init=False)
+    step: torch.Tensor = field(init=False)
+
+    def __post_init__(self):
+        d = self.device
+        self.slot_of_real = torch.full((self.n_expert,), -1, dtype=torch.int32, device=d)
+        self.real_in_slot = torch.full((self.cache_size,), -1, dtype=torch.int32, device=d)
+        self.last_used = torch.zeros((self.cache_size,), dtype=torch.int32, device=d)  # uint32 bits
+        self.step = torch.zeros((1,), dtype=torch.int32, device=d)                   # uint32 bits
+
+    def reset(self) -> None:
+        self.slot_of_real.fill_(-1)
+        self.real_in_slot.fill_(-1)
+        self.last_used.zero_()
+        self.step.zero_()
+
+    def struct(self, n_expert: int | None = None, id_base: int = 0) -> _lib.SlotTable:
+        return _lib.SlotTable(self.slot_of_real.data_ptr(), self.real_in_slot.data_ptr(),
+                              self.last_used.data_ptr(), self.step.data_ptr(),
+                              self.n_expert if n_expert is None else n_expert, self.cache_size,
+                              self.pinned_k, id_base)
+
+
+@dataclass
+class MissListGPU:
+    capacity: int
+    device: torch.device | str = "cuda"
+
+    def __post_init__(self):
+        d, c = self.device, self.capacity
+        self.unique_ids = torch.empty(c, dtype=torch.int32, device=d)
+        self.unique_slot = torch.empty(c, dtype=torch.int32, device=d)
+        self.unique_hit = torch.empty(c, dtype=torch.uint8, device=d)
+        self.miss_ids = torch.empty(c, dtype=torch.int32, device=d)
+        self.miss_slots = torch.empty(c, dtype=torch.int32, device=d)
+        self.evicted_ids = torch.empty(c, dtype=torch.int32, device=d)
+        self.counts = torch.zeros(4, dtype=torch.int32, device=d)
+
+    def struct(self) -> _lib.MissList:
+        return _lib.MissList(self.unique_ids.data_ptr(), self.unique_slot.data_ptr(),
+                             self.unique_hit.data_ptr(), self.miss_ids.data_ptr(),
+                             self.miss_slots.data_ptr(), self.evicted_ids.data_ptr(),
+                             self.counts.data_ptr(), self.capacity)
+
+    def to_host(self) -> dict:
+        c = self.counts.cpu().tolist()
+        u, m = c[0], c[1]
+        return {
+            "n_unique": u, "n_miss": m, "status": c[2],
+            "unique_ids": self.unique_ids[:u].cpu().numpy(),
+            "unique_slot": self.unique_slot[:u].cpu().numpy(),
+            "unique_hit": self.unique_hit[:u].cpu().numpy(),
+            "miss_ids": self.miss_ids[:m].cpu().numpy(),
+            "miss_slots": self.miss_slots[:m].cpu().numpy(),
+            "evicted": self.evicted_ids[:m].cpu().numpy(),
+        }
+
+
+def remap(table: SlotTableGPU, ids: torch.Tensor, is_decode: bool,
+          out: torch.Tensor | None = None, misses: MissListGPU | None = None,
+          id_base: int = 0, n_expert: int | None = None) -> tuple[torch.Tensor, MissListGPU]:
+    """Rewrite expert ids [n_tok, k] (rows may be strided, e.g. a column slice) to slots.
+    `out` may be `ids` itself (in-place rewrite, like eval_cb's write-back)."""
+    _require_cuda(ids)
+    assert ids.dtype == torch.int32 and ids.dim() == 2 and ids.stride(1) == 1
+    n_tok, k = ids.shape
+    if out is None:
+        out = torch.empty((n_tok, k), dtype=torch.int32, device=ids.device)
+    cap = max(1, min(n_tok * k, n_expert or table.n_expert))
+    if misses is None or misses.capacity < cap:
+        misses = MissListGPU(max(cap, n_tok * k), ids.device)
+    t = table.struct(n_expert=n_expert, id_base=id_base)
+    m = misses.struct()
+    check(lib().nvmoe_remap(C.byref(t), ids.data_ptr(), ids.stride(0) * 4, k, n_tok,
+                            int(is_decode), out.data_ptr(), out.stride(0) * 4, C.byref(m),
+                            _stream()), "nvmoe_remap")
+    return out, misses
+
+
+# ------------------------------------------------------------------ R8 dequant
+def dequant_nvfp4(codes: torch.Tensor, scales: torch.Tensor,
+                  glob: torch.Tensor | None = None) -> torch.Tensor:
+    _require_cuda(codes, scales, glob)
+    rows = codes.numel() // codes.shape[-1]
+    cols = codes.shape[-1] * 2
+    out = torch.empty((*codes.shape[:-1], cols), dtype=torch.float32, device=codes.device)
+    check(lib().nvmoe_dequant_nvfp4(codes.contiguous().data_ptr(), scales.contiguous().data_ptr(),
+                                    _ptr(glob), rows, cols, out.data_ptr(), _stream()),
+          "nvmoe_dequant_nvfp4")
+    return out
+
+
+def dequant_q2_k(blocks: torch.Tensor) -> torch.Tensor:
+    _require_cuda(blocks)
+    nb = blocks.numel() // 84
+    out = torch.empty(nb * 256, dtype=torch.float32, device=blocks.device)
+    check(lib().nvmoe_dequant_q2_k(blocks.contiguous().data_ptr(), nb, out.data_ptr(), _stream()),
+          "nvmoe_dequant_q2_k")
+    return out
+
+
+_grid_devices: set[int] = set()
+
+
+def ensure_iq2xxs_grid(device: torch.device | int | None = None) -> None:
+    """Registers ggml's IQ2_XXS codebook (from gguf-py) on the device, once."""
+    from .formats import iq2xxs_grid
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index or 0
+    if dev in _grid_devices:
+        return
+    import numpy as np
+    g = np.ascontiguousarray(iq2xxs_grid())
+    with torch.cuda.device(dev):
+        check(lib().nvmoe_set_iq2xxs_grid(g.ctypes.data), "nvmoe_set_iq2xxs_grid")
+    _grid_devices.add(dev)
+
+
+def dequant_iq2_xxs(blocks: torch.Tensor) -> torch.Tensor:
+    _require_cuda(blocks)
+    ensure_iq2xxs_grid(blocks.device)
+    nb = blocks.numel() // 66
+    out = torch.empty(nb * 256, dtype=torch.float32, device=blocks.device)
+    check(lib().nvmoe_dequant_iq2_xxs(blocks.contiguous().data_ptr(), nb, out.data_ptr(),
+                                      _stream()), "nvmoe_dequant_iq2_xxs")
+    return out
+
+
+# ------------------------------------------------------------------ R7/R9 FFN
+def _matrix_bank(m: QuantMatrix, row0: int) -> _lib.MatrixBank:
+    d = m.data
+    rs = d.stride(1)
+    data = d.data_ptr() + row0 * rs
+    if m.scale is not None:
+        s = m.scale
+        scale = s.data_ptr() + row0 * s.stride(1)
+        sss, srs = s.stride(0), s.stride(1)
+    else:
+        scale, sss, srs = None, 0, 0
+    glob = None if m.glob is None else m.glob.data_ptr()
+    gs = 0 if m.glob is None else m.glob.stride(0)
+    return _lib.MatrixBank(data, d.stride(0), rs, scale, sss, srs, glob, gs)
+
+
+def expert_pool_struct(w: ExpertWeights) -> _lib.ExpertPool:
+    """C view of an ExpertWeights pool: gate = rows [0, I) of gate_up, up = rows [I, 2I)."""
+    I = w.inter
+    return _lib.ExpertPool(_QUANT[w.quant], w.hidden, w.inter, w.n_slots,
+                           _matrix_bank(w.gate_up, 0), _matrix_bank(w.gate_up, I),
+                           _matrix_bank(w.down, 0))
+
+
+def ffn_workspace_bytes(n_tok: int, top_k: int, hidden: int, inter: int, n_slots: int) -> int:
+    return int(lib().nvmoe_moe_ffn_workspace_size(n_tok, top_k, hidden, inter, n_slots))
+
+
+class FfnWorkspace:
+    """Grow-only device scratch for nvmoe_moe_ffn."""
+
+    def __init__(self, device="cuda"):
+        self.device = device
+        self.buf = torch.empty(0, dtype=torch.uint8, device=device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf.numel() < nbytes:
+            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+_default_ws: dict[int, FfnWorkspace] = {}
+
+
+def moe_ffn(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor, weights: torch.Tensor,
+            shared: ExpertWeights | None = None, shared_gate: torch.Tensor | None = None,
+            out: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,
+            status: torch.Tensor | None = None) -> torch.Tensor:
+    """y = routed-expert FFN over the slot pool (bf16 [n, H]); see nvmoe_moe_ffn."""
+    _require_cuda(x, slot_ids, weights)
+    assert x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+    assert slot_ids.dtype == torch.int32 and weights.dtype == torch.float32
+    n, H = x.shape
+    k = slot_ids.shape[1]
+    if out is None:
+        out = torch.empty((n, H), dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        dev = x.device.index or 0
+        workspace = _default_ws.setdefault(dev, FfnWorkspace(x.device))
+    nbytes = ffn_workspace_bytes(n, k, pool.hidden, pool.inter, pool.n_slots)
+    ws = workspace.get(nbytes)
+    ps = expert_pool_struct(pool)
+    ss = expert_pool_struct(shared) if shared is not None else None
+    if shared_gate is not None:
+        assert shared_gate.dtype == torch.bfloat16 and shared_gate.is_contiguous()
+    args = _lib.FfnArgs(
+        C.pointer(ps), C.pointer(ss) if ss is not None else None,
+        _ptr(shared_gate), x.data_ptr(), x.stride(0), slot_ids.data_ptr(), slot_ids.stride(0),
+        weights.data_ptr(), weights.stride(0), k, n, out.data_ptr(), out.stride(0),
+        ws.data_ptr(), ws.numel(), _ptr(status))
+    check(lib().nvmoe_moe_ffn(C.byref(args), _stream()), "nvmoe_moe_ffn")
+    return out
+
+
+# ------------------------------------------------------------------ R5 refill
+def refill_banks(gpu: ExpertWeights, host: ExpertWeights) -> list[_lib.RefillBank]:
+    """One RefillBank per FTW bank (codes, scales, global) of gate_up and down."""
+    out = []
+    for g, h in ((gpu.gate_up, host.gate_up), (gpu.down, host.down)):
+        for gt, ht in ((g.data, h.data), (g.scale, h.scale), (g.glob, h.glob)):
+            if gt is None:
+                continue
+            rb = gt[0].numel() * gt.element_size()
+            out.append(_lib.RefillBank(gt.data_ptr(), ht.data_ptr(), gt.stride(0) * gt.element_size(),
+                                       ht.stride(0) * ht.element_size(), rb))
+    return out
+
+
+def refill_async(banks: list[_lib.RefillBank], gpu_slots, host_slots, n_gpu_slots: int,
+                 n_host_slots: int, copy_stream: torch.cuda.Stream,
+                 compute_stream: torch.cuda.Stream | None, done: torch.cuda.Event | None) -> None:
+    import numpy as np
+    g = np.ascontiguousarray(gpu_slots, np.int32)
+    h = np.ascontiguousarray(host_slots, np.int32)
+    arr = (_lib.RefillBank * len(banks))(*banks)
+    check(lib().nvmoe_refill_async(arr, len(banks), g.ctypes.data, h.ctypes.data, g.size,
+                                   n_gpu_slots, n_host_slots, int(copy_stream.cuda_stream),
+                                   None if compute_stream is None else int(compute_stream.cuda_stream),
+                                   None if done is None else done.cuda_event),
+          "nvmoe_refill_async")
+
+
+def refill_gather(banks: list[_lib.RefillBank], misses: MissListGPU,
+                  host_slot_of_id: torch.Tensor, n_gpu_slots: int) -> None:
+    arr = (_lib.RefillBank * len(banks))(*banks)
+    m = misses.struct()
+    check(lib().nvmoe_refill_gather(arr, len(banks), C.byref(m), host_slot_of_id.data_ptr(),
+                                    n_gpu_slots, _stream()), "nvmoe_refill_gather")
