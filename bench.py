@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark: Qwen3.8-Flash-Next-shaped NVFP4 MoE layer decode over a VRAM expert-slot cache.
+
+Workload (one "step" = one decode batch through a stack of MoE layers):
+  hidden 2048, 512 experts, top-10 softmax routing with Zipf(1.1) skew (N(0,1) + ln p router
+  logits, per-layer rank permutation), expert intermediate 512, one always-on shared expert,
+  NVFP4 weights (E2M1 codes uniform, E4M3 per-16 scales 2^U(-8,-2), fp32 global 1/448),
+  128 slots per layer prewarmed with each layer's most frequent experts; 48 layers with
+  distinct slot pools (10.9 GB of pools: inputs larger than L2 between steps); misses refill
+  from a pinned host tier holding all 512 experts (shared by the layers' pools).
+  Per layer: router top-k -> slot remap (LRU, miss list) -> SM refill gather from pinned host
+  -> fused FFN (gate/up SwiGLU, down, weighted combine, shared expert).  Every layer reads
+  the same token batch; layers are independent (no norm / attention between them).
+
+metric: layer tokens/s = batch * layers / step time (device CUDA events, max over ranks).
+N > 1: independent replicas (one stack per GPU, own batch): weak scaling, no collective on the
+data path.  --impl reference times the CPU oracle port of the same step on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer decode tokens/s (Qwen3.8-shaped NVFP4 layer, 128-slot VRAM expert cache)"
+UNIT = "layer-tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="nvmoe", choices=["nvmoe", "reference"])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def config_dict(a, world):
+    return {
+        "workload": f"Qwen3.8-shaped NVFP4 MoE layer decode, batch {a.batch}, {a.layers}-layer "
+                    "stack, 512 experts top-10 + shared, H2048 I512, 128 slots/layer",
+        "model": "Qwen3.8-Flash-Next MoE layer (synthetic NVFP4)",
+        "global_batch": a.batch * world,
+        "seq_len": 1,
+        "layers": a.layers,
+        "experts": 512, "top_k": 10, "hidden": 2048, "inter": 512, "slots_per_layer": 128,
+        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        "l2": "inputs larger than L2 (10.9 GB of distinct per-layer slot pools)",
+        "routing": "softmax top-10 of N(0,1) + ln Zipf(1.1), seed 0",
+    }
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float | None = None) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for n, v in zip(names, r[3][1:]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": rows[0][1],
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_nvmoe(a, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    from nvmoe_b200 import ops
+    from nvmoe_b200.engine import MoEStack, StackConfig
+    from nvmoe_b200.synth import layer_log_bias
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, B = a.layers, a.batch
+    cfg = StackConfig(n_layers=L)
+    E, k, H, I, S = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.inter, cfg.cache_size
+    stack = MoEStack(cfg, device=dev, seed=0)
+    bias = layer_log_bias(L, E, 1.1, seed=0)
+    stack.prewarm(np.argsort(-bias, axis=1, kind="stable"))
+
+    # fresh routing every step: one round of logits (and tokens) per warm-up / timed step
+    R = a.warmup + a.steps
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    bias_t = torch.from_numpy(bias).to(dev)
+    logits = torch.randn((R, L, B, E), generator=g, device=dev) + bias_t[None, :, None, :]
+    xs = torch.randn((R, B, H), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty((L, B, H), dtype=torch.bfloat16, device=dev)
+
+    # distinct experts per (round, layer) for the algorithmic byte count
+    U = np.zeros((R, L), np.int64)
+    for r in range(R):
+        ids, _ = ops.router_topk(logits[r].reshape(L * B, E), k)
+        ids = ids.view(L, B * k).cpu().numpy()
+        for l in range(L):
+            U[r, l] = len(np.unique(ids[l]))
+
+    # one captured graph per round: L x nvmoe_decode_layer (router+remap+refill+FFN)
+    plans = stack.plans(B)
+    cap_stream = torch.cuda.Stream(dev)
+    stack.forward(xs[0], logits[0], out)  # eager pass: attributes, allocations
+    torch.cuda.synchronize()
+    stack.prewarm(np.argsort(-bias, axis=1, kind="stable"))
+    graphs = []
+    for r in range(R):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cap_stream):
+            stack.forward(xs[r], logits[r], out)
+        graphs.append(gr)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(a.warmup):
+        graphs[i].replay()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        t0.record()
+        for i in range(a.steps):
+            graphs[a.warmup + i].replay()
+        t1.record()
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = t0.elapsed_time(t1)
+    misses_last = int(stack.misses.counts[1].item())
+    if world > 1:
+        tt = torch.tensor([elapsed], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        elapsed = float(tt.item())
+    clocks = clk.summary()
+    ms_step = elapsed / a.steps
+    value = B * L * world / (ms_step / 1e3)
+
+    # roofline kernel: the expert FFN (nvmoe_moe_ffn: prep + gate_up + down) of every layer
+    # on the slot ids of the final step, timed per launch with CUDA events
+    ffn_graph = torch.cuda.CUDAGraph()
+    evs = [(torch.cuda.Event(enable_timing=True, external=True),
+            torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
+    ws = ops.FfnWorkspace(dev)
+    yb = torch.empty((L, B, H), dtype=torch.bfloat16, device=dev)
+    xr = xs[R - 1]
+    for l in range(L):  # eager once (attributes)
+        ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
+                    shared=stack.shared[l], out=yb[l], workspace=ws)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(ffn_graph, stream=cap_stream):
+        for l in range(L):
+            evs[l][0].record()
+            ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
+                        shared=stack.shared[l], out=yb[l], workspace=ws)
+            evs[l][1].record()
+    Ulast = np.array([len(np.unique(plans[l].slot_ids.cpu().numpy())) for l in range(L)])
+    ffn_ms, reps = 0.0, 5
+    for _ in range(reps):
+        ffn_graph.replay()
+        torch.cuda.synchronize()
+        ffn_ms += sum(evs[l][0].elapsed_time(evs[l][1]) for l in range(L))
+    n_ffn = reps * L
+    ffn_bytes = reps * float(((Ulast + 1) * stack.bytes_per_expert).sum() +
+                             L * (2 * B * H * 2 + B * k * 8))
+
+    # e2e through the public API with host buffers: H2D tokens + logits, D2H outputs per step
+    xh = xs.cpu().pin_memory()
+    lh = logits.cpu().pin_memory()
+    yh = torch.empty((L, B, H), dtype=torch.bfloat16).pin_memory()
+    xin = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    lin = torch.empty((L, B, E), dtype=torch.float32, device=dev)
+    gr_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr_e2e, stream=cap_stream):
+        stack.forward(xin, lin, out)
+    torch.cuda.synchronize()
+    e2e_steps = min(R, max(10, a.steps))
+    for i in range(3):
+        xin.copy_(xh[i], non_blocking=True); lin.copy_(lh[i], non_blocking=True)
+        gr_e2e.replay(); yh.copy_(out, non_blocking=True)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        xin.copy_(xh[i], non_blocking=True)
+        lin.copy_(lh[i], non_blocking=True)
+        gr_e2e.replay()
+        yh.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (
+        ROOT / "MEASURED_PEAKS.json").exists() else None
+    hbm_peak = peaks["hbm_gbs"] if peaks else 6650.0
+    achieved = (ffn_bytes / n_ffn) / ((ffn_ms / n_ffn) / 1e3) / 1e9
+    step_bytes = float(((U[a.warmup:] + 1) * stack.bytes_per_expert).sum()) / a.steps
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4/f16",
+        "data": "synthetic (seeded; random-init NVFP4 expert weights)",
+        "config": config_dict(a, world),
+        "e2e": {"value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": B * H * 2 + L * B * E * 4,
+                "d2h_bytes_per_step": L * B * H * 2},
+        "gpu_launches": a.steps * L * 4,
+        "roofline": {"bound": "hbm", "kernel": "expert FFN (prep + gate_up + down, one layer)",
+                     "achieved": round(achieved, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else
+                     "fallback 6650 GB/s",
+                     "traffic": _traffic_from_profiles(),
+                     "bytes_per_launch": round(ffn_bytes / n_ffn),
+                     "avg_launch_us": round(1e3 * ffn_ms / n_ffn, 3)},
+        "breakdown": {"layer_step_us": round(1e3 * ms_step / L, 3),
+                      "layer_step_hbm_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
+                      "distinct_experts_per_layer": round(float(U.mean()), 2),
+                      "misses_last_layer_step": misses_last},
+        "clocks": clocks,
+    }
+    return line
+
+
+def _traffic_from_profiles():
+    p = ROOT / "profiles" / "ffn_decode_nvfp4_traffic.md"
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        if ln.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(ln.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ CPU (oracle port)
+def cpu_oracle_sample(batch: int, seconds: float, layers_cap: int = 48):
+    """Times the CPU restatement of one layer step (router, remap, dequant + FFN in fp32) on
+    this host's cores; returns (layer-tokens/s, cores, description)."""
+    import numpy as np
+    import torch
+
+    from nvmoe_b200.formats import random_experts
+    from nvmoe_b200.synth import layer_log_bias, router_logits
+    from oracle import ref_numpy as R
+    from oracle.native import OracleLayer
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    E, k, H, I, S = 512, 10, 2048, 512, 128
+    rng = np.random.default_rng(0)
+    host = random_experts("nvfp4", E, H, I, seed=0)
+    shared = random_experts("nvfp4", 1, H, I, seed=2)
+    bias = layer_log_bias(1, E, 1.1, seed=0)[0]
+    lay = OracleLayer(E, S)
+    for e in np.argsort(-bias)[:S]:
+        lay.eval(np.array([e], np.int32), is_decode=False)
+
+    def dense(w, which, s):
+        m = w.gate_up if which != "down" else w.down
+        rows = slice(0, I) if which == "gate" else (slice(I, 2 * I) if which == "up" else slice(None))
+        return R.dequant_nvfp4(m.data[s, rows].numpy(), m.scale[s, rows].numpy(), m.glob[s].item())
+
+    done, t_start = 0, time.perf_counter()
+    while True:
+        lg = router_logits(batch, bias, rng)
+        ids, w = R.router_topk_softmax(lg, k)
+        lay.eval(ids.reshape(-1), is_decode=True)  # slot bookkeeping; weights come from host
+        x = R.f32_to_bf16(rng.standard_normal((batch, H)).astype(np.float32))
+        # every expert used by the step (shared one included) is dequantised from its packed
+        # bytes, as a CPU implementation of the quantised path has to
+        sh = (dense(shared, "gate", 0), dense(shared, "up", 0), dense(shared, "down", 0))
+        R.moe_ffn(x, ids, w, lambda s: dense(host, "gate", s), lambda s: dense(host, "up", s),
+                  lambda s: dense(host, "down", s), shared=sh)
+        done += 1
+        el = time.perf_counter() - t_start
+        if el >= seconds or done >= layers_cap:
+            break
+    return batch * done / el, cores, f"{done} layer steps of batch {batch} (oracle port: numpy " \
+                                     f"dequant + fp32 FFN, torch/BLAS threads={cores})"
+
+
+def run_reference(a):
+    """Reference arm: the CPU implementation of the path (oracle port; the reference's own FFN
+    lives in FreeToken / ggml, which are not in the reference tree) on the host cores."""
+    per_step = max(0.5, min(3.0, 120.0 / max(1, a.steps + a.warmup)))
+    vals = []
+    for i in range(a.warmup + a.steps):
+        v, cores, desc = cpu_oracle_sample(a.batch, per_step, layers_cap=4)
+        if i >= a.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+        "n_gpus": 0, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": round(1e3 * a.batch / value, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (oracle port)",
+        "data": "synthetic (seeded)", "config": config_dict(a, 1),
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores,
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(a)), flush=True)
+        return
+    import torch
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    line = run_nvmoe(a, rank, world, local_rank)
+    if rank == 0:
+        v, cores, desc = cpu_oracle_sample(a.batch, a.cpu_baseline_seconds)
+        line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": cores,
+                                "kind": "port", "sample": desc}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -36,6 +36,7 @@ extern "C" {
 #define NVMOE_ERR_HOST_LOAD -7      /* the host-tier loader callback reported a failure */
 #define NVMOE_ERR_BAD_SLOT -8       /* a slot id outside [0, n_slots) reached the FFN */
 #define NVMOE_ERR_NO_TABLES -9      /* IQ2_XXS grid table not registered */
+#define NVMOE_ERR_TIMEOUT -10       /* a bounded wait inside a kernel gave up (status word) */
 
 typedef void* nvmoe_stream_t; /* cudaStream_t */
 typedef void* nvmoe_event_t;  /* cudaEvent_t  */
@@ -231,10 +232,44 @@ int nvmoe_refill_async(const nvmoe_refill_bank* banks, int n_banks, const int32_
 /* Device-driven variant for graph capture: reads n_miss = counts[1], miss_slots[] and the
  * host slot of each miss (host_slot_of_id[miss_ids[m]]) from device memory and copies with
  * an SM kernel from mapped pinned host memory (src pointers must be device-accessible
- * mappings).  Misses whose host slot is negative are skipped and reported in counts[2]. */
+ * mappings, e.g. cudaHostAlloc'd).  16-byte loads where a bank's bases, strides and row size
+ * allow it, 4-byte or byte copies otherwise.  Misses whose host slot is negative (or whose
+ * slot is out of range) are skipped and reported as NVMOE_ERR_HOST_LOAD in counts[2]. */
 int nvmoe_refill_gather(const nvmoe_refill_bank* banks, int n_banks, const nvmoe_miss_list* misses,
                         const int32_t* host_slot_of_id, int32_t n_gpu_slots,
                         nvmoe_stream_t stream);
+
+/* ================================================================ one decode layer step
+ * The whole device-side hot path of one MoE layer in one call, graph-capturable (no host
+ * synchronisation): router top-k -> slot remap + miss list -> (optional) refill of the misses
+ * from a device-mapped pinned host tier (nvmoe_refill_gather) -> routed-expert FFN + shared
+ * expert + combine.  This is eval_cb's GPU-tier work (moe_cache_probe.cpp:439-997) followed by
+ * the expert GEMM (_expert_gemm, nvme_offload_cache.py:2142-2184) without the per-layer D2H
+ * sync: router, remap and FFN grouping run fused in one kernel.
+ * slot_ids / weights receive the rewritten slot ids and combine weights [n_tok, top_k]
+ * (contiguous).  ffn.pool / shared / shared_gate / x / y / workspace / status are used;
+ * ffn.slot_ids / weights / top_k / n_tok are taken from this struct. */
+typedef struct nvmoe_decode_args {
+    const float* logits; /* fp32 [n_tok, n_expert]                     */
+    int64_t logits_row_stride;
+    int32_t router_mode; /* enum nvmoe_router_mode                     */
+    const float* router_bias;
+    int32_t norm_topk;
+    float routed_scaling;
+    int32_t top_k;
+    int32_t n_tok;
+    int32_t is_decode;
+    nvmoe_slot_table table;
+    nvmoe_miss_list misses;
+    int32_t* slot_ids;
+    float* weights;
+    const nvmoe_refill_bank* refill_banks; /* NULL: no refill (every routed id must be resident) */
+    int32_t n_refill_banks;
+    const int32_t* host_slot_of_id;
+    nvmoe_ffn_args ffn;
+} nvmoe_decode_args;
+
+int nvmoe_decode_layer(const nvmoe_decode_args* args, nvmoe_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -21,6 +21,7 @@ NVMOE_ERR_UNSUPPORTED = -6
 NVMOE_ERR_HOST_LOAD = -7
 NVMOE_ERR_BAD_SLOT = -8
 NVMOE_ERR_NO_TABLES = -9
+NVMOE_ERR_TIMEOUT = -10
 
 STATUS_NAMES = {
     0: "NVMOE_OK",
@@ -33,6 +34,7 @@ STATUS_NAMES = {
     -7: "NVMOE_ERR_HOST_LOAD",
     -8: "NVMOE_ERR_BAD_SLOT",
     -9: "NVMOE_ERR_NO_TABLES",
+    -10: "NVMOE_ERR_TIMEOUT",
 }
 
 NVMOE_Q_NVFP4 = 0
@@ -132,6 +134,28 @@ class RefillBank(C.Structure):
     ]
 
 
+class DecodeArgs(C.Structure):
+    _fields_ = [
+        ("logits", C.c_void_p),
+        ("logits_row_stride", C.c_int64),
+        ("router_mode", C.c_int32),
+        ("router_bias", C.c_void_p),
+        ("norm_topk", C.c_int32),
+        ("routed_scaling", C.c_float),
+        ("top_k", C.c_int32),
+        ("n_tok", C.c_int32),
+        ("is_decode", C.c_int32),
+        ("table", SlotTable),
+        ("misses", MissList),
+        ("slot_ids", C.c_void_p),
+        ("weights", C.c_void_p),
+        ("refill_banks", C.POINTER(RefillBank)),
+        ("n_refill_banks", C.c_int32),
+        ("host_slot_of_id", C.c_void_p),
+        ("ffn", FfnArgs),
+    ]
+
+
 # name -> (restype, argtypes); must match include/nvmoe_b200.h
 SIGNATURES = {
     "nvmoe_last_error": (C.c_char_p, []),
@@ -164,6 +188,7 @@ SIGNATURES = {
                                      C.c_void_p]),
     "nvmoe_refill_gather": (C.c_int, [C.POINTER(RefillBank), C.c_int, C.POINTER(MissList),
                                       C.c_void_p, C.c_int32, C.c_void_p]),
+    "nvmoe_decode_layer": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -29,6 +29,15 @@ struct FmtNvfp4 {
         r.codes = ldg_stream16(base + (k0 >> 1) + q * 16);
         r.scale2 = e4m3x2_to_f16x2(ldg_stream2(sbase + (k0 >> 4) + q * 2));
     }
+    // same, from a shared-memory copy of the rows (staged by the TMA producer)
+    __device__ __forceinline__ static void load_smem(Row& r, const uint8_t* base,
+                                                     const uint8_t* sbase, int k0, int q) {
+        r.codes = *reinterpret_cast<const uint4*>(base + (k0 >> 1) + q * 16);
+        r.scale2 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(sbase + (k0 >> 4) + q * 2));
+    }
+    // bytes of one row of K values in the code / scale banks
+    __host__ __device__ static constexpr int code_bytes(int k) { return k / 2; }
+    __host__ __device__ static constexpr int scale_bytes(int k) { return k / 16; }
     // A values of step s: two f16x2 regs {K0, K0+1}, {K0+2, K0+3}
     __device__ __forceinline__ static void deq(const Row& r, int s, uint32_t& lo, uint32_t& hi) {
         const uint32_t word = (&r.codes.x)[s >> 1];

@@ -1,0 +1,250 @@
+// Shared definitions of the expert-FFN kernels: workspace layout, kernel parameters, token
+// groups and the grouping step (shared by the FFN prep kernel and the fused decode front kernel).
+#pragma once
+
+#include "common.cuh"
+
+namespace nvmoe {
+
+constexpr int kPrepThreads = 256;
+constexpr int kGroupMaxTok = 8;  // entries (tokens) per token group, = the MMA N of one tile
+constexpr int kDescInts = 16;    // ints per group descriptor
+
+// Group descriptor: one token group (<= 8 entries of one active slot).
+enum {
+    GD_SLOT = 0,   // slot in its pool
+    GD_POOL = 1,   // 0 routed pool, 1 shared expert
+    GD_E0 = 2,     // first entry (entries of a group are consecutive)
+    GD_NT = 3,     // number of entries
+    GD_TOK = 4,    // token of each entry (8)
+    GD_END = 12,
+};
+
+// ------------------------------------------------------------------ workspace layout
+struct WsLayout {
+    size_t hdr, active_slot, tok_cnt, grp_desc, ent_tok, ent_w, ent_of, x16, sg, h16, ypart, total;
+    int a_max, n_ent_max, g_max;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline WsLayout ws_layout(int n_tok, int top_k, int H, int I, int n_slots) {
+    WsLayout L;
+    const int n_route = n_tok * top_k;
+    L.a_max = (n_route < n_slots ? n_route : n_slots) + 1;
+    L.n_ent_max = n_route + n_tok;
+    L.g_max = L.n_ent_max;  // a group holds at least one entry
+    size_t o = 0;
+    L.hdr = o;
+    o = align_up(o + 64, 256);
+    L.active_slot = o;
+    o = align_up(o + 4 * (size_t)L.a_max, 256);
+    L.tok_cnt = o;
+    o = align_up(o + 4 * (size_t)L.a_max, 256);
+    L.grp_desc = o;
+    o = align_up(o + 4 * (size_t)kDescInts * L.g_max, 256);
+    L.ent_tok = o;
+    o = align_up(o + 4 * (size_t)L.n_ent_max, 256);
+    L.ent_w = o;
+    o = align_up(o + 4 * (size_t)L.n_ent_max, 256);
+    L.ent_of = o;
+    o = align_up(o + 4 * (size_t)L.n_ent_max, 256);
+    L.x16 = o;
+    o = align_up(o + 2 * (size_t)n_tok * H, 256);
+    L.sg = o;
+    o = align_up(o + 4 * (size_t)n_tok, 256);
+    L.h16 = o;
+    o = align_up(o + 2 * (size_t)L.n_ent_max * I, 256);
+    L.ypart = o;  // used by the down kernel only when its shared-memory copy does not fit
+    o = align_up(o + 4 * (size_t)L.n_ent_max * H, 256);
+    L.total = o;
+    return L;
+}
+
+enum { HDR_N_ACTIVE = 0, HDR_N_ENT = 1, HDR_STATUS = 2, HDR_N_GROUPS = 3 };
+
+struct FfnParams {
+    nvmoe_expert_pool pool;
+    nvmoe_expert_pool shared;
+    int has_shared;
+    const uint16_t* shared_gate;
+    const uint16_t* x;
+    int64_t x_stride;
+    const int32_t* ids;
+    int64_t ids_stride;
+    const float* w;
+    int64_t w_stride;
+    int top_k;
+    int n_tok;
+    uint16_t* y;
+    int64_t y_stride;
+    unsigned char* ws;
+    WsLayout L;
+    int32_t* status;
+    int nst_gu, stage_gu;  // gate_up pipeline: stages, bytes per stage
+    int nst_dn, stage_dn;  // down pipeline
+    int ypart_smem;        // 1: the down kernel keeps y_part in shared memory
+};
+
+template <typename T>
+__device__ __forceinline__ T* wsp(const FfnParams& P, size_t off) {
+    return reinterpret_cast<T*>(P.ws + off);
+}
+
+#ifdef __CUDACC__
+// Token rows -> f16 copy (the MMA B operand) and the shared-expert gate sigmoid(x . g), for
+// tokens t = t_begin, t_begin + t_step, ... by the whole block.
+__device__ inline void ffn_convert_tokens(const FfnParams& P, int t_begin, int t_step) {
+    const int H = P.pool.hidden;
+    __shared__ float red[32];
+    for (int t = t_begin; t < P.n_tok; t += t_step) {
+        const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
+        __half* x16 = wsp<__half>(P, P.L.x16) + (int64_t)t * H;
+        float dot = 0.f;
+        for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+            const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+            const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
+            __align__(16) __half o[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float f = bf16_bits_to_f32(e[k]);
+                o[k] = __float2half_rn(f);
+                if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
+            }
+            *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+        }
+        if (P.shared_gate) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = dot;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                float s = 0.f;
+                for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+                wsp<float>(P, P.L.sg)[t] = 1.0f / (1.0f + expf(-s));
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Groups the (token, k) entries by slot: active slots ascending, entries of a slot in
+// arrival order, token groups of <= 8 consecutive entries with their descriptors, and the
+// inverse map ent_of[t*(k+1)+j].  Run by one whole block; smem: n_slots ints.
+__device__ inline void ffn_group_block(const FfnParams& P, int* smem_i) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int S = P.pool.n_slots;
+    int* cnt = smem_i;  // [S]: count, then scatter cursor
+    __shared__ int warp_sums[33];
+    __shared__ int s_bad;
+    const int K = P.top_k;
+    const int n = P.n_tok * K;
+    __syncthreads();
+    if (tid == 0) s_bad = 0;
+    for (int s = tid; s < S; s += nthr) cnt[s] = 0;
+    __syncthreads();
+    for (int p = tid; p < n; p += nthr) {
+        const int t = p / K, j = p - t * K;
+        const int s = P.ids[(int64_t)t * P.ids_stride + j];
+        if (s >= 0 && s < S)
+            atomicAdd(&cnt[s], 1);
+        else
+            s_bad = 1;
+    }
+    __syncthreads();
+    int* active_slot = wsp<int>(P, P.L.active_slot);
+    int* tok_cnt = wsp<int>(P, P.L.tok_cnt);
+    int* desc = wsp<int>(P, P.L.grp_desc);
+    int n_act = 0, n_ent = 0, n_grp = 0;
+    for (int base = 0; base < S; base += nthr) {
+        const int s = base + tid;
+        const int c = s < S ? cnt[s] : 0;
+        const int ng = (c + kGroupMaxTok - 1) / kGroupMaxTok;
+        int tot_a, tot_e, tot_g;
+        const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
+        const int re = block_exclusive_scan(c, warp_sums, &tot_e);
+        const int rg = block_exclusive_scan(ng, warp_sums, &tot_g);
+        if (c > 0) {
+            active_slot[n_act + ra] = s;
+            tok_cnt[n_act + ra] = c;
+            cnt[s] = n_ent + re;  // becomes the scatter cursor
+            for (int i = 0; i < ng; ++i) {
+                int* d = desc + (int64_t)(n_grp + rg + i) * kDescInts;
+                d[GD_SLOT] = s;
+                d[GD_POOL] = 0;
+                d[GD_E0] = n_ent + re + i * kGroupMaxTok;
+                d[GD_NT] = min(kGroupMaxTok, c - i * kGroupMaxTok);
+            }
+        }
+        n_act += tot_a;
+        n_ent += tot_e;
+        n_grp += tot_g;
+    }
+    __syncthreads();
+    int* ent_tok = wsp<int>(P, P.L.ent_tok);
+    float* ent_w = wsp<float>(P, P.L.ent_w);
+    int* ent_of = wsp<int>(P, P.L.ent_of);
+    for (int p = tid; p < n; p += nthr) {
+        const int t = p / K, j = p - t * K;
+        const int s = P.ids[(int64_t)t * P.ids_stride + j];
+        int e = -1;
+        if (s >= 0 && s < S) {
+            e = atomicAdd(&cnt[s], 1);
+            ent_tok[e] = t;
+            ent_w[e] = P.w[(int64_t)t * P.w_stride + j];
+        }
+        ent_of[t * (K + 1) + j] = e;
+    }
+    __syncthreads();
+    // token ids of every routed group (the entries of a group are consecutive)
+    for (int g = tid; g < n_grp; g += nthr) {
+        int* d = desc + (int64_t)g * kDescInts;
+        const int e0 = d[GD_E0], nt = d[GD_NT];
+        for (int i = 0; i < kGroupMaxTok; ++i) d[GD_TOK + i] = i < nt ? ent_tok[e0 + i] : 0;
+    }
+    if (P.has_shared) {
+        const int ngs = (P.n_tok + kGroupMaxTok - 1) / kGroupMaxTok;
+        for (int t = tid; t < P.n_tok; t += nthr) {
+            const int e = n_ent + t;
+            ent_tok[e] = t;
+            ent_w[e] = 1.0f;  // the sigmoid gate is applied by the down kernel
+            ent_of[t * (K + 1) + K] = e;
+        }
+        for (int i = tid; i < ngs; i += nthr) {
+            int* d = desc + (int64_t)(n_grp + i) * kDescInts;
+            const int nt = min(kGroupMaxTok, P.n_tok - i * kGroupMaxTok);
+            d[GD_SLOT] = 0;
+            d[GD_POOL] = 1;
+            d[GD_E0] = n_ent + i * kGroupMaxTok;
+            d[GD_NT] = nt;
+            for (int k = 0; k < kGroupMaxTok; ++k) d[GD_TOK + k] = k < nt ? i * kGroupMaxTok + k : 0;
+        }
+        if (tid == 0) {
+            active_slot[n_act] = 0;
+            tok_cnt[n_act] = P.n_tok;
+        }
+        n_act += 1;
+        n_ent += P.n_tok;
+        n_grp += ngs;
+    } else {
+        for (int t = tid; t < P.n_tok; t += nthr) ent_of[t * (K + 1) + K] = -1;
+    }
+    if (tid == 0) {
+        int* hdr = wsp<int>(P, P.L.hdr);
+        hdr[HDR_N_GROUPS] = n_grp;
+        hdr[HDR_N_ACTIVE] = n_act;
+        hdr[HDR_N_ENT] = n_ent;
+        hdr[HDR_STATUS] = s_bad ? NVMOE_ERR_BAD_SLOT : NVMOE_OK;
+        if (P.status) *P.status = s_bad ? NVMOE_ERR_BAD_SLOT : NVMOE_OK;
+    }
+    __syncthreads();
+}
+#endif  // __CUDACC__
+
+// Host: fills the kernel-shape part of FfnParams and launches gate_up + down (PDL-chained
+// after whatever ran before on `st`, which must have produced the group tables).
+int ffn_launch_main(FfnParams& P, cudaStream_t st);
+// Host: validates an nvmoe_ffn_args and fills FfnParams (no launch).
+int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P);
+
+}  // namespace nvmoe

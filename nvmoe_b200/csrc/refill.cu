@@ -23,6 +23,8 @@ constexpr int64_t kPiece = 32 * 1024;
 
 struct GatherParams {
     nvmoe_refill_bank banks[kMaxBanks];
+    uint8_t vec16[kMaxBanks];  // bank rows, strides and bases all 16-byte aligned
+    uint8_t vec4[kMaxBanks];   // ... 4-byte aligned
     int n_banks;
     int64_t max_pieces;  // pieces per (miss, bank) for the largest bank
     const int32_t* counts;
@@ -52,12 +54,19 @@ __global__ void __launch_bounds__(256) refill_gather_kernel(GatherParams P) {
             if (threadIdx.x == 0) atomicExch(P.counts_rw + 2, NVMOE_ERR_HOST_LOAD);
             continue;
         }
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const char*>(B.src) +
-                                                          (int64_t)hs * B.src_slot_stride + beg);
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(B.dst) +
-                                              (int64_t)gs * B.dst_slot_stride + beg);
-        const int64_t n16 = (end - beg) >> 4;
-        for (int64_t i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+        const char* src = static_cast<const char*>(B.src) + (int64_t)hs * B.src_slot_stride + beg;
+        char* dst = static_cast<char*>(B.dst) + (int64_t)gs * B.dst_slot_stride + beg;
+        const int64_t len = end - beg;
+        if (P.vec16[b]) {  // 16-byte aligned bank: vector copy
+            const int64_t n16 = len >> 4;
+            for (int64_t i = threadIdx.x; i < n16; i += blockDim.x)
+                reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+        } else if (P.vec4[b]) {  // e.g. the fp32 global-scale bank (4 bytes per slot)
+            for (int64_t i = threadIdx.x; i < (len >> 2); i += blockDim.x)
+                reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
+        } else {
+            for (int64_t i = threadIdx.x; i < len; i += blockDim.x) dst[i] = src[i];
+        }
     }
 }
 
@@ -125,11 +134,14 @@ extern "C" int nvmoe_refill_gather(const nvmoe_refill_bank* banks, int n_banks,
     int64_t maxp = 1;
     for (int b = 0; b < n_banks; ++b) {
         const nvmoe_refill_bank& B = banks[b];
-        if (!B.dst || !B.src || B.row_bytes < 0 || (B.row_bytes & 15) ||
-            (B.dst_slot_stride & 15) || (B.src_slot_stride & 15) ||
-            (reinterpret_cast<uintptr_t>(B.dst) & 15) || (reinterpret_cast<uintptr_t>(B.src) & 15))
-            return NVMOE_ERR_INVALID_ARG;
+        if (!B.dst || !B.src || B.row_bytes < 0) return NVMOE_ERR_INVALID_ARG;
+        const uint64_t bits = (uint64_t)B.row_bytes | (uint64_t)B.dst_slot_stride |
+                              (uint64_t)B.src_slot_stride | reinterpret_cast<uintptr_t>(B.dst) |
+                              reinterpret_cast<uintptr_t>(B.src);
         P.banks[b] = B;
+        // pieces start at multiples of kPiece (a multiple of 16), so base alignment is kept
+        P.vec16[b] = (bits & 15) == 0;
+        P.vec4[b] = (bits & 3) == 0;
         const int64_t pcs = (B.row_bytes + kPiece - 1) / kPiece;
         if (pcs > maxp) maxp = pcs;
     }

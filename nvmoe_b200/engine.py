@@ -1,0 +1,134 @@
+"""Decode engine over per-layer VRAM slot pools (the llama.cpp engine's layout: one pool of
+`cache_size` slots per MoE layer, scripts/moe_cache_probe.cpp:207-250) with a pinned host tier.
+
+One layer step, all on the device and graph-capturable (no host round trip):
+    router top-k (R1) -> slot remap + miss list (R2/R3/R6, in place on the ids)
+    -> refill of the misses from the pinned host tier by an SM gather (R5)
+    -> fused expert FFN + shared expert + combine (R7/R9)
+The host tier here holds every expert of a layer at host slot == expert id (the Python engine's
+materialised layout, nvme_offload_cache.py:1626-1682), so the miss list alone decides the copies.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import ops
+from .formats import ExpertWeights, QuantMatrix, random_experts
+
+
+def _slot_view(w: ExpertWeights, start: int, n: int) -> ExpertWeights:
+    def sl(m: QuantMatrix) -> QuantMatrix:
+        return QuantMatrix(m.quant, m.rows, m.cols, m.data[start:start + n],
+                           None if m.scale is None else m.scale[start:start + n],
+                           None if m.glob is None else m.glob[start:start + n])
+    return ExpertWeights(w.quant, w.hidden, w.inter, sl(w.gate_up), sl(w.down))
+
+
+def _pin(w: ExpertWeights) -> ExpertWeights:
+    def pm(m: QuantMatrix) -> QuantMatrix:
+        return QuantMatrix(m.quant, m.rows, m.cols, m.data.pin_memory(),
+                           None if m.scale is None else m.scale.pin_memory(),
+                           None if m.glob is None else m.glob.pin_memory())
+    return ExpertWeights(w.quant, w.hidden, w.inter, pm(w.gate_up), pm(w.down))
+
+
+@dataclass
+class StackConfig:
+    n_layers: int = 48
+    n_experts: int = 512
+    top_k: int = 10
+    hidden: int = 2048
+    inter: int = 512
+    cache_size: int = 128
+    quant: str = "nvfp4"
+    shared_expert: bool = True
+    router: str = "softmax"
+    pinned_k: int = 0
+
+
+class MoEStack:
+    """L MoE layers with device slot pools, slot tables and a shared pinned host tier."""
+
+    def __init__(self, cfg: StackConfig, device="cuda", seed: int = 0,
+                 host_tier: ExpertWeights | None = None):
+        self.cfg = c = cfg
+        self.device = torch.device(device)
+        d = self.device
+        # host tier: every expert of a layer, pinned, readable by the refill gather (UVA)
+        if host_tier is None:
+            host_tier = _pin(random_experts(c.quant, c.n_experts, c.hidden, c.inter, seed=seed,
+                                            device=d).to("cpu"))
+        self.host = host_tier
+        # device slot pools: L * cache_size slots in one allocation, one view per layer
+        self.pool_all = random_experts(c.quant, c.n_layers * c.cache_size, c.hidden, c.inter,
+                                       seed=seed + 1, device=d)
+        self.pools = [_slot_view(self.pool_all, l * c.cache_size, c.cache_size)
+                      for l in range(c.n_layers)]
+        self.shared_all = (random_experts(c.quant, c.n_layers, c.hidden, c.inter, seed=seed + 2,
+                                          device=d) if c.shared_expert else None)
+        self.shared = ([_slot_view(self.shared_all, l, 1) for l in range(c.n_layers)]
+                       if c.shared_expert else [None] * c.n_layers)
+        self.tables = [ops.SlotTableGPU(c.n_experts, c.cache_size, d, pinned_k=c.pinned_k)
+                       for _ in range(c.n_layers)]
+        self.misses = ops.MissListGPU(c.n_experts, d)
+        self.host_slot_of_id = torch.arange(c.n_experts, dtype=torch.int32, device=d)
+        self.banks = [ops.refill_banks(p, self.host) for p in self.pools]
+        self.ws = ops.FfnWorkspace(d)
+        self._plans: dict[int, list] = {}
+
+    @property
+    def bytes_per_expert(self) -> int:
+        return self.pool_all.bytes_per_slot
+
+    def prewarm(self, ranking: np.ndarray) -> None:
+        """Fill each layer's slots with its most frequent experts (ranking [L, E], most frequent
+        first), like the reference's calibration prewarm (moe_cache_probe.cpp:1335-1466)."""
+        c = self.cfg
+        cs = torch.cuda.Stream(self.device)
+        ev = torch.cuda.Event()
+        for l in range(c.n_layers):
+            ids = np.asarray(ranking[l][:c.cache_size], np.int32)
+            slots = np.arange(len(ids), dtype=np.int32)
+            ops.refill_async(self.banks[l], slots, ids, c.cache_size, c.n_experts, cs,
+                             torch.cuda.current_stream(self.device), ev)
+            t = self.tables[l]
+            sor = torch.full((c.n_experts,), -1, dtype=torch.int32)
+            sor[torch.from_numpy(ids).long()] = torch.from_numpy(slots)
+            ris = torch.full((c.cache_size,), -1, dtype=torch.int32)
+            ris[: len(ids)] = torch.from_numpy(ids)
+            t.slot_of_real.copy_(sor)
+            t.real_in_slot.copy_(ris)
+            t.last_used.zero_()
+            t.step.zero_()
+        torch.cuda.synchronize(self.device)
+
+    def plans(self, n_tok: int) -> list:
+        """Per-layer nvmoe_decode_layer argument plans for batches of n_tok tokens."""
+        c = self.cfg
+        if n_tok not in self._plans:
+            self._plans[n_tok] = [
+                ops.DecodeLayerPlan(self.pools[l], self.tables[l], self.misses, n_tok, c.top_k,
+                                    shared=self.shared[l], refill=self.banks[l],
+                                    host_slot_of_id=self.host_slot_of_id, workspace=self.ws,
+                                    router=c.router, device=self.device)
+                for l in range(c.n_layers)]
+        return self._plans[n_tok]
+
+    def layer_step(self, l: int, x: torch.Tensor, logits: torch.Tensor,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+        """One MoE layer on tokens x [n, H] bf16 with router logits [n, E] fp32: one
+        nvmoe_decode_layer call (router, remap, refill gather, FFN)."""
+        if out is None:
+            out = torch.empty((x.shape[0], self.cfg.hidden), dtype=torch.bfloat16,
+                              device=self.device)
+        return self.plans(x.shape[0])[l](x, logits, out)
+
+    def forward(self, x: torch.Tensor, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """All layers on the same token batch: logits [L, n, E], out [L, n, H]."""
+        plans = self.plans(x.shape[0])
+        for l in range(self.cfg.n_layers):
+            plans[l](x, logits[l], out[l])
+        return out

@@ -298,3 +298,64 @@ def refill_gather(banks: list[_lib.RefillBank], misses: MissListGPU,
     m = misses.struct()
     check(lib().nvmoe_refill_gather(arr, len(banks), C.byref(m), host_slot_of_id.data_ptr(),
                                     n_gpu_slots, _stream()), "nvmoe_refill_gather")
+
+
+# ------------------------------------------------------------------ one decode layer step
+class DecodeLayerPlan:
+    """Pre-built C arguments of nvmoe_decode_layer for one layer (pointers of the layer's slot
+    pool, tables, refill banks, workspace and output buffers); call() only patches the per-step
+    inputs.  Keeps every ctypes object alive as long as the plan lives."""
+
+    def __init__(self, pool: ExpertWeights, table: SlotTableGPU, misses: MissListGPU,
+                 n_tok: int, top_k: int, shared: ExpertWeights | None = None,
+                 shared_gate: torch.Tensor | None = None, refill: list | None = None,
+                 host_slot_of_id: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,
+                 router: str = "softmax", router_bias: torch.Tensor | None = None,
+                 norm_topk: bool = True, routed_scaling: float = 1.0, device="cuda"):
+        self.n_tok, self.top_k = n_tok, top_k
+        self.pool_s = expert_pool_struct(pool)
+        self.shared_s = expert_pool_struct(shared) if shared is not None else None
+        self.slot_ids = torch.empty((n_tok, top_k), dtype=torch.int32, device=device)
+        self.weights = torch.empty((n_tok, top_k), dtype=torch.float32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        ws = workspace or FfnWorkspace(device)
+        self.ws = ws.get(ffn_workspace_bytes(n_tok, top_k, pool.hidden, pool.inter, pool.n_slots))
+        self.refill = (_lib.RefillBank * len(refill))(*refill) if refill else None
+        self.table, self.misses, self.host_slot_of_id = table, misses, host_slot_of_id
+        self.router_bias, self.shared_gate = router_bias, shared_gate
+        a = _lib.DecodeArgs()
+        a.router_mode = _lib.NVMOE_ROUTER_SOFTMAX if router == "softmax" else \
+            _lib.NVMOE_ROUTER_SIGMOID_BIAS
+        a.router_bias = _ptr(router_bias)
+        a.norm_topk = int(norm_topk)
+        a.routed_scaling = float(routed_scaling)
+        a.top_k, a.n_tok, a.is_decode = top_k, n_tok, 1
+        a.table = table.struct()
+        a.misses = misses.struct()
+        a.slot_ids = self.slot_ids.data_ptr()
+        a.weights = self.weights.data_ptr()
+        if self.refill is not None:
+            a.refill_banks = C.cast(self.refill, C.POINTER(_lib.RefillBank))
+            a.n_refill_banks = len(refill)
+            a.host_slot_of_id = host_slot_of_id.data_ptr()
+        a.ffn.pool = C.pointer(self.pool_s)
+        if self.shared_s is not None:
+            a.ffn.shared = C.pointer(self.shared_s)
+        a.ffn.shared_gate = _ptr(shared_gate)
+        a.ffn.workspace = self.ws.data_ptr()
+        a.ffn.workspace_bytes = self.ws.numel()
+        a.ffn.status = self.status.data_ptr()
+        self.args = a
+
+    def __call__(self, x: torch.Tensor, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        assert x.shape[0] == self.n_tok and logits.shape[0] == self.n_tok
+        assert x.dtype == torch.bfloat16 and logits.dtype == torch.float32
+        a = self.args
+        a.logits = logits.data_ptr()
+        a.logits_row_stride = logits.stride(0)
+        a.ffn.x = x.data_ptr()
+        a.ffn.x_row_stride = x.stride(0)
+        a.ffn.y = out.data_ptr()
+        a.ffn.y_row_stride = out.stride(0)
+        check(lib().nvmoe_decode_layer(C.byref(a), _stream()), "nvmoe_decode_layer")
+        return out
