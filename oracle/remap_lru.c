@@ -235,6 +235,10 @@ int orc_layer_eval(void* p, const int32_t* ids, int n, int is_decode, int with_h
     for (int i = 0; i < n; ++i)
         if (find_int(unique_ids, nu, ids[i]) < 0) unique_ids[nu++] = ids[i];
     *n_unique = nu;
+    /* A victim exists for every miss iff the distinct ids fit in the pool (nu <= cache_size);
+     * the reference aborts when they do not (moe_cache_probe.cpp:709-712).  Detect it before
+     * any state changes, like the device kernel. */
+    if (nu > L->cache_size) return -3;
     uint8_t* active = (uint8_t*)calloc((size_t)L->n_expert, 1);
     for (int i = 0; i < nu; ++i) active[unique_ids[i]] = 1;
 

@@ -20,7 +20,7 @@ def _dense(w, which, s):
     return R.dequant_nvfp4(m.data[s, rows].numpy(), m.scale[s, rows].numpy(), m.glob[s].item())
 
 
-@pytest.mark.parametrize("n_tok,prewarm", [(1, False), (3, True), (8, False)])
+@pytest.mark.parametrize("n_tok,prewarm", [(1, False), (3, True), (4, False), (8, False)])
 def test_decode_layer_matches_oracle_chain(cuda_device, n_tok, prewarm):
     cfg = StackConfig(n_layers=2, n_experts=64, top_k=4, hidden=2048, inter=512, cache_size=16)
     stack = MoEStack(cfg, device=cuda_device, seed=3)
@@ -52,9 +52,16 @@ def test_decode_layer_matches_oracle_chain(cuda_device, n_tok, prewarm):
             y = stack.layer_step(l, x.to(cuda_device), torch.from_numpy(lg).to(cuda_device))
             plan = stack.plans(n_tok)[l]
             torch.cuda.synchronize()
-            assert int(plan.status.item()) == 0
             rids, rw = R.router_topk_softmax(lg, 4)
             ref = orc[l].eval(rids.reshape(-1), is_decode=True)
+            if ref["status"] == -3:
+                # more distinct experts than slots: the reference aborts (ubatch clamp,
+                # moe_cache_probe.cpp:1668-1684); here the step reports the overflow, leaves the
+                # tables untouched and outputs zeros
+                assert int(plan.status.item()) == -3
+                assert not y.float().abs().any()
+                continue
+            assert int(plan.status.item()) == 0
             assert ref["status"] == 0
             np.testing.assert_array_equal(plan.slot_ids.cpu().numpy().reshape(-1), ref["slots"])
             np.testing.assert_allclose(plan.weights.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
