@@ -37,6 +37,7 @@ extern "C" {
 #define NVMOE_ERR_BAD_SLOT -8       /* a slot id outside [0, n_slots) reached the FFN */
 #define NVMOE_ERR_NO_TABLES -9      /* IQ2_XXS grid table not registered */
 #define NVMOE_ERR_TIMEOUT -10       /* a bounded wait inside a kernel gave up (status word) */
+#define NVMOE_ERR_SCRATCH_LIMIT -11 /* call needs more scratch than nvmoe_moe_ffn_noalloc has */
 
 typedef void* nvmoe_stream_t; /* cudaStream_t */
 typedef void* nvmoe_event_t;  /* cudaEvent_t  */
@@ -183,6 +184,18 @@ typedef struct nvmoe_ffn_args {
 
 size_t nvmoe_moe_ffn_workspace_size(int n_tok, int top_k, int hidden, int inter, int n_slots);
 int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
+
+/* Same FFN as nvmoe_moe_ffn, for callers that cannot allocate device memory when they run it
+ * (e.g. a llama.cpp eval callback, where every device buffer belongs to ggml's allocator and a
+ * cudaMalloc would synchronise the device mid-graph, or a process whose spare VRAM is all given
+ * to the slot pool).  No counterpart in the reference: it is an addition of this library.
+ * args->workspace / workspace_bytes are ignored: the scratch is one 16 MiB device array built
+ * into the library, present on every GPU that loads it until the process exits.  Calls whose
+ * nvmoe_moe_ffn_workspace_size exceeds 16 MiB return NVMOE_ERR_SCRATCH_LIMIT.  The first call on
+ * a device looks up the array's address (once per device); make it before any stream capture.
+ * All calls on a device share the array (it keeps the last call's contents; nothing in it needs
+ * to start at zero), so calls that overlap on the GPU race: serialise them.  Allocates nothing. */
+int nvmoe_moe_ffn_noalloc(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
 
 /* ================================================================ R4: host tier (SLRU)
  * Segmented LRU of the pinned host tier (nvme_offload_cache.py:333-409;

@@ -22,6 +22,7 @@ NVMOE_ERR_HOST_LOAD = -7
 NVMOE_ERR_BAD_SLOT = -8
 NVMOE_ERR_NO_TABLES = -9
 NVMOE_ERR_TIMEOUT = -10
+NVMOE_ERR_SCRATCH_LIMIT = -11
 
 STATUS_NAMES = {
     0: "NVMOE_OK",
@@ -35,6 +36,7 @@ STATUS_NAMES = {
     -8: "NVMOE_ERR_BAD_SLOT",
     -9: "NVMOE_ERR_NO_TABLES",
     -10: "NVMOE_ERR_TIMEOUT",
+    -11: "NVMOE_ERR_SCRATCH_LIMIT",
 }
 
 NVMOE_Q_NVFP4 = 0
@@ -172,6 +174,7 @@ SIGNATURES = {
     "nvmoe_set_iq2xxs_grid": (C.c_int, [C.c_void_p]),
     "nvmoe_moe_ffn_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     "nvmoe_moe_ffn": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
+    "nvmoe_moe_ffn_noalloc": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
     "nvmoe_slru_create": (C.c_void_p, [C.c_double]),
     "nvmoe_slru_destroy": (None, [C.c_void_p]),
     "nvmoe_slru_set_capacity_hint": (None, [C.c_void_p, C.c_int64]),
