@@ -1,10 +1,11 @@
 // One decode layer step (engine path): fused router + remap + FFN grouping kernel, then the
 // optional refill gather and the FFN kernels, all chained with programmatic dependent launch.
 //
-// The front kernel is one CTA of 512 threads: warps compute the top-k of the token rows
-// (router_device.cuh), the block then runs the remap (remap_device.cuh) in place on the ids and
-// groups the slot ids for the FFN (ffn_common.cuh).  Replaces three launches (router, remap,
-// FFN prep) on the latency-critical small-batch decode path.
+// The front kernel is one CTA: warps compute the top-k of the token rows (router_device.cuh)
+// while the slot tables stream into shared memory, then the block runs the remap and the FFN
+// grouping entirely in shared memory and stores the results.  Replaces three launches (router,
+// remap, FFN prep) and their dependent global-memory round trips on the latency-critical
+// small-batch decode path.
 #include "common.cuh"
 #include "ffn_common.cuh"
 #include "remap_device.cuh"
@@ -19,7 +20,9 @@ extern "C" int nvmoe_refill_gather(const nvmoe_refill_bank* banks, int n_banks,
 namespace nvmoe {
 namespace {
 
-constexpr int kFrontThreads = 512;  // 16 warps; 128 registers per thread for the top-k tile
+constexpr int kFrontThreads = 512;  // at most 16 warps; 128 registers per thread for the top-k tile
+constexpr int kFrontMaxIds = 2048;  // routed (token, k) entries per call on this path
+constexpr int kFrontMaxSlots = 1024;
 
 struct FrontParams {
     const float* logits;
@@ -28,36 +31,350 @@ struct FrontParams {
     const float* bias;
     int norm_topk;
     float scaling;
-    RemapParams rp;
+    RemapParams rp;  // rp.out: slot ids [n_tok, k] (global), rp.ids unused
     float* weights;
     FfnParams fp;
 };
 
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Shared-memory layout of the front kernel (ints unless noted).
+struct FrontSmem {
+    int sor, ris, lu, first, uniq, uslot, miss_r, act, cnt, gbase, sids, sw, ent_tok, ent_w, keys,
+        total;
+};
+__host__ __device__ inline FrontSmem front_smem(int E, int S, int n, int n_ent) {
+    int s2 = 1;
+    while (s2 < S) s2 <<= 1;
+    FrontSmem L;
+    int o = 0;
+    L.keys = o;  // u64 [s2]
+    o += 8 * s2;
+    L.sor = o;
+    o += 4 * E;
+    L.ris = o;
+    o += 4 * S;
+    L.lu = o;
+    o += 4 * S;
+    L.first = o;
+    o += 4 * E;
+    L.uniq = o;
+    o += 4 * E;
+    L.uslot = o;
+    o += 4 * E;
+    L.miss_r = o;
+    o += 4 * E;
+    L.act = o;
+    o += 4 * S;
+    L.cnt = o;
+    o += 4 * S;
+    L.gbase = o;
+    o += 4 * S;
+    L.sids = o;
+    o += 4 * n;
+    L.sw = o;
+    o += 4 * n;
+    L.ent_tok = o;
+    o += 4 * n_ent;
+    L.ent_w = o;
+    o += 4 * n_ent;
+    L.total = o;
+    return L;
+}
+
+// Token rows -> f16 and the shared-expert gate, one warp per token (no block barrier).
+__device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, int lane) {
+    const int H = P.pool.hidden;
+    const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
+    __half* x16 = wsp<__half>(P, P.L.x16) + (int64_t)t * H;
+    float dot = 0.f;
+    for (int i = lane * 8; i < H; i += 256) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+        const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
+        __align__(16) __half o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float f = bf16_bits_to_f32(e[k]);
+            o[k] = __float2half_rn(f);
+            if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
+        }
+        *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+    }
+    if (P.shared_gate) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (lane == 0) wsp<float>(P, P.L.sg)[t] = 1.0f / (1.0f + expf(-dot));
+    }
+}
+
+// Router top-k -> slot remap -> FFN grouping for one decode step, in one CTA.  Every table the
+// step needs is prefetched into shared memory with cp.async while the warps load their logit
+// rows and token rows, so global memory costs one round trip; results are stored at the end.
+// Same rules as remap_device.cuh / ffn_common.cuh (eval_cb, moe_cache_probe.cpp:627-753,955-970).
 __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontParams F) {
     extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int warp_sums[33];
+    __shared__ int s_err, s_nuniq, s_nmiss, s_step;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nthr = blockDim.x, nw = nthr >> 5;
+    const int E = F.rp.t.n_expert, S = F.rp.t.cache_size, K = F.rp.top_k, n_tok = F.rp.n_tok;
+    const int n = n_tok * K;
+    const int id_base = F.rp.t.id_base;
+    const FfnParams& P = F.fp;
+    const FrontSmem L = front_smem(E, S, n, n + n_tok);
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
+    int* sor = reinterpret_cast<int*>(smem + L.sor);
+    int* ris = reinterpret_cast<int*>(smem + L.ris);
+    uint32_t* lu = reinterpret_cast<uint32_t*>(smem + L.lu);
+    int* first = reinterpret_cast<int*>(smem + L.first);
+    int* uniq = reinterpret_cast<int*>(smem + L.uniq);
+    int* uslot = reinterpret_cast<int*>(smem + L.uslot);
+    int* miss_r = reinterpret_cast<int*>(smem + L.miss_r);
+    int* act = reinterpret_cast<int*>(smem + L.act);
+    int* cnt = reinterpret_cast<int*>(smem + L.cnt);
+    int* gbase = reinterpret_cast<int*>(smem + L.gbase);
+    int* sids = reinterpret_cast<int*>(smem + L.sids);
+    float* sw = reinterpret_cast<float*>(smem + L.sw);
+    int* ent_tok_s = reinterpret_cast<int*>(smem + L.ent_tok);
+    float* ent_w_s = reinterpret_cast<float*>(smem + L.ent_w);
+
     grid_dep_wait();
     grid_dep_launch();
-    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int k = F.rp.top_k;
-    int32_t* ids = F.rp.out;
-    for (int t = warp; t < F.rp.n_tok; t += nw)
-        router_topk_warp(F.logits + (int64_t)t * F.lstride, F.rp.t.n_expert, k, F.mode, F.bias,
-                         F.norm_topk, F.scaling, ids + (int64_t)t * k, F.weights + (int64_t)t * k);
+    // ---- A. one round trip: table prefetch (async), logits (router), token rows (convert)
+    for (int e = tid; e < E; e += nthr) cp_async4(sor + e, F.rp.t.slot_of_real + id_base + e);
+    for (int s = tid; s < S; s += nthr) {
+        cp_async4(ris + s, F.rp.t.real_in_slot + s);
+        cp_async4(lu + s, F.rp.t.slot_last_used + s);
+        act[s] = 0;
+        cnt[s] = 0;
+    }
+    for (int e = tid; e < E; e += nthr) first[e] = 0x7fffffff;
+    if (tid == 0) {
+        s_err = NVMOE_OK;
+        s_step = (int)(*F.rp.t.current_step + 1u);
+    }
+    const int n_route_warps = min(nw, n_tok);
+    if (warp < n_route_warps) {
+        for (int t = warp; t < n_tok; t += n_route_warps)
+            router_topk_warp(F.logits + (int64_t)t * F.lstride, E, K, F.mode, F.bias,
+                             F.norm_topk, F.scaling, sids + t * K, sw + t * K);
+    }
+    {  // token conversion by the warps the router leaves idle (all warps if none are idle)
+        const int c0 = (n_route_warps < nw) ? n_route_warps : 0;
+        const int nconv = nw - c0;
+        if (warp >= c0)
+            for (int t = warp - c0; t < n_tok; t += nconv) front_convert_token(P, t, lane);
+    }
+    cp_async_wait_all();
     __syncthreads();
-    const int st = remap_block(F.rp, smem);
-    ffn_convert_tokens(F.fp, 0, 1);
-    if (st != NVMOE_OK) {  // ids were not rewritten: give the FFN nothing to do (y = 0)
-        if (threadIdx.x == 0) {
-            int* hdr = wsp<int>(F.fp, F.fp.L.hdr);
+
+    // ---- B. remap in shared memory
+    for (int p = tid; p < n; p += nthr) {
+        const int id = sids[p];
+        if (id < 0 || id >= E)
+            s_err = NVMOE_ERR_BAD_EXPERT_ID;
+        else
+            atomicMin(&first[id], p);
+    }
+    __syncthreads();
+    int status = s_err;
+    int nuniq = 0, nmiss = 0;
+    const uint32_t step = (uint32_t)s_step;
+    if (status == NVMOE_OK) {
+        nuniq = ordered_compact(n, warp_sums, [&](int p) { return first[sids[p]] == p; },
+                                [&](int p, int r) { uniq[r] = sids[p]; });
+        __syncthreads();
+        if (nuniq > S) status = NVMOE_ERR_CACHE_OVERFLOW;
+    }
+    if (status == NVMOE_OK) {
+        for (int r = tid; r < nuniq; r += nthr) {
+            const int e = uniq[r];
+            first[e] = r;  // id -> rank from here on
+            const int s = sor[e];
+            const bool hit = s >= 0 && s < S;
+            uslot[r] = hit ? s : -1;
+            if (hit) act[s] = 1;
+        }
+        __syncthreads();
+        nmiss = ordered_compact(nuniq, warp_sums, [&](int r) { return uslot[r] < 0; },
+                                [&](int r, int j) { miss_r[j] = r; });
+        __syncthreads();
+        if (nmiss > 0) {
+            int S2 = 1;
+            while (S2 < S) S2 <<= 1;
+            const int start = (F.rp.is_decode && F.rp.t.pinned_k > 0) ? min(F.rp.t.pinned_k, S) : 0;
+            for (int s = tid; s < S2; s += nthr) {
+                unsigned long long k = ~0ull;
+                if (s < S && !act[s]) {
+                    const int occ = ris[s];
+                    const bool hi = s >= start;
+                    const unsigned long long cls = occ < 0 ? (hi ? 0ull : 2ull) : (hi ? 1ull : 3ull);
+                    const unsigned long long l = occ < 0 ? 0ull : (unsigned long long)lu[s];
+                    k = (cls << 62) | (l << 24) | (unsigned long long)s;
+                }
+                keys[s] = k;
+            }
+            __syncthreads();
+            for (int size = 2; size <= S2; size <<= 1)
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    for (int i = tid; i < (S2 >> 1); i += nthr) {
+                        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+                        const bool up = ((lo & size) == 0);
+                        const unsigned long long a = keys[lo], b = keys[hi];
+                        if ((a > b) == up) keys[lo] = b, keys[hi] = a;
+                    }
+                    __syncthreads();
+                }
+            const nvmoe_miss_list& M = F.rp.m;
+            for (int j = tid; j < nmiss; j += nthr) {
+                const int r = miss_r[j], e = uniq[r];
+                const int s = (int)(keys[j] & 0xffffffull);
+                const int ev = ris[s];
+                if (ev >= 0) F.rp.t.slot_of_real[ev] = -1;
+                F.rp.t.real_in_slot[s] = id_base + e;
+                uslot[r] = s;
+                M.miss_ids[j] = e;
+                M.miss_slots[j] = s;
+                M.evicted_ids[j] = ev;
+            }
+            __syncthreads();
+        }
+        // write back: tables, distinct-id report, slot ids and weights
+        const nvmoe_miss_list& M = F.rp.m;
+        for (int r = tid; r < nuniq; r += nthr) {
+            const int e = uniq[r], s = uslot[r];
+            F.rp.t.slot_of_real[id_base + e] = s;
+            F.rp.t.slot_last_used[s] = step;
+            M.unique_ids[r] = e;
+            M.unique_slot[r] = s;
+        }
+        for (int r = tid; r < nuniq; r += nthr) M.unique_hit[r] = 1;
+        __syncthreads();
+        for (int j = tid; j < nmiss; j += nthr) M.unique_hit[miss_r[j]] = 0;
+        for (int p = tid; p < n; p += nthr) {
+            const int sl = uslot[first[sids[p]]];
+            sids[p] = sl;
+            F.rp.out[p] = sl;
+            F.weights[p] = sw[p];
+        }
+        if (tid == 0) *F.rp.t.current_step = step;
+    }
+    if (tid == 0) {
+        F.rp.m.counts[0] = status == NVMOE_ERR_BAD_EXPERT_ID ? 0 : nuniq;
+        F.rp.m.counts[1] = status == NVMOE_OK ? nmiss : 0;
+        F.rp.m.counts[2] = status;
+        F.rp.m.counts[3] = n;
+    }
+    int* hdr = wsp<int>(P, P.L.hdr);
+    if (status != NVMOE_OK) {  // the FFN gets nothing to do (y = 0) and the status
+        if (tid == 0) {
             hdr[HDR_N_GROUPS] = 0;
             hdr[HDR_N_ACTIVE] = 0;
             hdr[HDR_N_ENT] = 0;
-            hdr[HDR_STATUS] = st;
-            if (F.fp.status) *F.fp.status = st;
+            hdr[HDR_STATUS] = status;
+            if (P.status) *P.status = status;
         }
         return;
     }
-    ffn_group_block(F.fp, reinterpret_cast<int*>(smem));
+    __syncthreads();
+
+    // ---- C. FFN grouping from the slot ids in shared memory (ffn_group_block, staged)
+    for (int p = tid; p < n; p += nthr) atomicAdd(&cnt[sids[p]], 1);
+    __syncthreads();
+    int* desc = wsp<int>(P, P.L.grp_desc);
+    int n_act = 0, n_ent = 0, n_grp = 0;
+    for (int base = 0; base < S; base += nthr) {
+        const int s = base + tid;
+        const int c = s < S ? cnt[s] : 0;
+        const int ng = (c + kGroupMaxTok - 1) / kGroupMaxTok;
+        int tot_a, tot_e, tot_g;
+        const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
+        const int re = block_exclusive_scan(c, warp_sums, &tot_e);
+        const int rg = block_exclusive_scan(ng, warp_sums, &tot_g);
+        if (s < S) act[s] = c > 0 ? n_ent + re : -1;  // entry base of the slot
+        if (s < S) gbase[s] = n_grp + rg;               // first group of the slot
+        if (c > 0) {
+            wsp<int>(P, P.L.active_slot)[n_act + ra] = s;
+            wsp<int>(P, P.L.tok_cnt)[n_act + ra] = c;
+            cnt[s] = n_ent + re;  // scatter cursor
+            for (int i = 0; i < ng; ++i) {
+                int* d = desc + (int64_t)(n_grp + rg + i) * kDescInts;
+                d[GD_SLOT] = s;
+                d[GD_POOL] = 0;
+                d[GD_E0] = n_ent + re + i * kGroupMaxTok;
+                d[GD_NT] = min(kGroupMaxTok, c - i * kGroupMaxTok);
+            }
+        }
+        n_act += tot_a;
+        n_ent += tot_e;
+        n_grp += tot_g;
+    }
+    __syncthreads();
+    int* ent_of = wsp<int>(P, P.L.ent_of);
+    for (int p = tid; p < n; p += nthr) {
+        const int t = p / K, j = p - t * K;
+        const int e = atomicAdd(&cnt[sids[p]], 1);
+        ent_tok_s[e] = t;
+        ent_w_s[e] = sw[p];
+        ent_of[t * (K + 1) + j] = e;
+    }
+    __syncthreads();
+    for (int e = tid; e < n_ent; e += nthr) {
+        wsp<int>(P, P.L.ent_tok)[e] = ent_tok_s[e];
+        wsp<float>(P, P.L.ent_w)[e] = ent_w_s[e];
+    }
+    for (int s = tid; s < S; s += nthr) {  // token lists of the routed groups
+        const int eb = act[s];
+        if (eb < 0) continue;
+        const int c = cnt[s] - eb;  // the cursor ended at base + count
+        for (int i = 0; i * kGroupMaxTok < c; ++i) {
+            int* d = desc + (int64_t)(gbase[s] + i) * kDescInts;
+            for (int k = 0; k < kGroupMaxTok; ++k) {
+                const int e = i * kGroupMaxTok + k;
+                d[GD_TOK + k] = e < c ? ent_tok_s[eb + e] : 0;
+            }
+        }
+    }
+    if (P.has_shared) {
+        const int ngs = (n_tok + kGroupMaxTok - 1) / kGroupMaxTok;
+        for (int t = tid; t < n_tok; t += nthr) {
+            const int e = n_ent + t;
+            wsp<int>(P, P.L.ent_tok)[e] = t;
+            wsp<float>(P, P.L.ent_w)[e] = 1.0f;
+            ent_of[t * (K + 1) + K] = e;
+        }
+        for (int i = tid; i < ngs; i += nthr) {
+            int* d = desc + (int64_t)(n_grp + i) * kDescInts;
+            const int nt = min(kGroupMaxTok, n_tok - i * kGroupMaxTok);
+            d[GD_SLOT] = 0;
+            d[GD_POOL] = 1;
+            d[GD_E0] = n_ent + i * kGroupMaxTok;
+            d[GD_NT] = nt;
+            for (int k = 0; k < kGroupMaxTok; ++k) d[GD_TOK + k] = k < nt ? i * kGroupMaxTok + k : 0;
+        }
+        if (tid == 0) {
+            wsp<int>(P, P.L.active_slot)[n_act] = 0;
+            wsp<int>(P, P.L.tok_cnt)[n_act] = n_tok;
+        }
+        n_act += 1;
+        n_ent += n_tok;
+        n_grp += ngs;
+    } else {
+        for (int t = tid; t < n_tok; t += nthr) ent_of[t * (K + 1) + K] = -1;
+    }
+    if (tid == 0) {
+        hdr[HDR_N_GROUPS] = n_grp;
+        hdr[HDR_N_ACTIVE] = n_act;
+        hdr[HDR_N_ENT] = n_ent;
+        hdr[HDR_STATUS] = NVMOE_OK;
+        if (P.status) *P.status = NVMOE_OK;
+    }
 }
 
 }  // namespace
@@ -116,14 +433,17 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
     F.rp.is_decode = a->is_decode;
     F.rp.m = m;
 
-    const size_t smem = std::max(remap_smem_bytes(t.n_expert, t.cache_size),
-                                 (size_t)F.fp.pool.n_slots * 4);
+    if (n > kFrontMaxIds || t.cache_size > kFrontMaxSlots) return NVMOE_ERR_UNSUPPORTED;
+    if (F.fp.pool.n_slots < t.cache_size) return NVMOE_ERR_INVALID_ARG;
+    const size_t smem = (size_t)front_smem(t.n_expert, t.cache_size, (int)n, (int)n + a->n_tok).total;
     if (smem > 200 * 1024) return NVMOE_ERR_UNSUPPORTED;
     cudaStream_t st = (cudaStream_t)stream;
     if (smem > 48 * 1024)
         NVMOE_CUDA_TRY(cudaFuncSetAttribute(decode_front_kernel,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    cudaError_t e = launch_pdl(decode_front_kernel, dim3(1), dim3(kFrontThreads), smem, st, true, F);
+    // 8 warps up to 8 tokens, 16 above: routing warps plus token-conversion warps
+    const int threads = a->n_tok <= 8 ? 256 : kFrontThreads;
+    cudaError_t e = launch_pdl(decode_front_kernel, dim3(1), dim3(threads), smem, st, true, F);
     if (e != cudaSuccess) return cuda_status("decode_front launch", e);
     if (a->refill_banks && a->n_refill_banks > 0) {
         rc = nvmoe_refill_gather(a->refill_banks, a->n_refill_banks, &a->misses,

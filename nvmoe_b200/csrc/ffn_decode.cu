@@ -34,7 +34,8 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kTmaThreads = kConsumers + 32;  // + one producer warp
 constexpr int kSmemCap = 227 * 1024 - 1024;   // dynamic share; static use stays below 1 KB
-constexpr int kStageHdr = 64;                 // group descriptor copied into each stage
+constexpr int kStageHdr = 128;  // per stage: group descriptor + scalars fetched by the producer
+constexpr int kHdrExt = 10;     // header floats after the descriptor (see load_desc_ext)
 
 // ------------------------------------------------------------------ 1. prep
 __global__ void __launch_bounds__(kPrepThreads) ffn_prep_kernel(FfnParams P) {
@@ -76,7 +77,37 @@ __device__ __forceinline__ void load_desc(const FfnParams& P, int grp, int (&d)[
 }
 
 __device__ __forceinline__ float global_of(const nvmoe_matrix_bank& b, int slot) {
-    return b.global_scale ? b.global_scale[(int64_t)slot * b.global_stride] : 1.0f;
+    return b.global_scale ? __ldcg(b.global_scale + (int64_t)slot * b.global_stride) : 1.0f;
+}
+
+// Scalars an item needs in its epilogue, fetched by the producer lanes in parallel (off the
+// consumers' critical path) and shipped in the stage header after the descriptor:
+//   gate_up: ext[0] = gate global, ext[1] = up global
+//   down   : ext[0] = down global, ext[2 + n] = combine weight of entry n (times the shared
+//            expert's sigmoid gate for the shared pool)
+template <bool kDown>
+__device__ __forceinline__ void load_desc_ext(const FfnParams& P, int grp, int (&d)[kDescInts],
+                                              float (&ext)[kHdrExt]) {
+    load_desc(P, grp, d);
+    const nvmoe_expert_pool& pool = d[GD_POOL] ? P.shared : P.pool;
+#pragma unroll
+    for (int i = 0; i < kHdrExt; ++i) ext[i] = 0.f;
+    if (!kDown) {
+        ext[0] = global_of(pool.gate, d[GD_SLOT]);
+        ext[1] = global_of(pool.up, d[GD_SLOT]);
+    } else {
+        ext[0] = global_of(pool.down, d[GD_SLOT]);
+        const float* ent_w = wsp<float>(P, P.L.ent_w);
+        const float* sgv = (d[GD_POOL] && P.shared_gate) ? wsp<float>(P, P.L.sg) : nullptr;
+#pragma unroll
+        for (int n = 0; n < kGroupMaxTok; ++n) {
+            if (n < d[GD_NT]) {
+                float w = __ldcg(ent_w + d[GD_E0] + n);
+                if (sgv) w *= __ldcg(sgv + d[GD_TOK + n]);
+                ext[2 + n] = w;
+            }
+        }
+    }
 }
 
 // ------------------------------------------------------------------ 2. gate_up + SwiGLU
@@ -119,12 +150,16 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_gate_up_tma(FfnParams P) {
         for (int base = blockIdx.x; base < n_items && ok; base += 32 * gridDim.x) {
             const int my_item = base + lane * gridDim.x;
             int d[kDescInts];
-            if (my_item < n_items) load_desc(P, my_item / tiles, d);
+            float ext[kHdrExt];
+            if (my_item < n_items) load_desc_ext<false>(P, my_item / tiles, d, ext);
             const int n_here = min(32, (n_items - base + (int)gridDim.x - 1) / (int)gridDim.x);
             for (int i = 0; i < n_here; ++i, ++it) {
                 int dd[kDescInts];
+                float ee[kHdrExt];
 #pragma unroll
                 for (int k = 0; k < kDescInts; ++k) dd[k] = __shfl_sync(0xffffffffu, d[k], i);
+#pragma unroll
+                for (int k = 0; k < kHdrExt; ++k) ee[k] = __shfl_sync(0xffffffffu, ext[k], i);
                 if (lane == 0) {
                     const int item = base + i * gridDim.x;
                     const int st = it % NST;
@@ -140,6 +175,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_gate_up_tma(FfnParams P) {
                         int* hdr = reinterpret_cast<int*>(stg);
 #pragma unroll
                         for (int k = 0; k < kDescInts; ++k) hdr[k] = dd[k];
+#pragma unroll
+                        for (int k = 0; k < kHdrExt; ++k)
+                            reinterpret_cast<float*>(hdr + kDescInts)[k] = ee[k];
                         mbar_arrive_expect_tx(&full[st], (uint32_t)(32 * cb + 32 * sb + nt * H * 2));
                         const int64_t r0 = (int64_t)rt * 16;
                         bulk_rows(stg + off_codes,
@@ -185,7 +223,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_gate_up_tma(FfnParams P) {
         const int rt = item % tiles;
         const uint8_t* stg = smem + (size_t)st * stage_bytes;
         const int* hdr = reinterpret_cast<const int*>(stg);
-        const int slot = hdr[GD_SLOT], pl = hdr[GD_POOL], e0 = hdr[GD_E0], nt = hdr[GD_NT];
+        const int e0 = hdr[GD_E0], nt = hdr[GD_NT];
+        // the stage is released before the epilogue: keep its scalars in registers
+        const float gglob = reinterpret_cast<const float*>(hdr + kDescInts)[0];
+        const float uglob = reinterpret_cast<const float*>(hdr + kDescInts)[1];
         const __half* xs = reinterpret_cast<const __half*>(stg + off_x) + g * H;
         const bool has_tok = g < nt;
         float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
@@ -230,9 +271,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_gate_up_tma(FfnParams P) {
             const int row = (l >> 2) + ((v >> 1) << 3);
             const int n = 2 * (l & 3) + (v & 1);
             if (n < nt) {
-                const nvmoe_expert_pool& pool = pl ? P.shared : P.pool;
-                const float hv = silu(sg_ * global_of(pool.gate, slot)) *
-                                 (su_ * global_of(pool.up, slot));
+                const float hv = silu(sg_ * gglob) * (su_ * uglob);
                 h16[(int64_t)(e0 + n) * I + rt * 16 + row] = __float2half_rn(hv);
             }
         }
@@ -272,15 +311,19 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_down_tma(FfnParams P) {
         // ---------------- producer
         const int n_first = min(n_groups, NST);
         int d[kDescInts];
+        float ext[kHdrExt];
         bool ok = true;
         for (int base = 0; base < n_groups && ok; base += 32) {
-            if (base + lane < n_groups) load_desc(P, base + lane, d);
+            if (base + lane < n_groups) load_desc_ext<true>(P, base + lane, d, ext);
             const int n_here = min(32, n_groups - base);
             for (int i = 0; i < n_here; ++i) {
                 const int g = base + i;
                 int dd[kDescInts];
+                float ee[kHdrExt];
 #pragma unroll
                 for (int k = 0; k < kDescInts; ++k) dd[k] = __shfl_sync(0xffffffffu, d[k], i);
+#pragma unroll
+                for (int k = 0; k < kHdrExt; ++k) ee[k] = __shfl_sync(0xffffffffu, ext[k], i);
                 if (lane == 0) {
                     const int st = g % NST;
                     const uint32_t ph = (g / NST) & 1;
@@ -294,6 +337,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_down_tma(FfnParams P) {
                         int* hdr = reinterpret_cast<int*>(stg);
 #pragma unroll
                         for (int k = 0; k < kDescInts; ++k) hdr[k] = dd[k];
+#pragma unroll
+                        for (int k = 0; k < kHdrExt; ++k)
+                            reinterpret_cast<float*>(hdr + kDescInts)[k] = ee[k];
                         mbar_arrive_expect_tx(&full[st], (uint32_t)(16 * (cb + sb) + nt * I * 2));
                         const int64_t r0 = (int64_t)rb * 16;
                         bulk_rows(stg + off_codes,
@@ -340,9 +386,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_down_tma(FfnParams P) {
     float* ypart = P.ypart_smem ? yps : wsp<float>(P, P.L.ypart);
     const int ypstride = P.ypart_smem ? 16 : H;  // floats between entries
     const int ypcol = P.ypart_smem ? 0 : rb * 16;
-    const float* ent_w = wsp<float>(P, P.L.ent_w);
     const int* ent_of = wsp<int>(P, P.L.ent_of);
-    const float* sgv = P.shared_gate ? wsp<float>(P, P.L.sg) : nullptr;
     for (int grp = warp; grp < n_groups; grp += kConsumerWarps) {
         const int st = grp % NST;
         const uint32_t ph = (grp / NST) & 1;
@@ -352,7 +396,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_down_tma(FfnParams P) {
         }
         const uint8_t* stg = smem + (size_t)st * stage_bytes;
         const int* hdr = reinterpret_cast<const int*>(stg);
-        const int slot = hdr[GD_SLOT], pl = hdr[GD_POOL], e0 = hdr[GD_E0], nt = hdr[GD_NT];
+        const int e0 = hdr[GD_E0], nt = hdr[GD_NT];
+        // the stage is released before the epilogue: keep its scalars in registers
+        const float* ext_s = reinterpret_cast<const float*>(hdr + kDescInts);
+        const float dglob = ext_s[0];
+        const float w_lo = ext_s[2 + 2 * q], w_hi = ext_s[3 + 2 * q];  // tokens 2q, 2q+1
         const __half* hs = reinterpret_cast<const __half*>(stg + off_h) + g * I;
         const bool has_tok = g < nt;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -376,8 +424,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_down_tma(FfnParams P) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
-        const nvmoe_expert_pool& pool = pl ? P.shared : P.pool;
-        const float dglob = global_of(pool.down, slot);
         // C fragment: rows g, g+8; tokens 2q, 2q+1 of the group
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
@@ -385,9 +431,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_down_tma(FfnParams P) {
             const int n = 2 * q + (v & 1);
             if (n < nt) {
                 const int e = e0 + n;
-                float wgt = ent_w[e];
-                if (pl && sgv) wgt *= sgv[hdr[GD_TOK + n]];
-                ypart[(int64_t)e * ypstride + ypcol + row] = acc[v] * dglob * wgt;
+                ypart[(int64_t)e * ypstride + ypcol + row] = acc[v] * dglob * ((v & 1) ? w_hi : w_lo);
             }
         }
     }
