@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     for (int base = 0; base < S; base += nthr) {
         const int s = base + tid;
         const int c = s < S ? cnt[s] : 0;
-        const int ng = (c + kGroupMaxTok - 1) / kGroupMaxTok;
+        const int ng = (c + P.grp_tok - 1) / P.grp_tok;
         int tot_a, tot_e, tot_g;
         const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
         const int re = block_exclusive_scan(c, warp_sums, &tot_e);
@@ -307,8 +307,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
                 int* d = desc + (int64_t)(n_grp + rg + i) * kDescInts;
                 d[GD_SLOT] = s;
                 d[GD_POOL] = 0;
-                d[GD_E0] = n_ent + re + i * kGroupMaxTok;
-                d[GD_NT] = min(kGroupMaxTok, c - i * kGroupMaxTok);
+                d[GD_E0] = n_ent + re + i * P.grp_tok;
+                d[GD_NT] = min(P.grp_tok, c - i * P.grp_tok);
             }
         }
         n_act += tot_a;
@@ -329,20 +329,18 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         wsp<int>(P, P.L.ent_tok)[e] = ent_tok_s[e];
         wsp<float>(P, P.L.ent_w)[e] = ent_w_s[e];
     }
-    for (int s = tid; s < S; s += nthr) {  // token lists of the routed groups
+    for (int s = tid; s < S; s += nthr) {  // complete the routed groups' records
         const int eb = act[s];
         if (eb < 0) continue;
         const int c = cnt[s] - eb;  // the cursor ended at base + count
-        for (int i = 0; i * kGroupMaxTok < c; ++i) {
+        for (int i = 0; i * P.grp_tok < c; ++i) {
             int* d = desc + (int64_t)(gbase[s] + i) * kDescInts;
-            for (int k = 0; k < kGroupMaxTok; ++k) {
-                const int e = i * kGroupMaxTok + k;
-                d[GD_TOK + k] = e < c ? ent_tok_s[eb + e] : 0;
-            }
+            finish_record(P, gbase[s] + i, d, ent_tok_s + eb + i * P.grp_tok,
+                          ent_w_s + eb + i * P.grp_tok);
         }
     }
     if (P.has_shared) {
-        const int ngs = (n_tok + kGroupMaxTok - 1) / kGroupMaxTok;
+        const int ngs = (n_tok + P.grp_tok - 1) / P.grp_tok;
         for (int t = tid; t < n_tok; t += nthr) {
             const int e = n_ent + t;
             wsp<int>(P, P.L.ent_tok)[e] = t;
@@ -351,12 +349,15 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         }
         for (int i = tid; i < ngs; i += nthr) {
             int* d = desc + (int64_t)(n_grp + i) * kDescInts;
-            const int nt = min(kGroupMaxTok, n_tok - i * kGroupMaxTok);
+            const int nt = min(P.grp_tok, n_tok - i * P.grp_tok);
             d[GD_SLOT] = 0;
             d[GD_POOL] = 1;
-            d[GD_E0] = n_ent + i * kGroupMaxTok;
+            d[GD_E0] = n_ent + i * P.grp_tok;
             d[GD_NT] = nt;
-            for (int k = 0; k < kGroupMaxTok; ++k) d[GD_TOK + k] = k < nt ? i * kGroupMaxTok + k : 0;
+            int toks[kGroupMaxTok];
+#pragma unroll
+            for (int k = 0; k < kGroupMaxTok; ++k) toks[k] = i * P.grp_tok + k;
+            finish_record(P, n_grp + i, d, toks, nullptr);
         }
         if (tid == 0) {
             wsp<int>(P, P.L.active_slot)[n_act] = 0;

@@ -38,13 +38,29 @@ struct FmtNvfp4 {
     // bytes of one row of K values in the code / scale banks
     __host__ __device__ static constexpr int code_bytes(int k) { return k / 2; }
     __host__ __device__ static constexpr int scale_bytes(int k) { return k / 16; }
-    // A values of step s: two f16x2 regs {K0, K0+1}, {K0+2, K0+3}
+    // A values of step s: two f16x2 regs {K0, K0+1}, {K0+2, K0+3}.  The code word is split
+    // into byte registers by a vector mov (no shift / mask per byte) and each byte converted
+    // by cvt.rn.f16x2.e2m1x2; the scale multiply is exact (E2M1 x E4M3 fits f16).
     __device__ __forceinline__ static void deq(const Row& r, int s, uint32_t& lo, uint32_t& hi) {
         const uint32_t word = (&r.codes.x)[s >> 1];
-        const uint32_t sh = (s & 1) * 16;
         const uint32_t sc = (s < 4) ? prmt(r.scale2, 0, 0x1010) : prmt(r.scale2, 0, 0x3232);
-        lo = hmul2_u32(e2m1x2_to_f16x2((word >> sh) & 0xff), sc);
-        hi = hmul2_u32(e2m1x2_to_f16x2((word >> (sh + 8)) & 0xff), sc);
+        uint32_t a, b;
+        if ((s & 1) == 0)
+            asm("{ .reg .b8 b0, b1, b2, b3;\n\t"
+                "mov.b32 {b0, b1, b2, b3}, %2;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %1, b1; }"
+                : "=r"(a), "=r"(b)
+                : "r"(word));
+        else
+            asm("{ .reg .b8 b0, b1, b2, b3;\n\t"
+                "mov.b32 {b0, b1, b2, b3}, %2;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %0, b2;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %1, b3; }"
+                : "=r"(a), "=r"(b)
+                : "r"(word));
+        lo = hmul2_u32(a, sc);
+        hi = hmul2_u32(b, sc);
     }
     // physical K offset (inside the warp tile) of step s for lane quarter q
     __device__ __forceinline__ static int kofs(int q, int s) { return 32 * q + 4 * s; }

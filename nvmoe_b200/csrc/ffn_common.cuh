@@ -7,22 +7,29 @@
 namespace nvmoe {
 
 constexpr int kPrepThreads = 256;
-constexpr int kGroupMaxTok = 8;  // entries (tokens) per token group, = the MMA N of one tile
-constexpr int kDescInts = 16;    // ints per group descriptor
+constexpr int kGroupMaxTok = 8;  // largest token group (entries), = the MMA N of one tile
+constexpr int kDescInts = 32;    // ints per group record (128 bytes)
 
-// Group descriptor: one token group (<= 8 entries of one active slot).
+// Group record: one token group (<= 8 entries of one active slot), complete enough that the FFN
+// kernel's producer reads nothing else before it issues the group's weight copies.
 enum {
-    GD_SLOT = 0,   // slot in its pool
-    GD_POOL = 1,   // 0 routed pool, 1 shared expert
-    GD_E0 = 2,     // first entry (entries of a group are consecutive)
-    GD_NT = 3,     // number of entries
-    GD_TOK = 4,    // token of each entry (8)
-    GD_END = 12,
+    GD_SLOT = 0,    // slot in its pool
+    GD_POOL = 1,    // 0 routed pool, 1 shared expert
+    GD_E0 = 2,      // first entry (entries of a group are consecutive)
+    GD_NT = 3,      // number of entries
+    GD_TOK = 4,     // token of each entry (8)
+    GD_RT = 12,     // (stage copies only) row tile of the work item
+    GD_GID = 13,    // (stage copies only) group index
+    GD_GGLOB = 16,  // float: gate global scale of the slot (1 when the bank has none)
+    GD_UGLOB = 17,  // float: up global scale
+    GD_DGLOB = 18,  // float: down global scale
+    GD_W = 20,      // float: router weight of each entry (8); 1 for the shared expert
 };
 
 // ------------------------------------------------------------------ workspace layout
 struct WsLayout {
-    size_t hdr, active_slot, tok_cnt, grp_desc, ent_tok, ent_w, ent_of, x16, sg, h16, ypart, total;
+    size_t hdr, active_slot, tok_cnt, grp_desc, grp_done, ent_tok, ent_w, ent_of, x16, sg, h16,
+        ypart, total;
     int a_max, n_ent_max, g_max;
 };
 
@@ -43,6 +50,8 @@ __host__ __device__ inline WsLayout ws_layout(int n_tok, int top_k, int H, int I
     o = align_up(o + 4 * (size_t)L.a_max, 256);
     L.grp_desc = o;
     o = align_up(o + 4 * (size_t)kDescInts * L.g_max, 256);
+    L.grp_done = o;  // per group: gate/up row tiles whose h rows are stored
+    o = align_up(o + 4 * (size_t)L.g_max, 256);
     L.ent_tok = o;
     o = align_up(o + 4 * (size_t)L.n_ent_max, 256);
     L.ent_w = o;
@@ -55,7 +64,7 @@ __host__ __device__ inline WsLayout ws_layout(int n_tok, int top_k, int H, int I
     o = align_up(o + 4 * (size_t)n_tok, 256);
     L.h16 = o;
     o = align_up(o + 2 * (size_t)L.n_ent_max * I, 256);
-    L.ypart = o;  // used by the down kernel only when its shared-memory copy does not fit
+    L.ypart = o;  // used by the down phase only when its shared-memory copy does not fit
     o = align_up(o + 4 * (size_t)L.n_ent_max * H, 256);
     L.total = o;
     return L;
@@ -81,9 +90,8 @@ struct FfnParams {
     unsigned char* ws;
     WsLayout L;
     int32_t* status;
-    int nst_gu, stage_gu;  // gate_up pipeline: stages, bytes per stage
-    int nst_dn, stage_dn;  // down pipeline
-    int ypart_smem;        // 1: the down kernel keeps y_part in shared memory
+    int grp_tok;           // entries per token group: min(8, n_tok), at least 1
+    int ypart_smem;        // 1: the down phase keeps y_part in shared memory
 };
 
 template <typename T>
@@ -92,6 +100,33 @@ __device__ __forceinline__ T* wsp(const FfnParams& P, size_t off) {
 }
 
 #ifdef __CUDACC__
+__device__ __forceinline__ float global_of(const nvmoe_matrix_bank& b, int slot) {
+    return b.global_scale ? __ldcg(b.global_scale + (int64_t)slot * b.global_stride) : 1.0f;
+}
+
+// Completes group record d (slot, pool, e0, nt already set): token of each entry, router weight
+// of each entry (w_of_entry: the group's entries' weights, or null for the shared expert, whose
+// weight is 1 and whose sigmoid gate is applied per token by the down phase), global scales,
+// and resets the group's completion counter.
+__device__ inline void finish_record(const FfnParams& P, int grp, int* d, const int* tok_of_entry,
+                                     const float* w_of_entry) {
+    const nvmoe_expert_pool& pool = d[GD_POOL] ? P.shared : P.pool;
+    const int slot = d[GD_SLOT], nt = d[GD_NT];
+    float* f = reinterpret_cast<float*>(d);
+    for (int k = 0; k < kGroupMaxTok; ++k) {
+        d[GD_TOK + k] = k < nt ? tok_of_entry[k] : 0;
+        f[GD_W + k] = k < nt ? (w_of_entry ? w_of_entry[k] : 1.0f) : 0.0f;
+    }
+    d[GD_RT] = 0;
+    d[GD_GID] = grp;
+    d[14] = d[15] = d[19] = 0;
+    f[GD_GGLOB] = global_of(pool.gate, slot);
+    f[GD_UGLOB] = global_of(pool.up, slot);
+    f[GD_DGLOB] = global_of(pool.down, slot);
+    for (int k = 28; k < kDescInts; ++k) d[k] = 0;
+    wsp<int>(P, P.L.grp_done)[grp] = 0;
+}
+
 // Token rows -> f16 copy (the MMA B operand) and the shared-expert gate sigmoid(x . g), for
 // tokens t = t_begin, t_begin + t_step, ... by the whole block.
 __device__ inline void ffn_convert_tokens(const FfnParams& P, int t_begin, int t_step) {
@@ -159,7 +194,7 @@ __device__ inline void ffn_group_block(const FfnParams& P, int* smem_i) {
     for (int base = 0; base < S; base += nthr) {
         const int s = base + tid;
         const int c = s < S ? cnt[s] : 0;
-        const int ng = (c + kGroupMaxTok - 1) / kGroupMaxTok;
+        const int ng = (c + P.grp_tok - 1) / P.grp_tok;
         int tot_a, tot_e, tot_g;
         const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
         const int re = block_exclusive_scan(c, warp_sums, &tot_e);
@@ -172,8 +207,8 @@ __device__ inline void ffn_group_block(const FfnParams& P, int* smem_i) {
                 int* d = desc + (int64_t)(n_grp + rg + i) * kDescInts;
                 d[GD_SLOT] = s;
                 d[GD_POOL] = 0;
-                d[GD_E0] = n_ent + re + i * kGroupMaxTok;
-                d[GD_NT] = min(kGroupMaxTok, c - i * kGroupMaxTok);
+                d[GD_E0] = n_ent + re + i * P.grp_tok;
+                d[GD_NT] = min(P.grp_tok, c - i * P.grp_tok);
             }
         }
         n_act += tot_a;
@@ -196,28 +231,29 @@ __device__ inline void ffn_group_block(const FfnParams& P, int* smem_i) {
         ent_of[t * (K + 1) + j] = e;
     }
     __syncthreads();
-    // token ids of every routed group (the entries of a group are consecutive)
+    // complete the routed groups' records (the entries of a group are consecutive)
     for (int g = tid; g < n_grp; g += nthr) {
         int* d = desc + (int64_t)g * kDescInts;
-        const int e0 = d[GD_E0], nt = d[GD_NT];
-        for (int i = 0; i < kGroupMaxTok; ++i) d[GD_TOK + i] = i < nt ? ent_tok[e0 + i] : 0;
+        const int e0 = d[GD_E0];
+        finish_record(P, g, d, ent_tok + e0, ent_w + e0);
     }
     if (P.has_shared) {
-        const int ngs = (P.n_tok + kGroupMaxTok - 1) / kGroupMaxTok;
+        const int ngs = (P.n_tok + P.grp_tok - 1) / P.grp_tok;
         for (int t = tid; t < P.n_tok; t += nthr) {
             const int e = n_ent + t;
             ent_tok[e] = t;
-            ent_w[e] = 1.0f;  // the sigmoid gate is applied by the down kernel
+            ent_w[e] = 1.0f;  // the sigmoid gate is applied by the down phase
             ent_of[t * (K + 1) + K] = e;
         }
+        __syncthreads();
         for (int i = tid; i < ngs; i += nthr) {
             int* d = desc + (int64_t)(n_grp + i) * kDescInts;
-            const int nt = min(kGroupMaxTok, P.n_tok - i * kGroupMaxTok);
+            const int nt = min(P.grp_tok, P.n_tok - i * P.grp_tok);
             d[GD_SLOT] = 0;
             d[GD_POOL] = 1;
-            d[GD_E0] = n_ent + i * kGroupMaxTok;
+            d[GD_E0] = n_ent + i * P.grp_tok;
             d[GD_NT] = nt;
-            for (int k = 0; k < kGroupMaxTok; ++k) d[GD_TOK + k] = k < nt ? i * kGroupMaxTok + k : 0;
+            finish_record(P, n_grp + i, d, ent_tok + n_ent + i * P.grp_tok, nullptr);
         }
         if (tid == 0) {
             active_slot[n_act] = 0;

@@ -7,19 +7,19 @@
 // plus the always-on shared expert (nvme_offload_cache.py:2115-2123).
 //
 // Kernels (chained with programmatic dependent launch):
-//   prep    — x -> f16, shared-expert gate, grouping of the (token, k) entries by slot into
-//             token groups of <= 8 entries (ffn_common.cuh); the fused decode front kernel does
-//             the same work in the engine path
-//   gate_up — persistent, 1 CTA / SM: a producer warp streams work items (token group, 16 rows of
-//             gate + the same rows of up) with 1-D bulk copies (TMA) into a ring of shared-memory
-//             stages; 8 consumer warps split K, dequantise A fragments in registers from the
-//             staged bytes, run m16n8k16 f16 MMAs (fp32 accumulate), reduce across warps and
-//             write h = silu(g) * u (f16) per entry
-//   down    — one CTA per 16 output rows: the producer streams every token group's 16 down rows
-//             (issued before the grid-dependency wait: weights do not depend on gate_up) and its
-//             h rows; each consumer warp owns whole groups (full K), writes w * down(h) per entry
-//             into shared memory, and the CTA finally sums the entries of each token in the
-//             fixed order j = 0..k-1, shared, and stores bf16 y.  No atomics, deterministic.
+//   prep  — x -> f16, shared-expert gate, grouping of the (token, k) entries by slot into token
+//           groups of <= 8 entries with complete group records (ffn_common.cuh); the fused
+//           decode front kernel does the same work in the engine path
+//   fused — persistent, one CTA per SM, warp-specialised: a producer warp streams gate_up work
+//           items (token group x 16 rows of gate and of up) and then down slabs (16 rows of a
+//           CTA's output tile for every group) with 1-D bulk copies (TMA) into two rings of
+//           shared-memory stages; 8 MMA warps dequantise A fragments in registers from the
+//           staged bytes and run m16n8k16 f16 MMAs (fp32 accumulate); an epilogue warp sums the
+//           gate_up partials of the 8 warps, stores h = silu(g) * u (f16) and publishes each
+//           finished row tile on a per-group counter; the down phase starts a group once its
+//           counter is complete, writes w * down(h) per entry into shared memory, and each CTA
+//           finally sums the entries of each token in the fixed order j = 0..k-1, shared, and
+//           stores bf16 y.  No atomics on data, deterministic.
 // Only the slots that occur in slot_ids are read; every weight byte is read once per call.
 #include "common.cuh"
 #include "dequant_frag.cuh"
@@ -32,10 +32,11 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kTmaThreads = kConsumers + 32;  // + one producer warp
 constexpr int kSmemCap = 227 * 1024 - 1024;   // dynamic share; static use stays below 1 KB
-constexpr int kStageHdr = 128;  // per stage: group descriptor + scalars fetched by the producer
-constexpr int kHdrExt = 10;     // header floats after the descriptor (see load_desc_ext)
+// x rows in a gate_up stage are kXPad bytes apart beyond their length, so the 8 token rows of
+// a B-fragment load fall into different shared-memory banks
+constexpr int kXPad = 16;
+constexpr int kStageHdr = 128;  // per stage: a copy of the group record (kDescInts ints)
 
 // ------------------------------------------------------------------ 1. prep
 __global__ void __launch_bounds__(kPrepThreads) ffn_prep_kernel(FfnParams P) {
@@ -65,140 +66,263 @@ __device__ __forceinline__ void bulk_rows(uint8_t* dst, const uint8_t* src, int 
     }
 }
 
-// Loads the descriptor of group `grp` (16 ints) with L2 reads.
-__device__ __forceinline__ void load_desc(const FfnParams& P, int grp, int (&d)[kDescInts]) {
+// ------------------------------------------------------------------ 2. fused gate_up + down
+// Shared memory: [gate_up ring][resident x][down ring][red: 2 x 8 warps x 32 lanes x 8
+// floats][meta: 2 x 8 ints][y_part (optional)][mbarriers].  Once the gate_up phase has drained,
+// its ring's bytes hold further down stages.
+//   gate_up stage: [record 128 B] gate codes [16][H/2] | up codes | gate scales [16][H/16] |
+//                  up scales | x [XT][H + 8] f16 when x is staged per item (XT = the largest
+//                  group of this launch; the 8 extra halves per row only spread the rows over
+//                  the banks); resident x: [n_tok][H + 8] f16 once per CTA (n_tok <= 8)
+//   down stage   : [record 128 B] codes [16][I/2] | scales [16][I/16]
+struct FusedLayout {
+    int stage_gu, stage_dn;  // bytes per stage
+    int nst_gu;              // gate_up ring stages
+    int nst_dn;              // down stages in their own region (a multiple of 8)
+    int nst_dn_ext;          // down stages carved from the gate_up ring once it has drained
+    int xt;                  // x rows per gate_up stage (staged x), 0 with resident x
+    int x_res;               // 1: every token row resident in shared memory, loaded once
+    int off_x, off_dn, off_red, off_meta, off_yp, off_bar, total;
+};
+
+__host__ __device__ inline int round128(int v) { return (v + 127) / 128 * 128; }
+
+// One 128-wide K tile of a 16-row gate + up item: rows g and g + 8 of both matrices for the
+// lane quarter q, B = the activations of the group's tokens (token g of the lane).
+// The MMAs of consecutive steps go to kAcc independent accumulators (a single accumulator
+// chains every mma.sync on the previous one's result and leaves the warp latency-bound); the
+// accumulators are summed in a fixed order at the end of the item.
+constexpr int kAcc = 8;
+
+template <typename Fmt>
+__device__ __forceinline__ void gate_up_tile(const uint8_t* gcode, const uint8_t* ucode,
+                                             const uint8_t* gsc, const uint8_t* usc, int cb,
+                                             int sb, const __half* xs, bool has_tok, int k0,
+                                             int g, int q, float (&accg)[kAcc][4],
+                                             float (&accu)[kAcc][4]) {
+    typename Fmt::Row ga, gb, ua, ub;
+    Fmt::load_smem(ga, gcode + g * cb, gsc + g * sb, k0, q);
+    Fmt::load_smem(gb, gcode + (g + 8) * cb, gsc + (g + 8) * sb, k0, q);
+    Fmt::load_smem(ua, ucode + g * cb, usc + g * sb, k0, q);
+    Fmt::load_smem(ub, ucode + (g + 8) * cb, usc + (g + 8) * sb, k0, q);
+#pragma unroll
+    for (int s2 = 0; s2 < Fmt::kSteps; s2 += 2) {
+        const uint4 xb = has_tok ? *reinterpret_cast<const uint4*>(xs + k0 + Fmt::kofs(q, s2))
+                                 : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int ss = 0; ss < 2; ++ss) {
+            uint32_t ag[4], au[4];
+            Fmt::deq(ga, s2 + ss, ag[0], ag[2]);
+            Fmt::deq(gb, s2 + ss, ag[1], ag[3]);
+            Fmt::deq(ua, s2 + ss, au[0], au[2]);
+            Fmt::deq(ub, s2 + ss, au[1], au[3]);
+            const uint32_t b0 = ss ? xb.z : xb.x, b1 = ss ? xb.w : xb.y;
+            mma_f16_16816(accg[(s2 + ss) % kAcc], ag, b0, b1);
+            mma_f16_16816(accu[(s2 + ss) % kAcc], au, b0, b1);
+        }
+    }
+}
+
+// One 128-wide K tile of a 16-row down slab: rows g and g + 8; hb = the lane's h fragments of
+// this tile (4 x 8 halves of token g).
+template <typename Fmt>
+__device__ __forceinline__ void down_tile(const uint8_t* code, const uint8_t* sc, int cb, int sb,
+                                          const uint4 (&hb)[4], int k0, int g, int q,
+                                          float (&acc)[kAcc][4]) {
+    typename Fmt::Row ra, rbw;
+    Fmt::load_smem(ra, code + g * cb, sc + g * sb, k0, q);
+    Fmt::load_smem(rbw, code + (g + 8) * cb, sc + (g + 8) * sb, k0, q);
+#pragma unroll
+    for (int s2 = 0; s2 < Fmt::kSteps; s2 += 2) {
+        const uint4 h = hb[s2 >> 1];
+#pragma unroll
+        for (int ss = 0; ss < 2; ++ss) {
+            uint32_t af[4];
+            Fmt::deq(ra, s2 + ss, af[0], af[2]);
+            Fmt::deq(rbw, s2 + ss, af[1], af[3]);
+            mma_f16_16816(acc[(s2 + ss) % kAcc], af, ss ? h.z : h.x, ss ? h.w : h.y);
+        }
+    }
+}
+
+// Sum of the kAcc accumulators (fixed order) into acc[0].
+__device__ __forceinline__ void fold_acc(float (&acc)[kAcc][4]) {
+#pragma unroll
+    for (int a = 1; a < kAcc; ++a)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[0][v] += acc[a][v];
+}
+
+// h fragments of one 128-wide K tile for token row hrow (null: no token -> zeros), read through
+// L2 (h is written by other CTAs of this grid).
+__device__ __forceinline__ void load_h_tile(const __half* hrow, int k0, int q, uint4 (&hb)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        hb[i] = hrow ? __ldcg(reinterpret_cast<const uint4*>(hrow + k0 + 32 * q + 8 * i))
+                     : make_uint4(0, 0, 0, 0);
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until the group's h rows are complete (all I/16 gate/up row tiles stored).
+__device__ __forceinline__ bool wait_group_h(const int* done, int target) {
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        if (ld_acquire_gpu(done) >= target) return true;
+        if (i > 64) __nanosleep(64);
+    }
+    return false;
+}
+
+__device__ __forceinline__ void copy_record(int* dst, const int4 (&r)[kDescInts / 4]) {
+#pragma unroll
+    for (int k = 0; k < kDescInts / 4; ++k) reinterpret_cast<int4*>(dst)[k] = r[k];
+}
+__device__ __forceinline__ void load_record(const FfnParams& P, int grp, int4 (&r)[kDescInts / 4]) {
     const int4* src = reinterpret_cast<const int4*>(wsp<int>(P, P.L.grp_desc) +
                                                     (int64_t)grp * kDescInts);
 #pragma unroll
-    for (int i = 0; i < kDescInts / 4; ++i) {
-        const int4 v = __ldcg(src + i);
-        d[4 * i] = v.x, d[4 * i + 1] = v.y, d[4 * i + 2] = v.z, d[4 * i + 3] = v.w;
+    for (int k = 0; k < kDescInts / 4; ++k) r[k] = __ldcg(src + k);
+}
+__device__ __forceinline__ void shfl_record(int4 (&dst)[kDescInts / 4],
+                                            const int4 (&src)[kDescInts / 4], int lane) {
+#pragma unroll
+    for (int k = 0; k < kDescInts / 4; ++k) {
+        dst[k].x = __shfl_sync(0xffffffffu, src[k].x, lane);
+        dst[k].y = __shfl_sync(0xffffffffu, src[k].y, lane);
+        dst[k].z = __shfl_sync(0xffffffffu, src[k].z, lane);
+        dst[k].w = __shfl_sync(0xffffffffu, src[k].w, lane);
     }
 }
 
-__device__ __forceinline__ float global_of(const nvmoe_matrix_bank& b, int slot) {
-    return b.global_scale ? __ldcg(b.global_scale + (int64_t)slot * b.global_stride) : 1.0f;
-}
+constexpr int kCW = kConsumerWarps;       // MMA warps
+constexpr int kProdGU = kCW;              // bulk-copy producer of the gate_up items
+constexpr int kEpiWarp = kCW + 1;         // gate/up cross-warp sum + SwiGLU + h store
+constexpr int kProdDN = kCW + 2;          // bulk-copy producer of the down slabs
+constexpr int kFusedThreads = (kCW + 3) * 32;
 
-// Scalars an item needs in its epilogue, fetched by the producer lanes in parallel (off the
-// consumers' critical path) and shipped in the stage header after the descriptor:
-//   gate_up: ext[0] = gate global, ext[1] = up global
-//   down   : ext[0] = down global, ext[2 + n] = combine weight of entry n (times the shared
-//            expert's sigmoid gate for the shared pool)
-template <bool kDown>
-__device__ __forceinline__ void load_desc_ext(const FfnParams& P, int grp, int (&d)[kDescInts],
-                                              float (&ext)[kHdrExt]) {
-    load_desc(P, grp, d);
-    const nvmoe_expert_pool& pool = d[GD_POOL] ? P.shared : P.pool;
-#pragma unroll
-    for (int i = 0; i < kHdrExt; ++i) ext[i] = 0.f;
-    if (!kDown) {
-        ext[0] = global_of(pool.gate, d[GD_SLOT]);
-        ext[1] = global_of(pool.up, d[GD_SLOT]);
-    } else {
-        ext[0] = global_of(pool.down, d[GD_SLOT]);
-        const float* ent_w = wsp<float>(P, P.L.ent_w);
-        const float* sgv = (d[GD_POOL] && P.shared_gate) ? wsp<float>(P, P.L.sg) : nullptr;
-#pragma unroll
-        for (int n = 0; n < kGroupMaxTok; ++n) {
-            if (n < d[GD_NT]) {
-                float w = __ldcg(ent_w + d[GD_E0] + n);
-                if (sgv) w *= __ldcg(sgv + d[GD_TOK + n]);
-                ext[2 + n] = w;
-            }
-        }
-    }
-}
-
-// ------------------------------------------------------------------ 2. gate_up + SwiGLU
-// Stage layout: [hdr 64 B] gate codes [16][H/2] | up codes | gate scales [16][H/16] |
-// up scales | x [8][H] f16.
-template <typename Fmt>
-__global__ void __launch_bounds__(kTmaThreads, 1) ffn_gate_up_tma(FfnParams P) {
+// Persistent expert FFN, one CTA per SM.  CTA c runs
+//   gate_up items c, c + G, ... (item = token group x 16 rows of gate and of up, full K = H),
+//   then down row tiles r = G - 1 - c, 2G - 1 - c, ... (16 rows of y over every group, K = I).
+// Roles: two producer warps stream the two phases' weights into their rings (down weights do
+// not depend on h, so they are in flight while gate_up runs); the 8 MMA warps split K of a
+// gate_up item (TPW tiles each, straight-line code) and hand their partial sums to the
+// epilogue warp through a 2-deep ring, so they never wait for the cross-warp sum; the epilogue
+// warp stores h and counts the group's finished row tiles (release); a down MMA warp owns whole
+// groups and starts a group once its count is complete (acquire).
+template <typename Fmt, int TPW, int TD>
+__global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, FusedLayout FL) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int H = P.pool.hidden, I = P.pool.inter;
-    const int NST = P.nst_gu;
-    const int stage_bytes = P.stage_gu;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)NST * stage_bytes);
-    uint64_t* empty = full + NST;
-    float* red = reinterpret_cast<float*>(empty + NST);  // [8 warps][32 lanes][8]
+    const int G = gridDim.x;
+    const int NGU = FL.nst_gu, NDT = FL.nst_dn + FL.nst_dn_ext;
+    uint64_t* gu_full = reinterpret_cast<uint64_t*>(smem + FL.off_bar);
+    uint64_t* gu_empty = gu_full + NGU;
+    uint64_t* dn_full = gu_empty + NGU;
+    uint64_t* dn_empty = dn_full + NDT;
+    uint64_t* red_full = dn_empty + NDT;
+    uint64_t* red_empty = red_full + 2;
+    uint64_t* x_full = red_empty + 2;
+    uint64_t* gu_drained = x_full + 1;
+    float* red = reinterpret_cast<float*>(smem + FL.off_red);
+    int* meta = reinterpret_cast<int*>(smem + FL.off_meta);
     if (tid == 0) {
-        for (int s = 0; s < NST; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
+        for (int s = 0; s < NGU; ++s) mbar_init(&gu_full[s], 1), mbar_init(&gu_empty[s], kCW);
+        for (int s = 0; s < NDT; ++s) mbar_init(&dn_full[s], 1), mbar_init(&dn_empty[s], 1);
+        for (int s = 0; s < 2; ++s) mbar_init(&red_full[s], kCW), mbar_init(&red_empty[s], 1);
+        mbar_init(x_full, 1);
+        mbar_init(gu_drained, kCW);
         mbar_init_fence();
     }
     __syncthreads();
+    // everything below reads the group records / token rows of the kernel before this one
     grid_dep_wait();
     grid_dep_launch();
 
-    const int tiles = I / 16;
-    const int n_groups = __ldcg(wsp<int>(P, P.L.hdr) + HDR_N_GROUPS);
-    const int n_items = n_groups * tiles;
-    const int cb = Fmt::code_bytes(H), sb = Fmt::scale_bytes(H);
-    const int off_codes = kStageHdr, off_ucodes = kStageHdr + 16 * cb;
-    const int off_gsc = kStageHdr + 32 * cb, off_usc = off_gsc + 16 * sb;
-    const int off_x = off_usc + 16 * sb;
+    const int tiles_i = I / 16, n_dn = H / 16;
+    const int cbg = Fmt::code_bytes(H), sbg = Fmt::scale_bytes(H);
+    const int cbd = Fmt::code_bytes(I), sbd = Fmt::scale_bytes(I);
+    const int og_uc = kStageHdr + 16 * cbg, og_gs = kStageHdr + 32 * cbg;
+    const int og_us = og_gs + 16 * sbg, og_x = og_us + 16 * sbg;
+    const int od_sc = kStageHdr + 16 * cbd;
+    const int xrow = H * 2 + kXPad;  // bytes between x rows in shared memory
     const __half* x16 = wsp<__half>(P, P.L.x16);
+    __half* h16 = wsp<__half>(P, P.L.h16);
+    int* done = wsp<int>(P, P.L.grp_done);
+    const int* hdr_g = wsp<int>(P, P.L.hdr);
+    // down stage st: its own region first, then the drained gate_up ring
+    auto dn_stage = [&](int st) -> uint8_t* {
+        return st < FL.nst_dn ? smem + FL.off_dn + (size_t)st * FL.stage_dn
+                              : smem + (size_t)(st - FL.nst_dn) * FL.stage_dn;
+    };
 
-    if (warp == kConsumerWarps) {
-        // ---------------- producer: descriptors of 32 items at a time, one per lane
-        int it = 0;
+    if (warp == kProdGU) {
+        // the first batch of records is fetched together with the group count (speculative
+        // group indices, clamped into the workspace)
+        int4 rec[kDescInts / 4];
+        load_record(P, min((int)(blockIdx.x + lane * G) / tiles_i, P.L.g_max - 1), rec);
+        const int n_groups = __ldcg(hdr_g + HDR_N_GROUPS);
+        const int n_gu = n_groups * tiles_i;
+        if (FL.x_res && lane == 0 && n_gu > (int)blockIdx.x) {
+            mbar_arrive_expect_tx(x_full, (uint32_t)(P.n_tok * H * 2));
+            for (int t = 0; t < P.n_tok; ++t)
+                bulk_g2s(smem + FL.off_x + t * xrow, x16 + (int64_t)t * H, (uint32_t)(H * 2), x_full);
+        }
         bool ok = true;
-        for (int base = blockIdx.x; base < n_items && ok; base += 32 * gridDim.x) {
-            const int my_item = base + lane * gridDim.x;
-            int d[kDescInts];
-            float ext[kHdrExt];
-            if (my_item < n_items) load_desc_ext<false>(P, my_item / tiles, d, ext);
-            const int n_here = min(32, (n_items - base + (int)gridDim.x - 1) / (int)gridDim.x);
+        int it = 0;
+        for (int base = blockIdx.x; base < n_gu && ok; base += 32 * G) {
+            const int mine = base + lane * G;
+            if (base != (int)blockIdx.x && mine < n_gu) load_record(P, mine / tiles_i, rec);
+            const int n_here = min(32, (n_gu - base + G - 1) / G);
             for (int i = 0; i < n_here; ++i, ++it) {
-                int dd[kDescInts];
-                float ee[kHdrExt];
-#pragma unroll
-                for (int k = 0; k < kDescInts; ++k) dd[k] = __shfl_sync(0xffffffffu, d[k], i);
-#pragma unroll
-                for (int k = 0; k < kHdrExt; ++k) ee[k] = __shfl_sync(0xffffffffu, ext[k], i);
+                int4 r[kDescInts / 4];
+                shfl_record(r, rec, i);
                 if (lane == 0) {
-                    const int item = base + i * gridDim.x;
-                    const int st = it % NST;
-                    const uint32_t ph = (it / NST) & 1;
-                    if (!mbar_wait_bounded(&empty[st], ph ^ 1)) {
+                    const int item = base + i * G;
+                    const int st = it % NGU;
+                    if (!mbar_wait_bounded(&gu_empty[st], ((it / NGU) & 1) ^ 1)) {
                         report_timeout(P);
                         ok = false;
                     } else {
-                        const int rt = item % tiles;
-                        const nvmoe_expert_pool& pool = dd[GD_POOL] ? P.shared : P.pool;
-                        const int slot = dd[GD_SLOT], nt = dd[GD_NT];
-                        uint8_t* stg = smem + (size_t)st * stage_bytes;
+                        uint8_t* stg = smem + (size_t)st * FL.stage_gu;
                         int* hdr = reinterpret_cast<int*>(stg);
-#pragma unroll
-                        for (int k = 0; k < kDescInts; ++k) hdr[k] = dd[k];
-#pragma unroll
-                        for (int k = 0; k < kHdrExt; ++k)
-                            reinterpret_cast<float*>(hdr + kDescInts)[k] = ee[k];
-                        mbar_arrive_expect_tx(&full[st], (uint32_t)(32 * cb + 32 * sb + nt * H * 2));
-                        const int64_t r0 = (int64_t)rt * 16;
-                        bulk_rows(stg + off_codes,
+                        copy_record(hdr, r);
+                        hdr[GD_RT] = item % tiles_i;
+                        hdr[GD_GID] = item / tiles_i;
+                        const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
+                        const int slot = hdr[GD_SLOT], nt = hdr[GD_NT];
+                        const int64_t r0 = (int64_t)(item % tiles_i) * 16;
+                        mbar_arrive_expect_tx(
+                            &gu_full[st],
+                            (uint32_t)(32 * cbg + 32 * sbg + (FL.x_res ? 0 : nt * H * 2)));
+                        bulk_rows(stg + kStageHdr,
                                   (const uint8_t*)pool.gate.data + slot * pool.gate.slot_stride +
                                       r0 * pool.gate.row_stride,
-                                  16, cb, pool.gate.row_stride, &full[st]);
-                        bulk_rows(stg + off_ucodes,
+                                  16, cbg, pool.gate.row_stride, &gu_full[st]);
+                        bulk_rows(stg + og_uc,
                                   (const uint8_t*)pool.up.data + slot * pool.up.slot_stride +
                                       r0 * pool.up.row_stride,
-                                  16, cb, pool.up.row_stride, &full[st]);
-                        bulk_rows(stg + off_gsc,
-                                  (const uint8_t*)pool.gate.scale + slot * pool.gate.scale_slot_stride +
+                                  16, cbg, pool.up.row_stride, &gu_full[st]);
+                        bulk_rows(stg + og_gs,
+                                  (const uint8_t*)pool.gate.scale +
+                                      slot * pool.gate.scale_slot_stride +
                                       r0 * pool.gate.scale_row_stride,
-                                  16, sb, pool.gate.scale_row_stride, &full[st]);
-                        bulk_rows(stg + off_usc,
+                                  16, sbg, pool.gate.scale_row_stride, &gu_full[st]);
+                        bulk_rows(stg + og_us,
                                   (const uint8_t*)pool.up.scale + slot * pool.up.scale_slot_stride +
                                       r0 * pool.up.scale_row_stride,
-                                  16, sb, pool.up.scale_row_stride, &full[st]);
-                        for (int n = 0; n < nt; ++n)
-                            bulk_g2s(stg + off_x + n * H * 2, x16 + (int64_t)dd[GD_TOK + n] * H,
-                                     (uint32_t)(H * 2), &full[st]);
+                                  16, sbg, pool.up.scale_row_stride, &gu_full[st]);
+                        if (!FL.x_res)
+                            for (int n = 0; n < nt; ++n)
+                                bulk_g2s(stg + og_x + n * xrow, x16 + (int64_t)hdr[GD_TOK + n] * H,
+                                         (uint32_t)(H * 2), &gu_full[st]);
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -208,244 +332,254 @@ __global__ void __launch_bounds__(kTmaThreads, 1) ffn_gate_up_tma(FfnParams P) {
         return;
     }
 
-    // ---------------- consumers
-    const int g = lane >> 2, q = lane & 3;
-    const int KW = H / kConsumerWarps;
-    __half* h16 = wsp<__half>(P, P.L.h16);
-    int it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
-        const int st = it % NST;
-        const uint32_t ph = (it / NST) & 1;
-        if (!mbar_wait_bounded(&full[st], ph)) {
-            report_timeout(P);
-            break;
-        }
-        const int rt = item % tiles;
-        const uint8_t* stg = smem + (size_t)st * stage_bytes;
-        const int* hdr = reinterpret_cast<const int*>(stg);
-        const int e0 = hdr[GD_E0], nt = hdr[GD_NT];
-        // the stage is released before the epilogue: keep its scalars in registers
-        const float gglob = reinterpret_cast<const float*>(hdr + kDescInts)[0];
-        const float uglob = reinterpret_cast<const float*>(hdr + kDescInts)[1];
-        const __half* xs = reinterpret_cast<const __half*>(stg + off_x) + g * H;
-        const bool has_tok = g < nt;
-        float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k0 = warp * KW; k0 < (warp + 1) * KW; k0 += Fmt::kWarpTileK) {
-            typename Fmt::Row ga, gb, ua, ub;
-            Fmt::load_smem(ga, stg + off_codes + g * cb, stg + off_gsc + g * sb, k0, q);
-            Fmt::load_smem(gb, stg + off_codes + (g + 8) * cb, stg + off_gsc + (g + 8) * sb, k0, q);
-            Fmt::load_smem(ua, stg + off_ucodes + g * cb, stg + off_usc + g * sb, k0, q);
-            Fmt::load_smem(ub, stg + off_ucodes + (g + 8) * cb, stg + off_usc + (g + 8) * sb, k0, q);
-#pragma unroll
-            for (int s2 = 0; s2 < Fmt::kSteps; s2 += 2) {
-                const uint4 xb = has_tok
-                                     ? *reinterpret_cast<const uint4*>(xs + k0 + Fmt::kofs(q, s2))
-                                     : make_uint4(0, 0, 0, 0);
-#pragma unroll
-                for (int ss = 0; ss < 2; ++ss) {
-                    uint32_t ag[4], au[4];
-                    Fmt::deq(ga, s2 + ss, ag[0], ag[2]);
-                    Fmt::deq(gb, s2 + ss, ag[1], ag[3]);
-                    Fmt::deq(ua, s2 + ss, au[0], au[2]);
-                    Fmt::deq(ub, s2 + ss, au[1], au[3]);
-                    const uint32_t b0 = ss ? xb.z : xb.x, b1 = ss ? xb.w : xb.y;
-                    mma_f16_16816(accg, ag, b0, b1);
-                    mma_f16_16816(accu, au, b0, b1);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);  // the stage can be refilled
-        float* rw = red + (warp * 32 + lane) * 8;
-#pragma unroll
-        for (int v = 0; v < 4; ++v) rw[v] = accg[v], rw[4 + v] = accu[v];
-        named_bar_sync(1, kConsumers);
-        if (tid < 128) {
-            const int l = tid >> 2, v = tid & 3;
-            float sg_ = 0.f, su_ = 0.f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) {
-                sg_ += red[(w * 32 + l) * 8 + v];
-                su_ += red[(w * 32 + l) * 8 + 4 + v];
-            }
-            const int row = (l >> 2) + ((v >> 1) << 3);
-            const int n = 2 * (l & 3) + (v & 1);
-            if (n < nt) {
-                const float hv = silu(sg_ * gglob) * (su_ * uglob);
-                h16[(int64_t)(e0 + n) * I + rt * 16 + row] = __float2half_rn(hv);
-            }
-        }
-        named_bar_sync(1, kConsumers);
-    }
-}
-
-// ------------------------------------------------------------------ 3. down + combine
-// Stage layout: [hdr 64 B] codes [16][I/2] | scales [16][I/16] | h [8][I] f16.
-template <typename Fmt>
-__global__ void __launch_bounds__(kTmaThreads, 1) ffn_down_tma(FfnParams P) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int H = P.pool.hidden, I = P.pool.inter;
-    const int NST = P.nst_dn;
-    const int stage_bytes = P.stage_dn;
-    const int rb = blockIdx.x;  // rows [16 rb, 16 rb + 16)
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)NST * stage_bytes);
-    uint64_t* empty = full + NST;
-    float* yps = reinterpret_cast<float*>(empty + NST);  // [n_ent][16] when in shared memory
-    if (tid == 0) {
-        for (int s = 0; s < NST; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);  // one consumer warp per stage use
-        }
-        mbar_init_fence();
-    }
-    __syncthreads();
-    // the group tables come from prep / the front kernel, which completed before the gate_up
-    // grid could pass its own dependency wait; h comes from gate_up (read after grid_dep_wait)
-    const int n_groups = __ldcg(wsp<int>(P, P.L.hdr) + HDR_N_GROUPS);
-    const int cb = Fmt::code_bytes(I), sb = Fmt::scale_bytes(I);
-    const int off_codes = kStageHdr, off_sc = kStageHdr + 16 * cb, off_h = off_sc + 16 * sb;
-    const __half* h16 = wsp<__half>(P, P.L.h16);
-
-    if (warp == kConsumerWarps) {
-        // ---------------- producer
-        const int n_first = min(n_groups, NST);
-        int d[kDescInts];
-        float ext[kHdrExt];
-        bool ok = true;
-        for (int base = 0; base < n_groups && ok; base += 32) {
-            if (base + lane < n_groups) load_desc_ext<true>(P, base + lane, d, ext);
-            const int n_here = min(32, n_groups - base);
-            for (int i = 0; i < n_here; ++i) {
-                const int g = base + i;
-                int dd[kDescInts];
-                float ee[kHdrExt];
-#pragma unroll
-                for (int k = 0; k < kDescInts; ++k) dd[k] = __shfl_sync(0xffffffffu, d[k], i);
-#pragma unroll
-                for (int k = 0; k < kHdrExt; ++k) ee[k] = __shfl_sync(0xffffffffu, ext[k], i);
-                if (lane == 0) {
-                    const int st = g % NST;
-                    const uint32_t ph = (g / NST) & 1;
-                    if (!mbar_wait_bounded(&empty[st], ph ^ 1)) {
-                        report_timeout(P);
-                        ok = false;
-                    } else {
-                        const nvmoe_expert_pool& pool = dd[GD_POOL] ? P.shared : P.pool;
-                        const int slot = dd[GD_SLOT], nt = dd[GD_NT];
-                        uint8_t* stg = smem + (size_t)st * stage_bytes;
-                        int* hdr = reinterpret_cast<int*>(stg);
-#pragma unroll
-                        for (int k = 0; k < kDescInts; ++k) hdr[k] = dd[k];
-#pragma unroll
-                        for (int k = 0; k < kHdrExt; ++k)
-                            reinterpret_cast<float*>(hdr + kDescInts)[k] = ee[k];
-                        mbar_arrive_expect_tx(&full[st], (uint32_t)(16 * (cb + sb) + nt * I * 2));
-                        const int64_t r0 = (int64_t)rb * 16;
-                        bulk_rows(stg + off_codes,
-                                  (const uint8_t*)pool.down.data + slot * pool.down.slot_stride +
-                                      r0 * pool.down.row_stride,
-                                  16, cb, pool.down.row_stride, &full[st]);
-                        bulk_rows(stg + off_sc,
-                                  (const uint8_t*)pool.down.scale + slot * pool.down.scale_slot_stride +
-                                      r0 * pool.down.scale_row_stride,
-                                  16, sb, pool.down.scale_row_stride, &full[st]);
-                        if (g >= n_first)
-                            bulk_g2s(stg + off_h, h16 + (int64_t)dd[GD_E0] * I,
-                                     (uint32_t)(nt * I * 2), &full[st]);
-                    }
-                }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) break;
-                if (g == n_first - 1) {
-                    // every first-round stage has its weights in flight; now wait for gate_up
-                    grid_dep_wait();
-                    if (lane == 0)
-                        for (int gg = 0; gg < n_first; ++gg) {
-                            const int* hdr =
-                                reinterpret_cast<const int*>(smem + (size_t)gg * stage_bytes);
-                            bulk_g2s(smem + (size_t)gg * stage_bytes + off_h,
-                                     h16 + (int64_t)hdr[GD_E0] * I, (uint32_t)(hdr[GD_NT] * I * 2),
-                                     &full[gg]);
+    if (warp == kProdDN) {
+        // down slabs: for each of this CTA's row tiles, every group's 16 rows; stages past the
+        // dedicated region wait until the gate_up ring has drained
+        int4 rec[kDescInts / 4];
+        load_record(P, min(lane, P.L.g_max - 1), rec);
+        const int n_groups = __ldcg(hdr_g + HDR_N_GROUPS);
+        bool ok = true, drained = false;
+        int j = 0;
+        for (int rt = G - 1 - (int)blockIdx.x; rt < n_dn && ok; rt += G) {
+            for (int base = 0; base < n_groups && ok; base += 32) {
+                if ((base != 0 || j != 0) && base + lane < n_groups) load_record(P, base + lane, rec);
+                const int n_here = min(32, n_groups - base);
+                for (int i = 0; i < n_here; ++i, ++j) {
+                    int4 r[kDescInts / 4];
+                    shfl_record(r, rec, i);
+                    if (lane == 0) {
+                        const int st = j % NDT;
+                        if (st >= FL.nst_dn && !drained) {
+                            if (!mbar_wait_bounded(gu_drained, 0)) {
+                                report_timeout(P);
+                                ok = false;
+                            }
+                            drained = true;
                         }
+                        if (ok && !mbar_wait_bounded(&dn_empty[st], ((j / NDT) & 1) ^ 1)) {
+                            report_timeout(P);
+                            ok = false;
+                        }
+                        if (ok) {
+                            uint8_t* stg = dn_stage(st);
+                            int* hdr = reinterpret_cast<int*>(stg);
+                            copy_record(hdr, r);
+                            hdr[GD_GID] = base + i;
+                            const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
+                            const int slot = hdr[GD_SLOT];
+                            const int64_t r0 = (int64_t)rt * 16;
+                            mbar_arrive_expect_tx(&dn_full[st], (uint32_t)(16 * (cbd + sbd)));
+                            bulk_rows(stg + kStageHdr,
+                                      (const uint8_t*)pool.down.data +
+                                          slot * pool.down.slot_stride + r0 * pool.down.row_stride,
+                                      16, cbd, pool.down.row_stride, &dn_full[st]);
+                            bulk_rows(stg + od_sc,
+                                      (const uint8_t*)pool.down.scale +
+                                          slot * pool.down.scale_slot_stride +
+                                          r0 * pool.down.scale_row_stride,
+                                      16, sbd, pool.down.scale_row_stride, &dn_full[st]);
+                        }
+                    }
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
                 }
             }
         }
-        if (n_groups == 0) grid_dep_wait();
         return;
     }
 
-    // ---------------- consumers: warp w owns groups w, w + 8, ...
-    grid_dep_wait();
-    if (n_groups == 0) {  // no valid entry and no shared expert (or an upstream error): y = 0
-        for (int idx = tid; idx < P.n_tok * 16; idx += kConsumers)
-            P.y[(int64_t)(idx >> 4) * P.y_stride + rb * 16 + (idx & 15)] = 0;
+    const int n_groups = __ldcg(hdr_g + HDR_N_GROUPS);
+    const int n_gu = n_groups * tiles_i;
+
+    if (warp == kEpiWarp) {
+        // ---- gate_up epilogue: sum the 8 warps' partials in warp order, h = silu(g) * u
+        int it = 0;
+        for (int item = blockIdx.x; item < n_gu; item += G, ++it) {
+            const int rs = it & 1;
+            if (!mbar_wait_bounded(&red_full[rs], (it >> 1) & 1)) {
+                report_timeout(P);
+                break;
+            }
+            float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int w = 0; w < kCW; ++w) {
+                const float4* p =
+                    reinterpret_cast<const float4*>(red + ((rs * kCW + w) * 32 + lane) * 8);
+                const float4 a = p[0], b = p[1];
+                sg[0] += a.x, sg[1] += a.y, sg[2] += a.z, sg[3] += a.w;
+                su[0] += b.x, su[1] += b.y, su[2] += b.z, su[3] += b.w;
+            }
+            const int* m = meta + rs * 8;
+            const int e0 = m[0], nt = m[1], rt = m[2], gid = m[3];
+            const float gglob = __int_as_float(m[4]), uglob = __int_as_float(m[5]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&red_empty[rs]);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int row = (lane >> 2) + ((v >> 1) << 3);
+                const int n = 2 * (lane & 3) + (v & 1);
+                if (n < nt)
+                    h16[(int64_t)(e0 + n) * I + rt * 16 + row] =
+                        __float2half_rn(silu(sg[v] * gglob) * (su[v] * uglob));
+            }
+            __syncwarp();
+            if (lane == 0) red_release_gpu_add(done + gid, 1);
+        }
         return;
     }
+
+    // ---------------- MMA warps
     const int g = lane >> 2, q = lane & 3;
-    float* ypart = P.ypart_smem ? yps : wsp<float>(P, P.L.ypart);
-    const int ypstride = P.ypart_smem ? 16 : H;  // floats between entries
-    const int ypcol = P.ypart_smem ? 0 : rb * 16;
-    const int* ent_of = wsp<int>(P, P.L.ent_of);
-    for (int grp = warp; grp < n_groups; grp += kConsumerWarps) {
-        const int st = grp % NST;
-        const uint32_t ph = (grp / NST) & 1;
-        if (!mbar_wait_bounded(&full[st], ph)) {
+    bool ok = true;
+    {
+        if (FL.x_res && n_gu > (int)blockIdx.x && !mbar_wait_bounded(x_full, 0)) {
             report_timeout(P);
-            break;
+            ok = false;
         }
-        const uint8_t* stg = smem + (size_t)st * stage_bytes;
-        const int* hdr = reinterpret_cast<const int*>(stg);
-        const int e0 = hdr[GD_E0], nt = hdr[GD_NT];
-        // the stage is released before the epilogue: keep its scalars in registers
-        const float* ext_s = reinterpret_cast<const float*>(hdr + kDescInts);
-        const float dglob = ext_s[0];
-        const float w_lo = ext_s[2 + 2 * q], w_hi = ext_s[3 + 2 * q];  // tokens 2q, 2q+1
-        const __half* hs = reinterpret_cast<const __half*>(stg + off_h) + g * I;
-        const bool has_tok = g < nt;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k0 = 0; k0 < I; k0 += Fmt::kWarpTileK) {
-            typename Fmt::Row ra, rbw;
-            Fmt::load_smem(ra, stg + off_codes + g * cb, stg + off_sc + g * sb, k0, q);
-            Fmt::load_smem(rbw, stg + off_codes + (g + 8) * cb, stg + off_sc + (g + 8) * sb, k0, q);
+        int it = 0;
+        for (int item = blockIdx.x; item < n_gu; item += G, ++it) {
+            const int st = it % NGU;
+            if (ok && !mbar_wait_bounded(&gu_full[st], (it / NGU) & 1)) {
+                report_timeout(P);
+                ok = false;
+            }
+            float accg[kAcc][4] = {}, accu[kAcc][4] = {};
+            int mv[6] = {0, 0, 0, 0, 0, 0};
+            if (ok) {
+                const uint8_t* stg = smem + (size_t)st * FL.stage_gu;
+                const int* hdr = reinterpret_cast<const int*>(stg);
+                mv[0] = hdr[GD_E0], mv[1] = hdr[GD_NT], mv[2] = hdr[GD_RT], mv[3] = hdr[GD_GID];
+                mv[4] = hdr[GD_GGLOB], mv[5] = hdr[GD_UGLOB];
+                const bool has_tok = g < mv[1];
+                // B rows: the resident row of the lane's token, or the staged row g
+                const uint8_t* xb = FL.x_res ? smem + FL.off_x + (has_tok ? hdr[GD_TOK + g] : 0) * xrow
+                                             : stg + og_x + g * xrow;
+                const __half* xs = reinterpret_cast<const __half*>(xb);
+                if constexpr (TPW > 0) {
 #pragma unroll
-            for (int s2 = 0; s2 < Fmt::kSteps; s2 += 2) {
-                const uint4 hb = has_tok
-                                     ? *reinterpret_cast<const uint4*>(hs + k0 + Fmt::kofs(q, s2))
-                                     : make_uint4(0, 0, 0, 0);
-#pragma unroll
-                for (int ss = 0; ss < 2; ++ss) {
-                    uint32_t af[4];
-                    Fmt::deq(ra, s2 + ss, af[0], af[2]);
-                    Fmt::deq(rbw, s2 + ss, af[1], af[3]);
-                    mma_f16_16816(acc, af, ss ? hb.z : hb.x, ss ? hb.w : hb.y);
+                    for (int t = 0; t < TPW; ++t)
+                        gate_up_tile<Fmt>(stg + kStageHdr, stg + og_uc, stg + og_gs, stg + og_us,
+                                          cbg, sbg, xs, has_tok, (warp * TPW + t) * Fmt::kWarpTileK,
+                                          g, q, accg, accu);
+                } else {
+                    const int kw = H / kCW;
+                    for (int k0 = warp * kw; k0 < (warp + 1) * kw; k0 += Fmt::kWarpTileK)
+                        gate_up_tile<Fmt>(stg + kStageHdr, stg + og_uc, stg + og_gs, stg + og_us,
+                                          cbg, sbg, xs, has_tok, k0, g, q, accg, accu);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&gu_empty[st]);
+            fold_acc(accg);
+            fold_acc(accu);
+            const int rs = it & 1;
+            if (ok && !mbar_wait_bounded(&red_empty[rs], ((it >> 1) & 1) ^ 1)) {
+                report_timeout(P);
+                ok = false;
+            }
+            float4* rw = reinterpret_cast<float4*>(red + ((rs * kCW + warp) * 32 + lane) * 8);
+            rw[0] = make_float4(accg[0][0], accg[0][1], accg[0][2], accg[0][3]);
+            rw[1] = make_float4(accu[0][0], accu[0][1], accu[0][2], accu[0][3]);
+            if (warp == 0 && lane < 6) {
+                // lane i stores field i (selects, not an indexed register array)
+                int v = mv[0];
+                v = lane == 1 ? mv[1] : v;
+                v = lane == 2 ? mv[2] : v;
+                v = lane == 3 ? mv[3] : v;
+                v = lane == 4 ? mv[4] : v;
+                v = lane == 5 ? mv[5] : v;
+                meta[rs * 8 + lane] = v;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&red_full[rs]);
         }
+        // this warp reads no gate_up stage any more: the ring may hold down stages
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-        // C fragment: rows g, g+8; tokens 2q, 2q+1 of the group
+        if (lane == 0) mbar_arrive(gu_drained);
+    }
+
+    // ---- down: warp w owns the ring uses j = w, w + 8, ... (one use = one group of a row tile)
+    float* ypart = P.ypart_smem ? reinterpret_cast<float*>(smem + FL.off_yp)
+                                : wsp<float>(P, P.L.ypart);
+    const int ypstride = P.ypart_smem ? 16 : H;  // floats between entries
+    const float* sgate = (P.has_shared && P.shared_gate) ? wsp<float>(P, P.L.sg) : nullptr;
+    const int* ent_of = wsp<int>(P, P.L.ent_of);
+    const int K1 = P.top_k + 1;
+    int j = 0;
+    for (int rt = G - 1 - (int)blockIdx.x; rt < n_dn; rt += G) {
+        const int ypcol = P.ypart_smem ? 0 : rt * 16;
+        for (int grp = 0; grp < n_groups; ++grp, ++j) {
+            // use j of the down ring goes to warp j % 8 and the ring has a multiple of 8 stages,
+            // so each stage is always consumed by the same warp, in order: a warp is never a
+            // whole phase ahead of a stage's barrier (parity would alias)
+            if (j % kCW != warp) continue;
+            const int st = j % NDT;
+            if (ok && !mbar_wait_bounded(&dn_full[st], (j / NDT) & 1)) {
+                report_timeout(P);
+                ok = false;
+            }
+            if (ok && !wait_group_h(done + grp, tiles_i)) {
+                report_timeout(P);
+                ok = false;
+            }
+            __syncwarp();
+            float acc[kAcc][4] = {};
+            int e0 = 0, nt = 0;
+            float dglob = 0.f, w_lo = 0.f, w_hi = 0.f, s_lo = 1.f, s_hi = 1.f;
+            if (ok) {
+                const uint8_t* stg = dn_stage(st);
+                const int* hdr = reinterpret_cast<const int*>(stg);
+                e0 = hdr[GD_E0], nt = hdr[GD_NT];
+                dglob = __int_as_float(hdr[GD_DGLOB]);
+                w_lo = __int_as_float(hdr[GD_W + 2 * q]);
+                w_hi = __int_as_float(hdr[GD_W + 2 * q + 1]);
+                if (hdr[GD_POOL] && sgate) {
+                    s_lo = 2 * q < nt ? __ldcg(sgate + hdr[GD_TOK + 2 * q]) : 0.f;
+                    s_hi = 2 * q + 1 < nt ? __ldcg(sgate + hdr[GD_TOK + 2 * q + 1]) : 0.f;
+                }
+                const __half* hrow = g < nt ? h16 + (int64_t)(e0 + g) * I : nullptr;
+                if constexpr (TD > 0) {
+                    uint4 hb[TD][4];
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-            const int row = g + ((v >> 1) << 3);
-            const int n = 2 * q + (v & 1);
-            if (n < nt) {
-                const int e = e0 + n;
-                ypart[(int64_t)e * ypstride + ypcol + row] = acc[v] * dglob * ((v & 1) ? w_hi : w_lo);
+                    for (int t = 0; t < TD; ++t) load_h_tile(hrow, t * Fmt::kWarpTileK, q, hb[t]);
+#pragma unroll
+                    for (int t = 0; t < TD; ++t)
+                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, hb[t],
+                                       t * Fmt::kWarpTileK, g, q, acc);
+                } else {
+                    for (int k0 = 0; k0 < I; k0 += Fmt::kWarpTileK) {
+                        uint4 hb[4];
+                        load_h_tile(hrow, k0, q, hb);
+                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, hb, k0, g, q, acc);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dn_empty[st]);
+            fold_acc(acc);
+            // C fragment: rows g, g+8; entries 2q, 2q+1 of the group
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int row = g + ((v >> 1) << 3);
+                const int n = 2 * q + (v & 1);
+                if (n < nt)
+                    ypart[(int64_t)(e0 + n) * ypstride + ypcol + row] =
+                        acc[0][v] * dglob * ((v & 1) ? w_hi * s_hi : w_lo * s_lo);
             }
         }
-    }
-    named_bar_sync(1, kConsumers);
-    // y rows of this CTA: entries of each token summed in the order j = 0..k-1, shared
-    const int K1 = P.top_k + 1;
-    for (int idx = tid; idx < P.n_tok * 16; idx += kConsumers) {
-        const int t = idx >> 4, r = idx & 15;
-        float sum = 0.f;
-        for (int j = 0; j < K1; ++j) {
-            const int e = ent_of[t * K1 + j];
-            if (e >= 0) sum += ypart[(int64_t)e * ypstride + ypcol + r];
+        named_bar_sync(1, kConsumers);
+        // y rows of this tile: the entries of each token summed in the order j = 0..k-1, shared
+        // (no groups: an upstream error or no valid entry, y = 0 without reading the entry map)
+        for (int idx = tid; idx < P.n_tok * 16; idx += kConsumers) {
+            const int t = idx >> 4, r = idx & 15;
+            float sum = 0.f;
+            for (int jj = 0; jj < (n_groups > 0 ? K1 : 0); ++jj) {
+                const int e = ent_of[t * K1 + jj];
+                if (e >= 0) sum += ypart[(int64_t)e * ypstride + ypcol + r];
+            }
+            P.y[(int64_t)t * P.y_stride + rt * 16 + r] = f32_to_bf16_bits(sum);
         }
-        P.y[(int64_t)t * P.y_stride + rb * 16 + r] = f32_to_bf16_bits(sum);
+        named_bar_sync(1, kConsumers);  // y_part is reused by the next row tile
     }
 }
 
@@ -472,35 +606,65 @@ bool pool_aligned(const nvmoe_expert_pool& p) {
     return bank_aligned(p.gate, nv) && bank_aligned(p.up, nv) && bank_aligned(p.down, nv);
 }
 
+
+template <typename Fmt, int TPW>
+auto pick_fused(int td) {
+    // the down phase keeps all of a group's h fragments in registers for up to 4 K tiles
+    return (td == 2) ? ffn_fused<Fmt, TPW, 2>
+         : (td == 4) ? ffn_fused<Fmt, TPW, 4>
+                     : ffn_fused<Fmt, TPW, 0>;
+}
+
 template <typename Fmt>
 int launch_fmt(FfnParams& P, cudaStream_t st) {
     const int H = P.pool.hidden, I = P.pool.inter;
-    const int red_gu = kConsumerWarps * 32 * 8 * 4;
-    const int sgu = kStageHdr + 32 * Fmt::code_bytes(H) + 32 * Fmt::scale_bytes(H) +
-                    kGroupMaxTok * H * 2;
-    const int nst_gu = std::min(4, (kSmemCap - red_gu - 1024) / sgu);
-    const int sdn = kStageHdr + 16 * (Fmt::code_bytes(I) + Fmt::scale_bytes(I)) +
-                    kGroupMaxTok * I * 2;
-    const size_t yp_bytes = (size_t)P.L.n_ent_max * 16 * 4;
-    P.ypart_smem = (yp_bytes + 4 * (size_t)sdn + 1024 <= (size_t)kSmemCap) ? 1 : 0;
-    const size_t yp_used = P.ypart_smem ? yp_bytes : 0;
-    const int nst_dn = (int)std::min<size_t>(16, (kSmemCap - yp_used - 1024) / sdn);
-    if (nst_gu < 1 || nst_dn < 2) return NVMOE_ERR_UNSUPPORTED;
-    P.nst_gu = nst_gu;
-    P.stage_gu = sgu;
-    P.nst_dn = nst_dn;
-    P.stage_dn = sdn;
-    const size_t smem_gu = (size_t)nst_gu * sgu + 16 * nst_gu + red_gu;
-    const size_t smem_dn = (size_t)nst_dn * sdn + 16 * nst_dn + yp_used;
-    NVMOE_CUDA_TRY(cudaFuncSetAttribute(ffn_gate_up_tma<Fmt>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_gu));
-    NVMOE_CUDA_TRY(cudaFuncSetAttribute(ffn_down_tma<Fmt>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dn));
-    cudaError_t e =
-        launch_pdl(ffn_gate_up_tma<Fmt>, dim3(kNumSMs), dim3(kTmaThreads), smem_gu, st, true, P);
-    if (e != cudaSuccess) return cuda_status("ffn_gate_up launch", e);
-    e = launch_pdl(ffn_down_tma<Fmt>, dim3(H / 16), dim3(kTmaThreads), smem_dn, st, true, P);
-    return cuda_status("ffn_down launch", e);
+    int dev = 0, sms = 0;
+    NVMOE_CUDA_TRY(cudaGetDevice(&dev));
+    NVMOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    FusedLayout FL{};
+    // all token rows resident in shared memory for decode-sized batches, staged per item above
+    FL.x_res = P.n_tok <= kGroupMaxTok ? 1 : 0;
+    FL.xt = FL.x_res ? 0 : P.grp_tok;
+    const int xrow = H * 2 + kXPad;
+    FL.stage_gu = round128(kStageHdr + 32 * Fmt::code_bytes(H) + 32 * Fmt::scale_bytes(H) +
+                           FL.xt * xrow);
+    FL.stage_dn = round128(kStageHdr + 16 * (Fmt::code_bytes(I) + Fmt::scale_bytes(I)));
+    const int x_bytes = FL.x_res ? round128(std::max(1, P.n_tok) * xrow) : 0;
+    const int red_bytes = 2 * kCW * 32 * 8 * 4, meta_bytes = 2 * 8 * 4;
+    const int bar_bytes = 8 * (2 * 4 + 2 * 64 + 6) + 64;
+    const int yp_bytes = round128(P.L.n_ent_max * 16 * 4);
+    const int fixed = red_bytes + meta_bytes + bar_bytes + x_bytes;
+    // y_part in shared memory when it leaves room for 2 gate_up and 8 down stages
+    P.ypart_smem = (fixed + yp_bytes + 2 * FL.stage_gu + kCW * FL.stage_dn <= kSmemCap) ? 1 : 0;
+    const int avail = kSmemCap - fixed - (P.ypart_smem ? yp_bytes : 0);
+    // down stage counts are multiples of the 8 MMA warps (see the down phase)
+    FL.nst_gu = std::min(4, (avail - kCW * FL.stage_dn) / FL.stage_gu);
+    if (FL.nst_gu < 2) return NVMOE_ERR_UNSUPPORTED;
+    FL.nst_dn = std::min(32, (avail - FL.nst_gu * FL.stage_gu) / FL.stage_dn) / kCW * kCW;
+    if (FL.nst_dn < kCW) return NVMOE_ERR_UNSUPPORTED;
+    FL.nst_dn_ext = std::min(32, FL.nst_gu * FL.stage_gu / FL.stage_dn) / kCW * kCW;
+    FL.off_x = FL.nst_gu * FL.stage_gu;
+    FL.off_dn = FL.off_x + x_bytes;
+    FL.off_red = FL.off_dn + FL.nst_dn * FL.stage_dn;
+    FL.off_meta = FL.off_red + red_bytes;
+    FL.off_yp = FL.off_meta + meta_bytes;
+    FL.off_bar = FL.off_yp + (P.ypart_smem ? yp_bytes : 0);
+    FL.total = FL.off_bar + 8 * (2 * FL.nst_gu + 2 * (FL.nst_dn + FL.nst_dn_ext) + 6);
+    // compile-time K tiles per MMA warp (gate_up) and per down slab where the shape has an
+    // instantiation; other shapes take runtime tile loops
+    const int tpw = H / (kCW * Fmt::kWarpTileK), td = I / Fmt::kWarpTileK;
+    auto kern = (tpw == 1) ? pick_fused<Fmt, 1>(td)
+              : (tpw == 2) ? pick_fused<Fmt, 2>(td)
+              : (tpw == 4) ? pick_fused<Fmt, 4>(td)
+                           : pick_fused<Fmt, 0>(td);
+    NVMOE_CUDA_TRY(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FL.total));
+    // at most one CTA per SM and no more CTAs than SMs: every CTA is resident, so the down
+    // phase's waits on other CTAs' gate_up rows always end
+    const int grid = sms;
+    const cudaError_t e =
+        launch_pdl(kern, dim3(grid), dim3(kFusedThreads), (size_t)FL.total, st, true, P, FL);
+    return cuda_status("ffn_fused launch", e);
 }
 
 }  // namespace
@@ -552,6 +716,9 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
     P.ws = static_cast<unsigned char*>(args->workspace);
     P.L = L;
     P.status = args->status;
+    // groups never exceed the token count, so a group's x rows fit the stage even when the
+    // caller's slot ids repeat a slot within a token
+    P.grp_tok = std::max(1, std::min(kGroupMaxTok, args->n_tok));
     return NVMOE_OK;
 }
 

@@ -53,6 +53,34 @@ def test_router_random_shapes(cuda_device, E, k, n):
     np.testing.assert_allclose(w2.cpu().numpy(), rw2, rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("E,k", [(513, 32), (700, 10), (1000, 8), (1024, 16), (300, 10)])
+def test_router_edge_rows(cuda_device, E, k):
+    """Ties inside and across the two 512-expert halves of long rows, +0/-0 ties, NaN and -inf
+    logits, a short second half (E = 513); both router modes."""
+    rng = np.random.default_rng(E * 7 + k)
+    lg = rng.standard_normal((6, E)).astype(np.float32)
+    top = [5, E - 1, min(511, E - 1), min(512, E - 1), E // 2, 3]
+    lg[0, top] = 9.0                                     # six-way tie, ids across both halves
+    lg[1, :] = 0.0
+    lg[1, ::3] = -0.0                                    # +0 / -0 compare equal -> lower id
+    lg[2, ::5] = np.nan                                  # NaN never wins
+    lg[3, 1::2] = -np.inf
+    lg[4, :] = np.float32(1.25)                          # every key equal
+    lg[4, E - 1] = 1.5
+    t = torch.from_numpy(lg).to(cuda_device)
+    ids, w = ops.router_topk(t, k)
+    rids, rw = R.router_topk_softmax(lg, k)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rids)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    b = (rng.standard_normal(E) * 0.1).astype(np.float32)
+    b[top] = 0.0
+    ids2, w2 = ops.router_topk(t, k, mode="sigmoid_bias", bias=torch.from_numpy(b).to(cuda_device),
+                               norm_topk=True, routed_scaling=2.5)
+    rids2, rw2, _ = R.router_topk_sigmoid_bias(lg, k, b, True, 2.5)
+    np.testing.assert_array_equal(ids2.cpu().numpy(), rids2)
+    np.testing.assert_allclose(w2.cpu().numpy(), rw2, rtol=2e-6, atol=1e-7)
+
+
 # ------------------------------------------------------------------ R2/R3/R6 remap
 def _run_trace(dev, name, gold):
     E, k, S, pinned, n_tok, steps = gold[f"{name}_meta"].tolist()
