@@ -270,7 +270,7 @@ def run_nvmoe(a, rank, world, local_rank):
                 "h2d_bytes_per_step": B * H * 2 + L * B * E * 4,
                 "d2h_bytes_per_step": L * B * H * 2},
         "gpu_launches": a.steps * L * 4,
-        "roofline": {"bound": "hbm", "kernel": "expert FFN (prep + gate_up + down, one layer)",
+        "roofline": {"bound": "hbm", "kernel": "expert FFN (prep + ffn_fused, one layer)",
                      "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else
@@ -288,7 +288,7 @@ def run_nvmoe(a, rank, world, local_rank):
 
 
 def _traffic_from_profiles():
-    p = ROOT / "profiles" / "ffn_decode_nvfp4_traffic.md"
+    p = ROOT / "profiles" / "ffn_fused_nvfp4_decode_b8.md"
     if not p.exists():
         return None
     for ln in p.read_text().splitlines():
