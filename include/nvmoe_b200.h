@@ -197,6 +197,16 @@ int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
  * to start at zero), so calls that overlap on the GPU race: serialise them.  Allocates nothing. */
 int nvmoe_moe_ffn_noalloc(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
 
+/* R10 — the same FFN for large batches (prefill, ~1k tokens and up): entries sorted by slot into
+ * tiles of 128, each expert's gate/up and down as tcgen05 MMAs with the weights dequantised into
+ * tensor memory (NVFP4 pools).  Replaces the narrowed-union prefill's _expert_gemm call
+ * (nvme_offload_cache.py:1957-2013) and mul_mat_id for n_tokens > 1 (moe_cache_probe.cpp:1668-1684).
+ * Same arguments and result as nvmoe_moe_ffn; workspace >= nvmoe_moe_ffn_prefill_workspace_size
+ * (it holds the sorted activations, h and the per-entry outputs: about n_tok*(k+1)*(6H+2I) bytes). */
+size_t nvmoe_moe_ffn_prefill_workspace_size(int n_tok, int top_k, int hidden, int inter,
+                                            int n_slots);
+int nvmoe_moe_ffn_prefill(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
+
 /* ================================================================ R4: host tier (SLRU)
  * Segmented LRU of the pinned host tier (nvme_offload_cache.py:333-409;
  * scripts/segmented_host_lru.hpp:85-160): probation queue for first references, protected

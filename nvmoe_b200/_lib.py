@@ -175,6 +175,9 @@ SIGNATURES = {
     "nvmoe_moe_ffn_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     "nvmoe_moe_ffn": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
     "nvmoe_moe_ffn_noalloc": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
+    "nvmoe_moe_ffn_prefill_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int,
+                                                          C.c_int]),
+    "nvmoe_moe_ffn_prefill": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
     "nvmoe_slru_create": (C.c_void_p, [C.c_double]),
     "nvmoe_slru_destroy": (None, [C.c_void_p]),
     "nvmoe_slru_set_capacity_hint": (None, [C.c_void_p, C.c_int64]),

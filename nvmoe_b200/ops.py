@@ -264,6 +264,37 @@ def moe_ffn(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor, weight
     return out
 
 
+def moe_ffn_prefill(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor,
+                    weights: torch.Tensor, shared: ExpertWeights | None = None,
+                    shared_gate: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                    workspace: FfnWorkspace | None = None,
+                    status: torch.Tensor | None = None) -> torch.Tensor:
+    """The routed-expert FFN for large batches (token-sorted tcgen05 grouped GEMM); same result
+    as moe_ffn.  See nvmoe_moe_ffn_prefill."""
+    _require_cuda(x, slot_ids, weights)
+    assert x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+    assert slot_ids.dtype == torch.int32 and weights.dtype == torch.float32
+    n, H = x.shape
+    k = slot_ids.shape[1]
+    if out is None:
+        out = torch.empty((n, H), dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        dev = x.device.index or 0
+        workspace = _default_ws.setdefault(dev, FfnWorkspace(x.device))
+    nbytes = int(lib().nvmoe_moe_ffn_prefill_workspace_size(n, k, pool.hidden, pool.inter,
+                                                            pool.n_slots))
+    ws = workspace.get(nbytes)
+    ps = expert_pool_struct(pool)
+    ss = expert_pool_struct(shared) if shared is not None else None
+    args = _lib.FfnArgs(
+        C.pointer(ps), C.pointer(ss) if ss is not None else None,
+        _ptr(shared_gate), x.data_ptr(), x.stride(0), slot_ids.data_ptr(), slot_ids.stride(0),
+        weights.data_ptr(), weights.stride(0), k, n, out.data_ptr(), out.stride(0),
+        ws.data_ptr(), ws.numel(), _ptr(status))
+    check(lib().nvmoe_moe_ffn_prefill(C.byref(args), _stream()), "nvmoe_moe_ffn_prefill")
+    return out
+
+
 # ------------------------------------------------------------------ R5 refill
 def refill_banks(gpu: ExpertWeights, host: ExpertWeights) -> list[_lib.RefillBank]:
     """One RefillBank per FTW bank (codes, scales, global) of gate_up and down."""
