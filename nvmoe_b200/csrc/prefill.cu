@@ -13,7 +13,7 @@
 //   scan    — entry base per key, tiles of <= 128 entries per key
 //   scatter — entries sorted by key; inverse map ent_of[t * (k + 1) + j]
 //   gather  — the sorted activation matrix xs[e] = f16(x[tok(e)]) and the shared gate
-//   gate_up — one CTA per (tile, 128 rows of I): D_g = W_g xs^T and D_u = W_u xs^T with the
+//   gate_up — one CTA per (tile half, 128 rows of I): D_g = W_g xs^T and D_u = W_u xs^T with the
 //             weights dequantised by the CTA's warps straight into tensor memory (A operand),
 //             xs from shared memory (B operand), fp32 accumulators in tensor memory;
 //             h = silu(g * global_g) * (u * global_u) (f16)
@@ -247,52 +247,77 @@ __device__ __forceinline__ RowSrc row_src(const nvmoe_matrix_bank& b, int slot, 
     return r;
 }
 
-__device__ __forceinline__ void load_chunk(const RowSrc& r, int chunk, int k_off, int k_len,
-                                           uint4 (&c)[2], uint32_t& sc4) {
-    // k_len = 64: 32 bytes of codes, 4 scale bytes; k_len = 32: the half starting at k_off
-    const uint8_t* cp = r.codes + (chunk * kChunk + k_off) / 2;
-    c[0] = __ldg(reinterpret_cast<const uint4*>(cp));
-    c[1] = k_len == 64 ? __ldg(reinterpret_cast<const uint4*>(cp + 16)) : make_uint4(0, 0, 0, 0);
-    const uint8_t* sp = r.scales + (chunk * kChunk + k_off) / 16;
-    sc4 = k_len == 64 ? __ldg(reinterpret_cast<const uint32_t*>(sp))
-                      : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(sp));
+// Ampere-style asynchronous copies (per thread, into shared memory).
+__device__ __forceinline__ void cp16(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// B chunk: rows [eb, eb + nr) of a row-major f16 matrix (row length ld) -> canonical layout of
-// 128 rows x 64 K in shared memory (rows past nr are zero).  Thread i moves pieces i + 256 u.
-struct BPieces {
-    uint4 v[4];
-};
-__device__ __forceinline__ void load_b(const __half* m, int64_t ld, int eb, int nr, int chunk,
-                                       BPieces& b) {
+// Pipeline: kStages shared-memory stages, loads issued kStages - 2 chunks ahead; a stage and the
+// TMEM A buffer of chunk c are reused by chunk c + 2 once chunk c's MMAs have completed.
+// Four stages keep two CTAs per SM, so one CTA's prologue and epilogue overlap the other's MMAs.
+constexpr int kStages = 4;
+
+// B chunk c: rows [eb, eb + nr) of a row-major f16 matrix (row length ld) into the canonical
+// layout of an NB-row tile; rows >= nr are zero.
+template <int NB>
+__device__ __forceinline__ void issue_b(uint8_t* dst, const __half* m, int64_t ld, int eb, int nr,
+                                        int c) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < NB * 8 / kPfThreads; ++u) {
         const int p = threadIdx.x + kPfThreads * u;
         const int n = p >> 3, kp = p & 7;
-        b.v[u] = n < nr ? __ldg(reinterpret_cast<const uint4*>(m + (int64_t)(eb + n) * ld +
-                                                                chunk * kChunk + kp * 8))
-                        : make_uint4(0, 0, 0, 0);
+        const bool v = n < nr;
+        cp16(dst + umma::canon_off(n, kp * 8, NB),
+             m + (int64_t)(eb + (v ? n : 0)) * ld + c * kChunk + kp * 8, v ? 16 : 0);
     }
 }
-__device__ __forceinline__ void store_b(uint8_t* stage, const BPieces& b) {
+
+// The tail of a chunk: make this thread's TMEM stores and async copies visible to the MMA, then
+// one thread issues the chunk's K-steps (A columns a_col[j] + 8 ks for each accumulator j).
+template <int NB, int NACC>
+__device__ __forceinline__ void chunk_mma(uint8_t* bstage, const uint32_t (&d)[NACC],
+                                          const uint32_t (&a_col)[NACC], int c, uint64_t* done) {
+    umma::wait_st();
+    umma::fence_smem_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    if (threadIdx.x == 0) {
+        constexpr uint32_t idesc = umma::idesc_f16(kTileM, NB);
+        const uint32_t b0 = smem_u32(bstage);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int p = threadIdx.x + kPfThreads * u;
-        const int n = p >> 3, kp = p & 7;
-        *reinterpret_cast<uint4*>(stage + umma::canon_off(n, kp * 8, kTileN)) = b.v[u];
+        for (int ks = 0; ks < kChunk / 16; ++ks) {
+            const uint64_t bd = umma::smem_desc(b0 + ks * 2 * (NB / 8) * 128, (NB / 8) * 128, 128);
+#pragma unroll
+            for (int j = 0; j < NACC; ++j)
+                umma::mma_ts(d[j], a_col[j] + 8 * ks, bd, idesc, (c > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma::commit(done);
     }
 }
 
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity) {
-    return mbar_wait_bounded(bar, parity);
-}
+// gate_up.  One CTA per (tile, 128 rows of I, half of the tile's entries): N = 64 keeps the
+// CTA's tensor memory at 256 columns (two CTAs per SM).  Per stage: codes [256 rows][32 B]
+// (rows 0-127 gate, 128-255 up; row = thread), scales [256][4 B], B [64 x 64 f16].  TMEM: D_g
+// [0,64), D_u [64,128), A buffer b: gate [128 + 64 b, +32), up [160 + 64 b, +32).  Warps 0-3
+// dequantise gate rows, warps 4-7 up rows.
+constexpr int kGuN = 64;
+constexpr int kGuCodes = 2 * kTileM * 32, kGuScales = 2 * kTileM * 4;
+constexpr int kGuStage = kGuCodes + kGuScales + kGuN * kChunk * 2;
 
-constexpr int kBStage = kTileN * kChunk * 2;  // 16 KB
-
-// gate_up: TMEM columns: D_g [0,128) D_u [128,256) A stages: stage s gate [256+64s, +32),
-// up [288+64s, +32).  Warps 0-3 dequantise gate rows, warps 4-7 up rows (lane quadrant w % 4).
 __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up(PfParams P) {
-    __shared__ __align__(1024) uint8_t bst[2 * kBStage];
+    extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t mma_done[2];
     __shared__ uint32_t tmem_base;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -300,7 +325,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up(PfParams P) {
     const int tile = blockIdx.x, mt = blockIdx.y;
     if (tile >= hdr[PH_N_TILES]) return;
     const int* tl = pws<int>(P, P.L.tiles) + 3 * tile;
-    const int key = tl[0], eb = tl[1], nr = tl[2];
+    const int key = tl[0];
+    const int eb = tl[1] + kGuN * blockIdx.z, nr = min(kGuN, tl[2] - kGuN * (int)blockIdx.z);
+    if (nr <= 0) return;
     const int H = P.pool.hidden, I = P.pool.inter, S = P.pool.n_slots;
     const bool sh = key == S;
     const nvmoe_expert_pool& pool = sh ? P.shared : P.pool;
@@ -309,113 +336,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gate_up(PfParams P) {
     const bool is_up = warp >= 4;
     const RowSrc src = row_src(is_up ? pool.up : pool.gate, slot, (int64_t)mt * kTileM + row);
     const __half* xs = pws<__half>(P, P.L.xs);
-
-    if (tid == 0) {
-        mbar_init(&mma_done[0], 1);
-        mbar_init(&mma_done[1], 1);
-        mbar_init_fence();
-    }
-    if (warp == 0) umma::tmem_alloc(&tmem_base, 512);
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
-    const uint32_t tm = tmem_base;
-    const uint32_t d_g = tm, d_u = tm + 128;
-    constexpr uint32_t idesc = umma::idesc_f16(kTileM, kTileN);
-
-    const int n_chunks = H / kChunk;
-    uint4 c[2];
-    uint32_t sc4;
-    BPieces bp;
-    load_chunk(src, 0, 0, 64, c, sc4);
-    load_b(xs, H, eb, nr, 0, bp);
-    bool ok = true;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-        const int s = ch & 1;
-        if (ch >= 2 && ok && !wait_bar(&mma_done[s], ((ch - 2) >> 1) & 1)) ok = false;
-        umma::fence_after_sync();
-        uint32_t a[32];
-        deq_row64(c, sc4, a);
-        const uint32_t acol = 256 + 64 * s + (is_up ? 32 : 0);
-        uint32_t lo[16], hi[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) lo[i] = a[i], hi[i] = a[16 + i];
-        umma::st_x16(umma::lane_addr(tm, warp, acol), lo);
-        umma::st_x16(umma::lane_addr(tm, warp, acol + 16), hi);
-        store_b(bst + s * kBStage, bp);
-        if (ch + 1 < n_chunks) {  // next chunk's loads in flight during this chunk's MMAs
-            load_chunk(src, ch + 1, 0, 64, c, sc4);
-            load_b(xs, H, eb, nr, ch + 1, bp);
-        }
-        umma::wait_st();
-        umma::fence_smem_async();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
-        if (tid == 0) {
-            const uint32_t b0 = smem_u32(bst + s * kBStage);
-#pragma unroll
-            for (int ks = 0; ks < kChunk / 16; ++ks) {
-                const uint64_t bd = umma::smem_desc(b0 + ks * 2 * (kTileN / 8) * 128,
-                                                    (kTileN / 8) * 128, 128);
-                const uint32_t acc = (ch > 0 || ks > 0) ? 1u : 0u;
-                umma::mma_ts(d_g, tm + 256 + 64 * s + 8 * ks, bd, idesc, acc);
-                umma::mma_ts(d_u, tm + 288 + 64 * s + 8 * ks, bd, idesc, acc);
-            }
-            umma::commit(&mma_done[s]);
-        }
-    }
-    // the last commit covers every MMA of the tile
-    const int last = n_chunks - 1;
-    if (ok && !wait_bar(&mma_done[last & 1], (last >> 1) & 1)) ok = false;
-    umma::fence_after_sync();
-    if (!ok) {
-        if (lane == 0) atomicExch(pws<int>(P, P.L.hdr) + PH_STATUS, NVMOE_ERR_TIMEOUT);
-    } else {
-        // epilogue: warps 0-3 entries [0, 64), warps 4-7 entries [64, 128) of the rows they own
-        const float gg = global_of(pool.gate, slot), ug = global_of(pool.up, slot);
-        __half* h = pws<__half>(P, P.L.h);
-        const int c0 = is_up ? 64 : 0;
-#pragma unroll 1
-        for (int cc = c0; cc < c0 + 64; cc += 16) {
-            uint32_t g[16], u[16];
-            umma::ld_x16(umma::lane_addr(d_g, warp, cc), g);
-            umma::ld_x16(umma::lane_addr(d_u, warp, cc), u);
-            umma::wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int n = cc + i;
-                if (n < nr)
-                    h[(int64_t)(eb + n) * I + mt * kTileM + row] = __float2half_rn(
-                        silu(__uint_as_float(g[i]) * gg) * (__uint_as_float(u[i]) * ug));
-            }
-        }
-    }
-    umma::fence_before_sync();
-    __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tm, 512);
-}
-
-// down: TMEM columns: D [0,128), A stages [128 + 64 s, +32).  Every warp dequantises rows of
-// its lane quadrant: warps 0-3 the first 32 K of a chunk, warps 4-7 the second 32.
-__global__ void __launch_bounds__(kPfThreads, 1) pf_down(PfParams P) {
-    __shared__ __align__(1024) uint8_t bst[2 * kBStage];
-    __shared__ __align__(8) uint64_t mma_done[2];
-    __shared__ uint32_t tmem_base;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int* hdr = pws<int>(P, P.L.hdr);
-    const int tile = blockIdx.x, mt = blockIdx.y;
-    if (tile >= hdr[PH_N_TILES]) return;
-    const int* tl = pws<int>(P, P.L.tiles) + 3 * tile;
-    const int key = tl[0], eb = tl[1], nr = tl[2];
-    const int H = P.pool.hidden, I = P.pool.inter, S = P.pool.n_slots;
-    const bool sh = key == S;
-    const nvmoe_expert_pool& pool = sh ? P.shared : P.pool;
-    const int slot = sh ? 0 : key;
-    const int row = (warp & 3) * 32 + lane;
-    const int khalf = warp >= 4 ? 32 : 0;
-    const RowSrc src = row_src(pool.down, slot, (int64_t)mt * kTileM + row);
-    const __half* hm = pws<__half>(P, P.L.h);
+    auto stage = [&](int c) { return smem + (size_t)(c % kStages) * kGuStage; };
+    auto issue = [&](int c) {
+        uint8_t* st = stage(c);
+        cp16(st + tid * 32, src.codes + c * 32, 16);
+        cp16(st + tid * 32 + 16, src.codes + c * 32 + 16, 16);
+        cp4(st + kGuCodes + tid * 4, src.scales + c * 4);
+        issue_b<kGuN>(st + kGuCodes + kGuScales, xs, H, eb, nr, c);
+    };
 
     if (tid == 0) {
         mbar_init(&mma_done[0], 1);
@@ -427,49 +355,143 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down(PfParams P) {
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tm = tmem_base;
-    constexpr uint32_t idesc = umma::idesc_f16(kTileM, kTileN);
+    const uint32_t dd[2] = {tm, tm + kGuN};
+
+    const int n_chunks = H / kChunk;
+    for (int c = 0; c < kStages - 2; ++c) {
+        if (c < n_chunks) issue(c);
+        cp_commit();
+    }
+    bool ok = true;
+    for (int c = 0; c < n_chunks; ++c) {
+        if (c >= 2 && ok && !mbar_wait_bounded(&mma_done[c & 1], ((c - 2) >> 1) & 1)) ok = false;
+        if (c + kStages - 2 < n_chunks) issue(c + kStages - 2);
+        cp_commit();
+        cp_wait<kStages - 2>();
+        umma::fence_after_sync();
+        const uint8_t* st = stage(c);
+        uint4 cw[2];
+        cw[0] = *reinterpret_cast<const uint4*>(st + tid * 32);
+        cw[1] = *reinterpret_cast<const uint4*>(st + tid * 32 + 16);
+        const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(st + kGuCodes + tid * 4);
+        uint32_t a[32];
+        deq_row64(cw, sc4, a);
+        const uint32_t acol = 128 + 64 * (c & 1) + (is_up ? 32 : 0);
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) lo[i] = a[i], hi[i] = a[16 + i];
+        umma::st_x16(umma::lane_addr(tm, warp, acol), lo);
+        umma::st_x16(umma::lane_addr(tm, warp, acol + 16), hi);
+        const uint32_t ac[2] = {tm + 128 + 64 * (c & 1), tm + 160 + 64 * (c & 1)};
+        chunk_mma<kGuN, 2>(const_cast<uint8_t*>(st) + kGuCodes + kGuScales, dd, ac, c,
+                           &mma_done[c & 1]);
+    }
+    // the last commit covers every MMA of the tile
+    const int last = n_chunks - 1;
+    if (ok && !mbar_wait_bounded(&mma_done[last & 1], (last >> 1) & 1)) ok = false;
+    umma::fence_after_sync();
+    if (!ok) {
+        if (lane == 0) atomicExch(pws<int>(P, P.L.hdr) + PH_STATUS, NVMOE_ERR_TIMEOUT);
+    } else {
+        // epilogue: warps 0-3 entries [0, 32), warps 4-7 entries [32, 64) of the rows they own
+        const float gg = global_of(pool.gate, slot), ug = global_of(pool.up, slot);
+        __half* h = pws<__half>(P, P.L.h);
+        const int c0 = is_up ? kGuN / 2 : 0;
+#pragma unroll 1
+        for (int cc = c0; cc < c0 + kGuN / 2 && cc < nr; cc += 16) {
+            uint32_t g[16], u[16];
+            umma::ld_x16(umma::lane_addr(dd[0], warp, cc), g);
+            umma::ld_x16(umma::lane_addr(dd[1], warp, cc), u);
+            umma::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int n = cc + i;
+                if (n < nr)
+                    h[(int64_t)(eb + n) * I + mt * kTileM + row] = __float2half_rn(
+                        silu(__uint_as_float(g[i]) * gg) * (__uint_as_float(u[i]) * ug));
+            }
+        }
+    }
+    cp_wait<0>();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tm, 256);
+}
+
+// down.  Per stage: codes [128 rows][32 B] (each thread copies its row's half: warps 0-3 K 0-31,
+// warps 4-7 K 32-63), scales [128][4 B], B [128 x 64 f16] = h.  TMEM: D [0,128), A buffer b
+// [128 + 32 b, +32).
+constexpr int kDnCodes = kTileM * 32, kDnScales = kTileM * 4;
+constexpr int kDnStage = kDnCodes + kDnScales + kTileN * kChunk * 2;
+
+__global__ void __launch_bounds__(kPfThreads, 1) pf_down(PfParams P) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t mma_done[2];
+    __shared__ uint32_t tmem_base;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int* hdr = pws<int>(P, P.L.hdr);
+    const int tile = blockIdx.x, mt = blockIdx.y;
+    if (tile >= hdr[PH_N_TILES]) return;
+    const int* tl = pws<int>(P, P.L.tiles) + 3 * tile;
+    const int key = tl[0], eb = tl[1], nr = tl[2];
+    const int H = P.pool.hidden, I = P.pool.inter, S = P.pool.n_slots;
+    const bool sh = key == S;
+    const nvmoe_expert_pool& pool = sh ? P.shared : P.pool;
+    const int slot = sh ? 0 : key;
+    const int row = (warp & 3) * 32 + lane;
+    const int half = warp >= 4 ? 1 : 0;  // K half of each chunk
+    const RowSrc src = row_src(pool.down, slot, (int64_t)mt * kTileM + row);
+    const __half* hm = pws<__half>(P, P.L.h);
+    auto stage = [&](int c) { return smem + (size_t)(c % kStages) * kDnStage; };
+    auto issue = [&](int c) {
+        uint8_t* st = stage(c);
+        cp16(st + row * 32 + half * 16, src.codes + c * 32 + half * 16, 16);
+        if (!half) cp4(st + kDnCodes + row * 4, src.scales + c * 4);
+        issue_b<kTileN>(st + kDnCodes + kDnScales, hm, I, eb, nr, c);
+    };
+
+    if (tid == 0) {
+        mbar_init(&mma_done[0], 1);
+        mbar_init(&mma_done[1], 1);
+        mbar_init_fence();
+    }
+    if (warp == 0) umma::tmem_alloc(&tmem_base, 256);
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tm = tmem_base;
+    const uint32_t dd[1] = {tm};
 
     const int n_chunks = I / kChunk;
-    uint4 c[2];
-    uint32_t sc4;
-    BPieces bp;
-    load_chunk(src, 0, khalf, 32, c, sc4);
-    load_b(hm, I, eb, nr, 0, bp);
+    for (int c = 0; c < kStages - 2; ++c) {
+        if (c < n_chunks) issue(c);
+        cp_commit();
+    }
     bool ok = true;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-        const int s = ch & 1;
-        if (ch >= 2 && ok && !wait_bar(&mma_done[s], ((ch - 2) >> 1) & 1)) ok = false;
+    for (int c = 0; c < n_chunks; ++c) {
+        if (c >= 2 && ok && !mbar_wait_bounded(&mma_done[c & 1], ((c - 2) >> 1) & 1)) ok = false;
+        if (c + kStages - 2 < n_chunks) issue(c + kStages - 2);
+        cp_commit();
+        cp_wait<kStages - 2>();
+        __syncthreads();  // the scale bytes of a row are copied by the warp of its first half
         umma::fence_after_sync();
+        const uint8_t* st = stage(c);
+        uint4 cw[2];
+        cw[0] = *reinterpret_cast<const uint4*>(st + row * 32 + half * 16);
+        cw[1] = make_uint4(0, 0, 0, 0);
+        const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(st + kDnCodes + row * 4);
         uint32_t a[32];
-        deq_row64(c, sc4, a);  // only the first 16 words (32 K values) are meaningful
+        deq_row64(cw, half ? (sc4 >> 16) : (sc4 & 0xffff), a);  // first 16 words meaningful
         uint32_t lo[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) lo[i] = a[i];
-        umma::st_x16(umma::lane_addr(tm, warp, 128 + 64 * s + khalf / 2), lo);
-        store_b(bst + s * kBStage, bp);
-        if (ch + 1 < n_chunks) {
-            load_chunk(src, ch + 1, khalf, 32, c, sc4);
-            load_b(hm, I, eb, nr, ch + 1, bp);
-        }
-        umma::wait_st();
-        umma::fence_smem_async();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
-        if (tid == 0) {
-            const uint32_t b0 = smem_u32(bst + s * kBStage);
-#pragma unroll
-            for (int ks = 0; ks < kChunk / 16; ++ks) {
-                const uint64_t bd = umma::smem_desc(b0 + ks * 2 * (kTileN / 8) * 128,
-                                                    (kTileN / 8) * 128, 128);
-                umma::mma_ts(tm, tm + 128 + 64 * s + 8 * ks, bd, idesc,
-                             (ch > 0 || ks > 0) ? 1u : 0u);
-            }
-            umma::commit(&mma_done[s]);
-        }
+        umma::st_x16(umma::lane_addr(tm, warp, 128 + 32 * (c & 1) + 16 * half), lo);
+        const uint32_t ac[1] = {tm + 128 + 32 * (c & 1)};
+        chunk_mma<kTileN, 1>(const_cast<uint8_t*>(st) + kDnCodes + kDnScales, dd, ac, c,
+                             &mma_done[c & 1]);
     }
     const int last = n_chunks - 1;
-    if (ok && !wait_bar(&mma_done[last & 1], (last >> 1) & 1)) ok = false;
+    if (ok && !mbar_wait_bounded(&mma_done[last & 1], (last >> 1) & 1)) ok = false;
     umma::fence_after_sync();
     if (!ok) {
         if (lane == 0) atomicExch(pws<int>(P, P.L.hdr) + PH_STATUS, NVMOE_ERR_TIMEOUT);
@@ -479,9 +501,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down(PfParams P) {
         const int* ent_tok = pws<int>(P, P.L.ent_tok);
         const float* sgv = (sh && P.shared_gate) ? pws<float>(P, P.L.sg) : nullptr;
         float* yp = pws<float>(P, P.L.ypart);
-        const int c0 = warp >= 4 ? 64 : 0;
+        const int c0 = half ? 64 : 0;
 #pragma unroll 1
-        for (int cc = c0; cc < c0 + 64; cc += 16) {
+        for (int cc = c0; cc < c0 + 64 && cc < nr; cc += 16) {
             uint32_t d[16];
             umma::ld_x16(umma::lane_addr(tm, warp, cc), d);
             umma::wait_ld();
@@ -497,6 +519,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_down(PfParams P) {
             }
         }
     }
+    cp_wait<0>();
     umma::fence_before_sync();
     __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tm, 256);
@@ -597,8 +620,13 @@ extern "C" int nvmoe_moe_ffn_prefill(const nvmoe_ffn_args* a, nvmoe_stream_t str
     const int n_all = a->n_tok * (a->top_k + 1);
     pf_scatter<<<std::min(4 * kNumSMs, (n_all + 255) / 256), 256, 0, st>>>(P);
     pf_gather<<<P.L.n_ent_max, 128, 0, st>>>(P);
-    pf_gate_up<<<dim3(P.L.max_tiles, I / kTileM), kPfThreads, 0, st>>>(P);
-    pf_down<<<dim3(P.L.max_tiles, H / kTileM), kPfThreads, 0, st>>>(P);
+    const int gu_smem = kStages * kGuStage, dn_smem = kStages * kDnStage;
+    NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        gu_smem));
+    NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf_down, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        dn_smem));
+    pf_gate_up<<<dim3(P.L.max_tiles, I / kTileM, kTileN / kGuN), kPfThreads, gu_smem, st>>>(P);
+    pf_down<<<dim3(P.L.max_tiles, H / kTileM), kPfThreads, dn_smem, st>>>(P);
     const int64_t n4 = (int64_t)a->n_tok * (H / 4);
     pf_combine<<<(int)std::min<int64_t>(8 * kNumSMs, (n4 + 255) / 256), 256, 0, st>>>(P);
     pf_status<<<1, 1, 0, st>>>(P);
