@@ -91,6 +91,7 @@ struct FfnParams {
     WsLayout L;
     int32_t* status;
     int grp_tok;           // entries per token group: min(8, n_tok), at least 1
+    const uint32_t* aux_table;  // the format's lookup table in device memory (IQ2_XXS grid)
     int ypart_smem;        // 1: the down phase keeps y_part in shared memory
 };
 

@@ -28,6 +28,11 @@
 #include <algorithm>
 
 namespace nvmoe {
+
+// IQ2_XXS grid registered with nvmoe_set_iq2xxs_grid (dequant.cu)
+bool iq2xxs_grid_ready(int device);
+const uint8_t* iq2xxs_grid_device_ptr();
+
 namespace {
 
 constexpr int kConsumerWarps = 8;
@@ -83,6 +88,7 @@ struct FusedLayout {
     int xt;                  // x rows per gate_up stage (staged x), 0 with resident x
     int x_res;               // 1: every token row resident in shared memory, loaded once
     int off_x, off_dn, off_red, off_meta, off_yp, off_bar, total;
+    int off_aux;             // the format's lookup table (IQ2_XXS grid)
 };
 
 __host__ __device__ inline int round128(int v) { return (v + 127) / 128 * 128; }
@@ -97,14 +103,15 @@ constexpr int kAcc = 8;
 template <typename Fmt>
 __device__ __forceinline__ void gate_up_tile(const uint8_t* gcode, const uint8_t* ucode,
                                              const uint8_t* gsc, const uint8_t* usc, int cb,
-                                             int sb, const __half* xs, bool has_tok, int k0,
+                                             int sb, const uint32_t* aux, const __half* xs,
+                                             bool has_tok, int k0,
                                              int g, int q, float (&accg)[kAcc][4],
                                              float (&accu)[kAcc][4]) {
     typename Fmt::Row ga, gb, ua, ub;
-    Fmt::load_smem(ga, gcode + g * cb, gsc + g * sb, k0, q);
-    Fmt::load_smem(gb, gcode + (g + 8) * cb, gsc + (g + 8) * sb, k0, q);
-    Fmt::load_smem(ua, ucode + g * cb, usc + g * sb, k0, q);
-    Fmt::load_smem(ub, ucode + (g + 8) * cb, usc + (g + 8) * sb, k0, q);
+    Fmt::load_smem(ga, gcode + g * cb, gsc + g * sb, k0, q, aux);
+    Fmt::load_smem(gb, gcode + (g + 8) * cb, gsc + (g + 8) * sb, k0, q, aux);
+    Fmt::load_smem(ua, ucode + g * cb, usc + g * sb, k0, q, aux);
+    Fmt::load_smem(ub, ucode + (g + 8) * cb, usc + (g + 8) * sb, k0, q, aux);
 #pragma unroll
     for (int s2 = 0; s2 < Fmt::kSteps; s2 += 2) {
         const uint4 xb = has_tok ? *reinterpret_cast<const uint4*>(xs + k0 + Fmt::kofs(q, s2))
@@ -127,11 +134,12 @@ __device__ __forceinline__ void gate_up_tile(const uint8_t* gcode, const uint8_t
 // this tile (4 x 8 halves of token g).
 template <typename Fmt>
 __device__ __forceinline__ void down_tile(const uint8_t* code, const uint8_t* sc, int cb, int sb,
-                                          const uint4 (&hb)[4], int k0, int g, int q,
-                                          float (&acc)[kAcc][4]) {
+                                          const uint32_t* aux, const uint4 (&hb)[Fmt::kSteps / 2],
+                                          int k0, int g,
+                                          int q, float (&acc)[kAcc][4]) {
     typename Fmt::Row ra, rbw;
-    Fmt::load_smem(ra, code + g * cb, sc + g * sb, k0, q);
-    Fmt::load_smem(rbw, code + (g + 8) * cb, sc + (g + 8) * sb, k0, q);
+    Fmt::load_smem(ra, code + g * cb, sc + g * sb, k0, q, aux);
+    Fmt::load_smem(rbw, code + (g + 8) * cb, sc + (g + 8) * sb, k0, q, aux);
 #pragma unroll
     for (int s2 = 0; s2 < Fmt::kSteps; s2 += 2) {
         const uint4 h = hb[s2 >> 1];
@@ -153,12 +161,14 @@ __device__ __forceinline__ void fold_acc(float (&acc)[kAcc][4]) {
         for (int v = 0; v < 4; ++v) acc[0][v] += acc[a][v];
 }
 
-// h fragments of one 128-wide K tile for token row hrow (null: no token -> zeros), read through
-// L2 (h is written by other CTAs of this grid).
-__device__ __forceinline__ void load_h_tile(const __half* hrow, int k0, int q, uint4 (&hb)[4]) {
+// h fragments of one K tile for token row hrow (null: no token -> zeros), in the order of the
+// format's step pairs, read through L2 (h is written by other CTAs of this grid).
+template <typename Fmt>
+__device__ __forceinline__ void load_h_tile(const __half* hrow, int k0, int q,
+                                            uint4 (&hb)[Fmt::kSteps / 2]) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-        hb[i] = hrow ? __ldcg(reinterpret_cast<const uint4*>(hrow + k0 + 32 * q + 8 * i))
+    for (int i = 0; i < Fmt::kSteps / 2; ++i)
+        hb[i] = hrow ? __ldcg(reinterpret_cast<const uint4*>(hrow + k0 + Fmt::kofs(q, 2 * i)))
                      : make_uint4(0, 0, 0, 0);
 }
 
@@ -241,6 +251,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
         mbar_init(gu_drained, kCW);
         mbar_init_fence();
     }
+    // the format's lookup table (IQ2_XXS grid), constant across calls
+    uint32_t* aux = reinterpret_cast<uint32_t*>(smem + FL.off_aux);
+    for (int i = tid; i < Fmt::kAuxBytes / 4; i += blockDim.x) aux[i] = __ldg(P.aux_table + i);
     __syncthreads();
     // everything below reads the group records / token rows of the kernel before this one
     grid_dep_wait();
@@ -310,15 +323,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                                   (const uint8_t*)pool.up.data + slot * pool.up.slot_stride +
                                       r0 * pool.up.row_stride,
                                   16, cbg, pool.up.row_stride, &gu_full[st]);
-                        bulk_rows(stg + og_gs,
-                                  (const uint8_t*)pool.gate.scale +
-                                      slot * pool.gate.scale_slot_stride +
-                                      r0 * pool.gate.scale_row_stride,
-                                  16, sbg, pool.gate.scale_row_stride, &gu_full[st]);
-                        bulk_rows(stg + og_us,
-                                  (const uint8_t*)pool.up.scale + slot * pool.up.scale_slot_stride +
-                                      r0 * pool.up.scale_row_stride,
-                                  16, sbg, pool.up.scale_row_stride, &gu_full[st]);
+                        if (sbg > 0) {  // formats with a separate scale bank
+                            bulk_rows(stg + og_gs,
+                                      (const uint8_t*)pool.gate.scale +
+                                          slot * pool.gate.scale_slot_stride +
+                                          r0 * pool.gate.scale_row_stride,
+                                      16, sbg, pool.gate.scale_row_stride, &gu_full[st]);
+                            bulk_rows(stg + og_us,
+                                      (const uint8_t*)pool.up.scale +
+                                          slot * pool.up.scale_slot_stride +
+                                          r0 * pool.up.scale_row_stride,
+                                      16, sbg, pool.up.scale_row_stride, &gu_full[st]);
+                        }
                         if (!FL.x_res)
                             for (int n = 0; n < nt; ++n)
                                 bulk_g2s(stg + og_x + n * xrow, x16 + (int64_t)hdr[GD_TOK + n] * H,
@@ -373,11 +389,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                                       (const uint8_t*)pool.down.data +
                                           slot * pool.down.slot_stride + r0 * pool.down.row_stride,
                                       16, cbd, pool.down.row_stride, &dn_full[st]);
-                            bulk_rows(stg + od_sc,
-                                      (const uint8_t*)pool.down.scale +
-                                          slot * pool.down.scale_slot_stride +
-                                          r0 * pool.down.scale_row_stride,
-                                      16, sbd, pool.down.scale_row_stride, &dn_full[st]);
+                            if (sbd > 0)
+                                bulk_rows(stg + od_sc,
+                                          (const uint8_t*)pool.down.scale +
+                                              slot * pool.down.scale_slot_stride +
+                                              r0 * pool.down.scale_row_stride,
+                                          16, sbd, pool.down.scale_row_stride, &dn_full[st]);
                         }
                     }
                     ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -459,13 +476,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
 #pragma unroll
                     for (int t = 0; t < TPW; ++t)
                         gate_up_tile<Fmt>(stg + kStageHdr, stg + og_uc, stg + og_gs, stg + og_us,
-                                          cbg, sbg, xs, has_tok, (warp * TPW + t) * Fmt::kWarpTileK,
+                                          cbg, sbg, aux, xs, has_tok, (warp * TPW + t) * Fmt::kWarpTileK,
                                           g, q, accg, accu);
                 } else {
                     const int kw = H / kCW;
                     for (int k0 = warp * kw; k0 < (warp + 1) * kw; k0 += Fmt::kWarpTileK)
                         gate_up_tile<Fmt>(stg + kStageHdr, stg + og_uc, stg + og_gs, stg + og_us,
-                                          cbg, sbg, xs, has_tok, k0, g, q, accg, accu);
+                                          cbg, sbg, aux, xs, has_tok, k0, g, q, accg, accu);
                 }
             }
             __syncwarp();
@@ -539,18 +556,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 }
                 const __half* hrow = g < nt ? h16 + (int64_t)(e0 + g) * I : nullptr;
                 if constexpr (TD > 0) {
-                    uint4 hb[TD][4];
-#pragma unroll
-                    for (int t = 0; t < TD; ++t) load_h_tile(hrow, t * Fmt::kWarpTileK, q, hb[t]);
+                    uint4 hb[TD][Fmt::kSteps / 2];
 #pragma unroll
                     for (int t = 0; t < TD; ++t)
-                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, hb[t],
+                        load_h_tile<Fmt>(hrow, t * Fmt::kWarpTileK, q, hb[t]);
+#pragma unroll
+                    for (int t = 0; t < TD; ++t)
+                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, aux, hb[t],
                                        t * Fmt::kWarpTileK, g, q, acc);
                 } else {
                     for (int k0 = 0; k0 < I; k0 += Fmt::kWarpTileK) {
-                        uint4 hb[4];
-                        load_h_tile(hrow, k0, q, hb);
-                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, hb, k0, g, q, acc);
+                        uint4 hb[Fmt::kSteps / 2];
+                        load_h_tile<Fmt>(hrow, k0, q, hb);
+                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, aux, hb, k0, g, q,
+                                       acc);
                     }
                 }
             }
@@ -590,9 +609,12 @@ bool pool_ok(const nvmoe_expert_pool& p) {
 
 // Rows are staged with 1-D bulk copies (TMA), which need 16-byte aligned addresses and sizes;
 // reject any bank whose base or strides would break that alignment.
-bool bank_aligned(const nvmoe_matrix_bank& b, bool nvfp4) {
+// Bulk copies move 16 rows at a time: either as one run (rows contiguous) or row by row (each
+// row a multiple of 16 bytes); row_bytes is the format's bytes per row of K values.
+bool bank_aligned(const nvmoe_matrix_bank& b, bool nvfp4, int row_bytes) {
     const uintptr_t d = reinterpret_cast<uintptr_t>(b.data);
-    if ((d & 15) || (b.slot_stride & 15) || (b.row_stride & 15)) return false;
+    if ((d & 15) || (b.slot_stride & 15)) return false;
+    if (b.row_stride != row_bytes && ((b.row_stride & 15) || (row_bytes & 15))) return false;
     if (nvfp4) {
         const uintptr_t s = reinterpret_cast<uintptr_t>(b.scale);
         if (!b.scale || (s & 15) || (b.scale_slot_stride & 15) || (b.scale_row_stride & 15))
@@ -603,7 +625,13 @@ bool bank_aligned(const nvmoe_matrix_bank& b, bool nvfp4) {
 
 bool pool_aligned(const nvmoe_expert_pool& p) {
     const bool nv = p.quant == NVMOE_Q_NVFP4;
-    return bank_aligned(p.gate, nv) && bank_aligned(p.up, nv) && bank_aligned(p.down, nv);
+    auto rb = [&](int k) {
+        return p.quant == NVMOE_Q_NVFP4 ? k / 2
+             : p.quant == NVMOE_Q_Q2_K  ? FmtQ2K::code_bytes(k)
+                                        : FmtIQ2XXS::code_bytes(k);
+    };
+    return bank_aligned(p.gate, nv, rb(p.hidden)) && bank_aligned(p.up, nv, rb(p.hidden)) &&
+           bank_aligned(p.down, nv, rb(p.inter));
 }
 
 
@@ -632,8 +660,9 @@ int launch_fmt(FfnParams& P, cudaStream_t st) {
     const int x_bytes = FL.x_res ? round128(std::max(1, P.n_tok) * xrow) : 0;
     const int red_bytes = 2 * kCW * 32 * 8 * 4, meta_bytes = 2 * 8 * 4;
     const int bar_bytes = 8 * (2 * 4 + 2 * 64 + 6) + 64;
+    const int aux_bytes = round128(Fmt::kAuxBytes);
     const int yp_bytes = round128(P.L.n_ent_max * 16 * 4);
-    const int fixed = red_bytes + meta_bytes + bar_bytes + x_bytes;
+    const int fixed = red_bytes + meta_bytes + bar_bytes + x_bytes + aux_bytes;
     // y_part in shared memory when it leaves room for 2 gate_up and 8 down stages
     P.ypart_smem = (fixed + yp_bytes + 2 * FL.stage_gu + kCW * FL.stage_dn <= kSmemCap) ? 1 : 0;
     const int avail = kSmemCap - fixed - (P.ypart_smem ? yp_bytes : 0);
@@ -648,7 +677,8 @@ int launch_fmt(FfnParams& P, cudaStream_t st) {
     FL.off_red = FL.off_dn + FL.nst_dn * FL.stage_dn;
     FL.off_meta = FL.off_red + red_bytes;
     FL.off_yp = FL.off_meta + meta_bytes;
-    FL.off_bar = FL.off_yp + (P.ypart_smem ? yp_bytes : 0);
+    FL.off_aux = FL.off_yp + (P.ypart_smem ? yp_bytes : 0);
+    FL.off_bar = FL.off_aux + aux_bytes;
     FL.total = FL.off_bar + 8 * (2 * FL.nst_gu + 2 * (FL.nst_dn + FL.nst_dn_ext) + 6);
     // compile-time K tiles per MMA warp (gate_up) and per down slab where the shape has an
     // instantiation; other shapes take runtime tile loops
@@ -681,17 +711,34 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
         if (!pool_ok(sp) || sp.quant != pool.quant || sp.hidden != H || sp.inter != I)
             return NVMOE_ERR_INVALID_ARG;
     }
-    if (pool.quant != NVMOE_Q_NVFP4) return NVMOE_ERR_UNSUPPORTED;
-    // warp tiling: gate_up K = H over 8 warps, down K = I per warp, 16-row tiles
-    if (H % (kConsumerWarps * FmtNvfp4::kWarpTileK) != 0 || I % FmtNvfp4::kWarpTileK != 0 ||
-        I % 16 != 0 || H % 16 != 0)
+    const bool nv = pool.quant == NVMOE_Q_NVFP4;
+    if (!nv && pool.quant != NVMOE_Q_Q2_K && pool.quant != NVMOE_Q_IQ2_XXS)
         return NVMOE_ERR_UNSUPPORTED;
-    if (!pool.gate.scale || !pool.up.scale || !pool.down.scale) return NVMOE_ERR_INVALID_ARG;
+    // warp tiling: gate_up K = H over 8 warps, down K = I per warp, 16-row tiles; K tiles of
+    // 128 values (NVFP4) or one 256-value super-block (Q2_K / IQ2_XXS)
+    const int tk = nv ? FmtNvfp4::kWarpTileK : FmtQ2K::kWarpTileK;
+    if (H % (kConsumerWarps * tk) != 0 || I % tk != 0 || I % 16 != 0 || H % 16 != 0)
+        return NVMOE_ERR_UNSUPPORTED;
+    if (nv && (!pool.gate.scale || !pool.up.scale || !pool.down.scale))
+        return NVMOE_ERR_INVALID_ARG;
     if (!pool_aligned(pool) || (args->shared && !pool_aligned(*args->shared)))
         return NVMOE_ERR_INVALID_ARG;
-    if (pool.gate.row_stride < H / 2 || pool.down.row_stride < I / 2 ||
-        pool.gate.scale_row_stride < H / 16 || pool.down.scale_row_stride < I / 16)
+    const int rbh = nv ? H / 2 : (pool.quant == NVMOE_Q_Q2_K ? FmtQ2K::code_bytes(H)
+                                                             : FmtIQ2XXS::code_bytes(H));
+    const int rbi = nv ? I / 2 : (pool.quant == NVMOE_Q_Q2_K ? FmtQ2K::code_bytes(I)
+                                                             : FmtIQ2XXS::code_bytes(I));
+    if (pool.gate.row_stride < rbh || pool.up.row_stride < rbh || pool.down.row_stride < rbi)
         return NVMOE_ERR_INVALID_ARG;
+    if (nv && (pool.gate.scale_row_stride < H / 16 || pool.down.scale_row_stride < I / 16))
+        return NVMOE_ERR_INVALID_ARG;
+    const uint32_t* aux_table = nullptr;
+    if (pool.quant == NVMOE_Q_IQ2_XXS) {
+        int dev = 0;
+        NVMOE_CUDA_TRY(cudaGetDevice(&dev));
+        if (!iq2xxs_grid_ready(dev)) return NVMOE_ERR_NO_TABLES;
+        aux_table = reinterpret_cast<const uint32_t*>(iq2xxs_grid_device_ptr());
+        if (!aux_table) return NVMOE_ERR_NO_TABLES;
+    }
     if (args->x_row_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(args->x) & 15))
         return NVMOE_ERR_INVALID_ARG;
     const WsLayout L = ws_layout(args->n_tok > 0 ? args->n_tok : 1, args->top_k, H, I, pool.n_slots);
@@ -719,10 +766,17 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
     // groups never exceed the token count, so a group's x rows fit the stage even when the
     // caller's slot ids repeat a slot within a token
     P.grp_tok = std::max(1, std::min(kGroupMaxTok, args->n_tok));
+    P.aux_table = aux_table;
     return NVMOE_OK;
 }
 
-int ffn_launch_main(FfnParams& P, cudaStream_t st) { return launch_fmt<FmtNvfp4>(P, st); }
+int ffn_launch_main(FfnParams& P, cudaStream_t st) {
+    switch (P.pool.quant) {
+        case NVMOE_Q_Q2_K: return launch_fmt<FmtQ2K>(P, st);
+        case NVMOE_Q_IQ2_XXS: return launch_fmt<FmtIQ2XXS>(P, st);
+        default: return launch_fmt<FmtNvfp4>(P, st);
+    }
+}
 
 int ffn_launch_prep(FfnParams& P, cudaStream_t st) {
     const size_t prep_smem = (size_t)P.pool.n_slots * 4;
