@@ -185,6 +185,15 @@ typedef struct nvmoe_ffn_args {
 size_t nvmoe_moe_ffn_workspace_size(int n_tok, int top_k, int hidden, int inter, int n_slots);
 int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
 
+/* Which kernel nvmoe_moe_ffn takes for these arguments (no launch): NVMOE_FFN_PATH_MMA
+ * (in-register dequantisation feeding mma.sync; the default) or NVMOE_FFN_PATH_FP4 (block-scaled
+ * FP4 MMAs on the tensor cores, weights fed unchanged from the slot banks, activations as 4
+ * NVFP4 residual terms), which runs for NVFP4 pools with H and I multiples of 256 when the
+ * environment variable NVMOE_FFN_KERNEL is "fp4".  Negative = the call's error status.  An
+ * addition of this library (no counterpart in the reference). */
+enum { NVMOE_FFN_PATH_MMA = 0, NVMOE_FFN_PATH_FP4 = 1 };
+int nvmoe_moe_ffn_path(const nvmoe_ffn_args* args);
+
 /* Same FFN as nvmoe_moe_ffn, for callers that cannot allocate device memory when they run it
  * (e.g. a llama.cpp eval callback, where every device buffer belongs to ggml's allocator and a
  * cudaMalloc would synchronise the device mid-graph, or a process whose spare VRAM is all given

@@ -93,7 +93,7 @@ __device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, i
     const int H = P.pool.hidden;
     const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
     __half* x16 = wsp<__half>(P, P.L.x16) + (int64_t)t * H;
-    float dot = 0.f;
+    float dot = 0.f, amax = 0.f;
     for (int i = lane * 8; i < H; i += 256) {
         const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
         const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
@@ -102,9 +102,15 @@ __device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, i
         for (int k = 0; k < 8; ++k) {
             const float f = bf16_bits_to_f32(e[k]);
             o[k] = __float2half_rn(f);
+            amax = fmaxf(amax, fabsf(f));
             if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
         }
-        *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+        if (!P.use_fp4) *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+    }
+    if (P.use_fp4) {  // the row's FP4 term exponent
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0) wsp<int>(P, P.L.xk)[t] = fp4_row_exp(amax);
     }
     if (P.shared_gate) {
 #pragma unroll
@@ -285,6 +291,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     __syncthreads();
 
     // ---- C. FFN grouping from the slot ids in shared memory (ffn_group_block, staged)
+    reset_phase_counters(P);
     for (int p = tid; p < n; p += nthr) atomicAdd(&cnt[sids[p]], 1);
     __syncthreads();
     int* desc = wsp<int>(P, P.L.grp_desc);

@@ -2,6 +2,8 @@
 // groups and the grouping step (shared by the FFN prep kernel and the fused decode front kernel).
 #pragma once
 
+#include <string.h>
+
 #include "common.cuh"
 
 namespace nvmoe {
@@ -27,10 +29,17 @@ enum {
 };
 
 // ------------------------------------------------------------------ workspace layout
+// Tensor-core (block-scaled FP4) FFN path: per-group activation images and counters.
+constexpr int kFp4Terms = 4;          // NVFP4 terms per activation (x = sum of 4 scaled E2M1 tiles)
+constexpr int kFp4BRows = 4 * 8;      // B rows of a group: kFp4Terms x up to 8 tokens
+constexpr int kFp4ImgStage = kFp4BRows * 144;  // one 256-wide K stage: codes rows x 128 B, SF x 16 B
+constexpr int kFp4MaxCtas = 160;
+
 struct WsLayout {
     size_t hdr, active_slot, tok_cnt, grp_desc, grp_done, ent_tok, ent_w, ent_of, x16, sg, h16,
-        ypart, total;
+        ypart, bimg, ximg, xk, hk, h32, gcnt, phase, total;
     int a_max, n_ent_max, g_max;
+    int jb, rb, ks_gu, ks_dn;  // FP4 path: 64-row j-blocks, 128-row H blocks, K stages (0: off)
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -40,7 +49,15 @@ __host__ __device__ inline WsLayout ws_layout(int n_tok, int top_k, int H, int I
     const int n_route = n_tok * top_k;
     L.a_max = (n_route < n_slots ? n_route : n_slots) + 1;
     L.n_ent_max = n_route + n_tok;
-    L.g_max = L.n_ent_max;  // a group holds at least one entry
+    // a group holds at least one entry; slot s with c_s entries makes ceil(c_s / gt) groups
+    const int gt = n_tok < 8 ? (n_tok > 0 ? n_tok : 1) : 8;
+    const int g_bound = n_route / gt + L.a_max + (n_tok + gt - 1) / gt + 2;
+    L.g_max = L.n_ent_max < g_bound ? L.n_ent_max : g_bound;
+    const bool fp4 = H % 256 == 0 && I % 256 == 0;
+    L.jb = fp4 ? I / 64 : 0;
+    L.rb = fp4 ? H / 128 : 0;
+    L.ks_gu = fp4 ? H / 256 : 0;
+    L.ks_dn = fp4 ? I / 256 : 0;
     size_t o = 0;
     L.hdr = o;
     o = align_up(o + 64, 256);
@@ -66,6 +83,21 @@ __host__ __device__ inline WsLayout ws_layout(int n_tok, int top_k, int H, int I
     o = align_up(o + 2 * (size_t)L.n_ent_max * I, 256);
     L.ypart = o;  // used by the down phase only when its shared-memory copy does not fit
     o = align_up(o + 4 * (size_t)L.n_ent_max * H, 256);
+    L.bimg = o;  // per group: the down K stages of the B operand image (h)
+    o = align_up(o + (size_t)L.g_max * L.ks_dn * kFp4ImgStage, 1024);
+    L.ximg = o;  // per token: gate_up operand rows (2 swizzle phases x K stages x 4 rows x 128 B,
+                 // then K stages x 4 rows x 16 B of scales)
+    o = align_up(o + (size_t)n_tok * L.ks_gu * (2 * 512 + 64), 1024);
+    L.xk = o;  // per token: the power-of-two exponent of its activation terms
+    o = align_up(o + 4 * (size_t)n_tok, 256);
+    L.hk = o;  // per (group, token of the group): the exponent of its h terms
+    o = align_up(o + 4 * (size_t)L.g_max * kGroupMaxTok, 256);
+    L.h32 = o;  // per (group, token of the group): h in fp32 [I]
+    o = align_up(o + (fp4 ? 4 * (size_t)L.g_max * kGroupMaxTok * I : 0), 256);
+    L.gcnt = o;  // per group: gate_up units stored, h rows built
+    o = align_up(o + 8 * (size_t)L.g_max, 256);
+    L.phase = o;  // grid phase counters of the FP4 kernel (4 ints)
+    o = align_up(o + 16, 256);
     L.total = o;
     return L;
 }
@@ -93,6 +125,7 @@ struct FfnParams {
     int grp_tok;           // entries per token group: min(8, n_tok), at least 1
     const uint32_t* aux_table;  // the format's lookup table in device memory (IQ2_XXS grid)
     int ypart_smem;        // 1: the down phase keeps y_part in shared memory
+    int use_fp4;           // 1: the block-scaled FP4 tensor-core kernel runs this call (NVFP4)
 };
 
 template <typename T>
@@ -126,17 +159,44 @@ __device__ inline void finish_record(const FfnParams& P, int grp, int* d, const 
     f[GD_DGLOB] = global_of(pool.down, slot);
     for (int k = 28; k < kDescInts; ++k) d[k] = 0;
     wsp<int>(P, P.L.grp_done)[grp] = 0;
+    wsp<int>(P, P.L.gcnt)[2 * grp] = 0;
+    wsp<int>(P, P.L.gcnt)[2 * grp + 1] = 0;
+}
+
+// Zeroes the grid phase counters of the FP4 kernel (whole block).
+__device__ inline void reset_phase_counters(const FfnParams& P) {
+    if (threadIdx.x < 4) wsp<int>(P, P.L.phase)[threadIdx.x] = 0;
+}
+
+// Power-of-two exponent of an activation row for the FP4 path: |row max| * 2^k in [1024, 2048)
+// (k = 0 for a zero, infinite or NaN maximum), kept within +-120 so 2^k and 2^-(k + 6) are
+// normal floats.
+__host__ __device__ inline int fp4_row_exp(float amax) {
+    if (!(amax > 0.f) || !(amax < 3.0e38f)) return 0;
+    uint32_t bits;
+    memcpy(&bits, &amax, 4);
+    const int e = (int)((bits >> 23) & 0xff) - 127;  // floor(log2 amax) for normal values
+    const int k = 10 - e;
+    return k < -120 ? -120 : (k > 120 ? 120 : k);
+}
+__host__ __device__ inline float fp4_exp2(int k) {  // 2^k for k in [-126, 127]
+    const uint32_t bits = (uint32_t)(k + 127) << 23;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
 }
 
 // Token rows -> f16 copy (the MMA B operand) and the shared-expert gate sigmoid(x . g), for
-// tokens t = t_begin, t_begin + t_step, ... by the whole block.
+// tokens t = t_begin, t_begin + t_step, ... by the whole block.  On the FP4 path: no f16 copy,
+// the row's term exponent instead (xk).
 __device__ inline void ffn_convert_tokens(const FfnParams& P, int t_begin, int t_step) {
     const int H = P.pool.hidden;
     __shared__ float red[32];
+    __shared__ float amx[32];
     for (int t = t_begin; t < P.n_tok; t += t_step) {
         const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
         __half* x16 = wsp<__half>(P, P.L.x16) + (int64_t)t * H;
-        float dot = 0.f;
+        float dot = 0.f, amax = 0.f;
         for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
             const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
             const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
@@ -145,9 +205,22 @@ __device__ inline void ffn_convert_tokens(const FfnParams& P, int t_begin, int t
             for (int k = 0; k < 8; ++k) {
                 const float f = bf16_bits_to_f32(e[k]);
                 o[k] = __float2half_rn(f);
+                amax = fmaxf(amax, fabsf(f));
                 if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
             }
-            *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+            if (!P.use_fp4) *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+        }
+        if (P.use_fp4) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            if ((threadIdx.x & 31) == 0) amx[threadIdx.x >> 5] = amax;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                float m = 0.f;
+                for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, amx[w]);
+                wsp<int>(P, P.L.xk)[t] = fp4_row_exp(m);
+            }
+            __syncthreads();
         }
         if (P.shared_gate) {
 #pragma unroll
@@ -178,6 +251,7 @@ __device__ inline void ffn_group_block(const FfnParams& P, int* smem_i) {
     __syncthreads();
     if (tid == 0) s_bad = 0;
     for (int s = tid; s < S; s += nthr) cnt[s] = 0;
+    reset_phase_counters(P);
     __syncthreads();
     for (int p = tid; p < n; p += nthr) {
         const int t = p / K, j = p - t * K;

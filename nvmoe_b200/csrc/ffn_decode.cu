@@ -63,11 +63,12 @@ __device__ __forceinline__ void report_timeout(const FfnParams& P) {
 // Copies `rows` rows of `row_bytes` from a bank (row stride `stride`) into contiguous smem.
 __device__ __forceinline__ void bulk_rows(uint8_t* dst, const uint8_t* src, int rows,
                                           int row_bytes, int64_t stride, uint64_t* bar) {
+    const uint64_t pol = l2_evict_first_policy();
     if (stride == row_bytes) {
-        bulk_g2s(dst, src, (uint32_t)(rows * row_bytes), bar);
+        bulk_g2s_stream(dst, src, (uint32_t)(rows * row_bytes), bar, pol);
     } else {
         for (int r = 0; r < rows; ++r)
-            bulk_g2s(dst + r * row_bytes, src + r * stride, (uint32_t)row_bytes, bar);
+            bulk_g2s_stream(dst + r * row_bytes, src + r * stride, (uint32_t)row_bytes, bar, pol);
     }
 }
 
@@ -699,6 +700,9 @@ int launch_fmt(FfnParams& P, cudaStream_t st) {
 
 }  // namespace
 
+bool ffn_fp4_eligible(const FfnParams& P);
+int ffn_fp4_launch(const FfnParams& P, cudaStream_t st);
+
 int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
     if (!args || !args->pool || !args->x || !args->slot_ids || !args->weights || !args->y)
         return NVMOE_ERR_INVALID_ARG;
@@ -716,9 +720,12 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
         return NVMOE_ERR_UNSUPPORTED;
     // warp tiling: gate_up K = H over 8 warps, down K = I per warp, 16-row tiles; K tiles of
     // 128 values (NVFP4) or one 256-value super-block (Q2_K / IQ2_XXS)
+    // (NVFP4 shapes with H and I multiples of 256 also run on the FP4 tensor-core kernel, which
+    // has no further constraint; ffn_fp4_eligible decides below)
     const int tk = nv ? FmtNvfp4::kWarpTileK : FmtQ2K::kWarpTileK;
-    if (H % (kConsumerWarps * tk) != 0 || I % tk != 0 || I % 16 != 0 || H % 16 != 0)
-        return NVMOE_ERR_UNSUPPORTED;
+    const bool mma_shape = H % (kConsumerWarps * tk) == 0 && I % tk == 0 && I % 16 == 0;
+    const bool fp4_shape = nv && H % 256 == 0 && I % 256 == 0;
+    if (!mma_shape && !fp4_shape) return NVMOE_ERR_UNSUPPORTED;
     if (nv && (!pool.gate.scale || !pool.up.scale || !pool.down.scale))
         return NVMOE_ERR_INVALID_ARG;
     if (!pool_aligned(pool) || (args->shared && !pool_aligned(*args->shared)))
@@ -767,10 +774,13 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
     // caller's slot ids repeat a slot within a token
     P.grp_tok = std::max(1, std::min(kGroupMaxTok, args->n_tok));
     P.aux_table = aux_table;
+    P.use_fp4 = ffn_fp4_eligible(P) ? 1 : 0;
+    if (!P.use_fp4 && !mma_shape) return NVMOE_ERR_UNSUPPORTED;
     return NVMOE_OK;
 }
 
 int ffn_launch_main(FfnParams& P, cudaStream_t st) {
+    if (P.use_fp4) return ffn_fp4_launch(P, st);
     switch (P.pool.quant) {
         case NVMOE_Q_Q2_K: return launch_fmt<FmtQ2K>(P, st);
         case NVMOE_Q_IQ2_XXS: return launch_fmt<FmtIQ2XXS>(P, st);
@@ -797,6 +807,13 @@ extern "C" size_t nvmoe_moe_ffn_workspace_size(int n_tok, int top_k, int hidden,
                                                int n_slots) {
     if (n_tok <= 0 || top_k <= 0 || hidden <= 0 || inter <= 0 || n_slots <= 0) return 0;
     return nvmoe::ws_layout(n_tok, top_k, hidden, inter, n_slots).total;
+}
+
+extern "C" int nvmoe_moe_ffn_path(const nvmoe_ffn_args* args) {
+    nvmoe::FfnParams P;
+    const int rc = nvmoe::ffn_setup(args, P);
+    if (rc != NVMOE_OK) return rc;
+    return P.use_fp4 ? NVMOE_FFN_PATH_FP4 : NVMOE_FFN_PATH_MMA;
 }
 
 extern "C" int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream) {

@@ -101,6 +101,41 @@ __device__ __forceinline__ void ld_x16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr)
         : "memory");
 }
+// Shared-memory descriptor of a K-major tile in the 128-byte swizzle layout that TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B: 128-byte rows, 8-row (1024-byte) swizzle atoms stacked along M/N
+// (SBO = 1024; LBO unused).  The tile base must be 1024-byte aligned; a K step inside the
+// 128-byte row advances the start address (32 bytes per 64 FP4 values).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of kind::mxf4nvf4: A and B E2M1 (packed, two per byte), UE4M3 scale
+// factors, K-major, dense K = 64 per instruction, fp32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_mxf4(int m, int n) {
+    return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// D (+)= (A x SFA) * (B x SFB)^T, K = 64, one UE4M3 scale per 16 values of each row of A and B.
+// Scale factors in tensor memory (column addresses 4-column aligned):
+//   SFA (M = 128): column sfa + m1, lane m0 (and the same in the other three lane quadrants)
+//                  hold the 4 scales of row 32 m1 + m0, K block j in byte j;
+//   SFB (N <= 32): column sfb, lane n (every quadrant) holds the 4 scales of row n.
+__device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], "
+        "[%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem));
+}
+
 __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 

@@ -234,6 +234,26 @@ class FfnWorkspace:
 _default_ws: dict[int, FfnWorkspace] = {}
 
 
+def ffn_path(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor,
+             weights: torch.Tensor, shared: ExpertWeights | None = None) -> str:
+    """Kernel that moe_ffn takes for these arguments: "fp4" (block-scaled FP4 tensor-core
+    MMAs) or "mma" (mma.sync on in-register dequantised weights); see nvmoe_moe_ffn_path."""
+    _require_cuda(x, slot_ids, weights)
+    n, H = x.shape
+    k = slot_ids.shape[1]
+    ws = _default_ws.setdefault(x.device.index or 0, FfnWorkspace(x.device)).get(
+        ffn_workspace_bytes(n, k, pool.hidden, pool.inter, pool.n_slots))
+    ps = expert_pool_struct(pool)
+    ss = expert_pool_struct(shared) if shared is not None else None
+    args = _lib.FfnArgs(
+        C.pointer(ps), C.pointer(ss) if ss is not None else None, None, x.data_ptr(),
+        x.stride(0), slot_ids.data_ptr(), slot_ids.stride(0), weights.data_ptr(),
+        weights.stride(0), k, n, x.data_ptr(), x.stride(0), ws.data_ptr(), ws.numel(), None)
+    rc = lib().nvmoe_moe_ffn_path(C.byref(args))
+    check(min(rc, 0), "nvmoe_moe_ffn_path")
+    return "fp4" if rc == 1 else "mma"
+
+
 def moe_ffn(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor, weights: torch.Tensor,
             shared: ExpertWeights | None = None, shared_gate: torch.Tensor | None = None,
             out: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,

@@ -273,7 +273,8 @@ def test_ffn_nvfp4_matches_oracle(cuda_device, n_tok, k, shared, sgate):
 def test_ffn_shrunk_pool_equals_full_pool(cuda_device):
     """Reference invariant (scripts/test_mul_mat_id_shrink.cpp:71-137): the FFN over a shrunk
     slot pool with remapped ids equals the FFN over the full expert tensor with real ids.
-    Our kernels are deterministic, so the outputs must be identical bit for bit."""
+    Each expert's tiles are computed whole by one CTA and summed in a fixed order, so the
+    outputs must be identical bit for bit."""
     H, I, E, S = 2048, 512, 64, 16
     full = random_experts("nvfp4", E, H, I, seed=9)
     real = np.array([[29, 10, 5, 2, 19, 63, 50, 17]], np.int32)  # 8 routed experts, 1 token
