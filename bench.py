@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
+    ap.add_argument("--prefill-tokens", type=int, default=4096,
+                    help="also time one prefill layer of this many tokens (0: skip)")
     return ap.parse_args()
 
 
@@ -284,7 +286,51 @@ def run_nvmoe(a, rank, world, local_rank):
                       "misses_last_layer_step": misses_last},
         "clocks": clocks,
     }
+    if a.prefill_tokens > 0:
+        line["prefill"] = run_prefill(a, dev, peaks)
     return line
+
+
+def run_prefill(a, dev, peaks):
+    """One Qwen3.8-shaped NVFP4 MoE layer over a.prefill_tokens bf16 tokens (the prefill
+    config: 512 experts all resident, top-10 Zipf routing, shared expert) through
+    nvmoe_moe_ffn_prefill; device time per layer with CUDA events over 10 launches."""
+    import numpy as np
+    import torch
+
+    from nvmoe_b200 import ops
+    from nvmoe_b200.formats import random_experts
+    from nvmoe_b200.synth import layer_log_bias, router_logits
+    from nvmoe_b200.engine import StackConfig
+
+    cfg = StackConfig(n_layers=1)
+    T, E, k, H, I = a.prefill_tokens, cfg.n_experts, cfg.top_k, cfg.hidden, cfg.inter
+    pool = random_experts("nvfp4", E, H, I, seed=11, device=dev)
+    shared = random_experts("nvfp4", 1, H, I, seed=12, device=dev)
+    rng = np.random.default_rng(7)
+    lg = torch.from_numpy(router_logits(T, layer_log_bias(1, E, 1.1, seed=0)[0], rng)).to(dev)
+    ids, w = ops.router_topk(lg, k)
+    x = torch.randn((T, H), device=dev).to(torch.bfloat16)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        ops.moe_ffn_prefill(pool, x, ids, w, shared=shared, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 10
+    e0.record()
+    for _ in range(n):
+        ops.moe_ffn_prefill(pool, x, ids, w, shared=shared, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    flop = 6.0 * T * (k + 1) * H * I
+    tf = flop / (ms / 1e3) / 1e12
+    bf16 = peaks["bf16_tflops"] if peaks else 1590.0
+    del pool, shared
+    return {"tokens": T, "ms_per_layer": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
+            "algorithmic_tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / bf16, 4),
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback",
+            "kernel": "tcgen05 kind::f16 grouped GEMM, weights dequantised into tensor memory"}
 
 
 def _traffic_from_profiles():

@@ -207,11 +207,15 @@ int nvmoe_moe_ffn_path(const nvmoe_ffn_args* args);
 int nvmoe_moe_ffn_noalloc(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
 
 /* R10 — the same FFN for large batches (prefill, ~1k tokens and up): entries sorted by slot into
- * tiles of 128, each expert's gate/up and down as tcgen05 MMAs with the weights dequantised into
- * tensor memory (NVFP4 pools).  Replaces the narrowed-union prefill's _expert_gemm call
- * (nvme_offload_cache.py:1957-2013) and mul_mat_id for n_tokens > 1 (moe_cache_probe.cpp:1668-1684).
- * Same arguments and result as nvmoe_moe_ffn; workspace >= nvmoe_moe_ffn_prefill_workspace_size
- * (it holds the sorted activations, h and the per-entry outputs: about n_tok*(k+1)*(6H+2I) bytes). */
+ * tiles, each expert's gate/up and down as tcgen05 grouped GEMMs (NVFP4 pools).  Default kernel:
+ * block-scaled FP4 MMAs (kind::mxf4nvf4) on the slot banks' codes and scales as stored, the
+ * activations as 4 NVFP4 residual terms, tiles of 32 entries (H a multiple of 512, I of 256 up
+ * to 1536); NVMOE_PREFILL_KERNEL=f16 (or other shapes) selects kind::f16 MMAs on weights
+ * dequantised into tensor memory, tiles of 128.  Replaces the narrowed-union prefill's
+ * _expert_gemm call (nvme_offload_cache.py:1957-2013) and mul_mat_id for n_tokens > 1
+ * (moe_cache_probe.cpp:1668-1684).  Same arguments and result as nvmoe_moe_ffn; workspace >=
+ * nvmoe_moe_ffn_prefill_workspace_size (the sorted activation images, h and the per-entry
+ * outputs: about n_tok*(k+1)*(11H/4+6.5I) bytes on the FP4 path). */
 size_t nvmoe_moe_ffn_prefill_workspace_size(int n_tok, int top_k, int hidden, int inter,
                                             int n_slots);
 int nvmoe_moe_ffn_prefill(const nvmoe_ffn_args* args, nvmoe_stream_t stream);

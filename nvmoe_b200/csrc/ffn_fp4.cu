@@ -55,6 +55,7 @@
 #include "common.cuh"
 #include "ffn_common.cuh"
 #include "umma.cuh"
+#include "fp4_common.cuh"
 
 namespace nvmoe {
 namespace {
@@ -99,131 +100,13 @@ struct __align__(64) Fp4Params {
     CUtensorMap map[12];  // [pool][gate codes, gate scales, up codes, up scales, down ...]
     FfnParams P;
 };
-enum { M_GATE = 0, M_GATE_SF = 1, M_UP = 2, M_UP_SF = 3, M_DOWN = 4, M_DOWN_SF = 5 };
 
-// ------------------------------------------------------------------ device helpers
-__device__ __forceinline__ int ld_acquire(const int* p) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_release_add(int* p, int v) {
-    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_global() {
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
-                                            uint64_t* bar, uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
-        : "memory");
-}
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-
-// Bounded waits that also stop when another role of the CTA has given up (abort flag).
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
-        if (mbar_test_wait(bar, parity)) return true;
-        if ((i & 63) == 63 && *abort) return false;
-        if (i > 32) __nanosleep(i < 1024 ? 20 : 200);
-    }
-    *abort = 1;
-    return false;
-}
-__device__ __forceinline__ bool wait_count(const int* p, int target, volatile int* abort) {
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
-        if (ld_acquire(p) >= target) return true;
-        if ((i & 63) == 63 && *abort) return false;
-        if (i > 16) __nanosleep(i < 1024 ? 32 : 200);
-    }
-    *abort = 1;
-    return false;
-}
 __device__ __forceinline__ void report_timeout(const FfnParams& P) {
     atomicExch(wsp<int>(P, P.L.hdr) + HDR_STATUS, NVMOE_ERR_TIMEOUT);
     if (P.status) atomicExch(P.status, NVMOE_ERR_TIMEOUT);
 }
 
-// ---- activation quantisation: 16 values -> kFp4Terms x (8 bytes E2M1, 1 byte UE4M3)
-__device__ __forceinline__ uint32_t e4m3_code(float v) {
-    uint16_t r;
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(v));
-    return r & 0xffu;
-}
-__device__ __forceinline__ float e4m3_value(uint32_t code) {
-    const uint32_t h2 = e4m3x2_to_f16x2((uint16_t)code);
-    return __half2float(__ushort_as_half((uint16_t)(h2 & 0xffffu)));
-}
-// Byte offsets inside one stage of an operand image (npad rows): row n's 128 code bytes in the
-// 128-byte swizzle (16-byte chunk c stored at chunk c ^ (n % 8)), then the rows' 16 scale bytes.
-__device__ __forceinline__ int img_code_off(int n, int blk) {
-    return n * 128 + ((((blk >> 1) ^ (n & 7))) << 4) + ((blk & 1) << 3);
-}
-__device__ __forceinline__ int img_sf_off(int npad, int n, int blk) {
-    return npad * 128 + n * 16 + blk;
-}
-// Four consecutive lanes (q = lane & 3) quantise one 16-block, 4 values each: per term, the
-// block maximum over the 4 lanes, a UE4M3 scale rounded up so the block fits, E2M1
-// round-to-nearest of the residual.  The block's kFp4Terms rows go to a group image (npad > 0:
-// row 4 i + t of the stage, 128-byte swizzle) or to a token image (npad = 0: term row t of the
-// stage's 512-byte row block, stored in both swizzle phases a token can take in a group (even
-// or odd position), and the scales at byte offset i).  Each lane writes its 2 code bytes per
-// term, lane q = 0 the scale bytes.  Called by all 32 lanes of the warp together; lanes
-// without a block pass active = false.
-__device__ __forceinline__ void quant4_put(float (&v)[4], int ke, bool active, uint8_t* img,
-                                           int npad, int i, int blk) {
-    const int q = threadIdx.x & 3;
-#pragma unroll
-    for (int t = 0; t < kFp4Terms; ++t) {
-        float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-        const float target = am * (1.0f / 6.0f) * fp4_exp2(ke + 2 * t);
-        uint32_t sc = e4m3_code(target);
-        float sv = e4m3_value(sc);
-        if (sv < target && sc < 0x7eu) sv = e4m3_value(++sc);  // round the scale up
-        const float s = sv * fp4_exp2(-(ke + 2 * t));
-        const float inv = s > 0.f ? 1.0f / s : 0.f;
-        uint16_t two;
-        asm("{ .reg .b8 b0, b1;\n\t"
-            "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
-            "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
-            "mov.b16 %0, {b0, b1}; }"
-            : "=h"(two)
-            : "f"(v[0] * inv), "f"(v[1] * inv), "f"(v[2] * inv), "f"(v[3] * inv));
-        const uint32_t lo = e2m1x2_to_f16x2(two & 0xffu), hi = e2m1x2_to_f16x2(two >> 8);
-        const float2 d01 = __half22float2(*reinterpret_cast<const __half2*>(&lo));
-        const float2 d23 = __half22float2(*reinterpret_cast<const __half2*>(&hi));
-        v[0] = fmaf(-d01.x, s, v[0]);
-        v[1] = fmaf(-d01.y, s, v[1]);
-        v[2] = fmaf(-d23.x, s, v[2]);
-        v[3] = fmaf(-d23.y, s, v[3]);
-        if (active) {
-            if (npad > 0) {  // a group image: row n = 4 i + t
-                const int n = kFp4Terms * i + t;
-                *reinterpret_cast<uint16_t*>(img + img_code_off(n, blk) + 2 * q) = two;
-                if (q == 0) img[img_sf_off(npad, n, blk)] = (uint8_t)sc;
-            } else {  // a token image: term row t in both swizzle phases, then the scales
-                const int off = ((blk & 1) << 3) + 2 * q;
-                *reinterpret_cast<uint16_t*>(img + t * 128 + ((((blk >> 1) ^ t)) << 4) + off) = two;
-                *reinterpret_cast<uint16_t*>(img + 512 + t * 128 + ((((blk >> 1) ^ (4 + t))) << 4) + off) = two;
-                if (q == 0) img[i + t * 16 + blk] = (uint8_t)sc;  // i = the scales' offset
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ int npad_of(int nt) { return (kFp4Terms * nt + 7) & ~7; }
-
-// Contiguous per-CTA ranges of S items over G CTAs (S * (G + 1) < 2^32: 32-bit division).
-__device__ __forceinline__ int range_lo(int S, int c, int G) {
-    return (int)((uint32_t)c * (uint32_t)S / (uint32_t)G);
-}
+using namespace fp4;
 
 struct Smem {
     uint8_t* base;
@@ -836,7 +719,9 @@ bool bank_map(CUtensorMap* out, const void* base, uint64_t row_bytes, uint64_t r
     return true;
 }
 
-bool pool_maps(const nvmoe_expert_pool& p, CUtensorMap* m) {
+}  // namespace
+
+bool fp4_pool_maps(const nvmoe_expert_pool& p, CUtensorMap* m) {
     const int H = p.hidden, I = p.inter;
     const uint64_t S = (uint64_t)p.n_slots;
     return bank_map(m + M_GATE, p.gate.data, H / 2, I, S, p.gate.row_stride, p.gate.slot_stride,
@@ -853,7 +738,6 @@ bool pool_maps(const nvmoe_expert_pool& p, CUtensorMap* m) {
                     p.down.scale_slot_stride, 16, 128, false);
 }
 
-}  // namespace
 
 // Whether a call runs on the FP4 tensor-core kernel (decided in ffn_setup, so the kernels
 // before it know whether to write the f16 token copy): NVFP4 pools whose shapes it covers, when
@@ -874,8 +758,8 @@ bool ffn_fp4_eligible(const FfnParams& P) {
     const char* env = std::getenv("NVMOE_FFN_KERNEL");
     if (!env || std::strcmp(env, "fp4") != 0) return false;
     CUtensorMap m[6];
-    if (!pool_maps(P.pool, m)) return false;
-    if (P.has_shared && !pool_maps(P.shared, m)) return false;
+    if (!fp4_pool_maps(P.pool, m)) return false;
+    if (P.has_shared && !fp4_pool_maps(P.shared, m)) return false;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -888,8 +772,8 @@ int ffn_fp4_launch(const FfnParams& P, cudaStream_t st) {
     Fp4Params A;
     std::memset(&A, 0, sizeof(A));
     A.P = P;
-    if (!pool_maps(P.pool, A.map)) return NVMOE_ERR_UNSUPPORTED;
-    if (!pool_maps(P.has_shared ? P.shared : P.pool, A.map + 6)) return NVMOE_ERR_UNSUPPORTED;
+    if (!fp4_pool_maps(P.pool, A.map)) return NVMOE_ERR_UNSUPPORTED;
+    if (!fp4_pool_maps(P.has_shared ? P.shared : P.pool, A.map + 6)) return NVMOE_ERR_UNSUPPORTED;
     int dev = 0, sms = 0;
     NVMOE_CUDA_TRY(cudaGetDevice(&dev));
     NVMOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

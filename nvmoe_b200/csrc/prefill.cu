@@ -25,6 +25,8 @@
 #include "ffn_common.cuh"
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 namespace nvmoe {
 namespace {
@@ -566,11 +568,27 @@ bool pf_pool_ok(const nvmoe_expert_pool& p, int H, int I) {
 }
 
 }  // namespace
+
+bool prefill_fp4_ok(const nvmoe_ffn_args* a);
+size_t prefill_fp4_workspace(int n_tok, int top_k, int H, int I, int n_slots);
+int prefill_fp4_run(const nvmoe_ffn_args* a, cudaStream_t st);
+
+// The block-scaled FP4 path (prefill_fp4.cu) runs when the shapes suit it, unless the
+// environment variable NVMOE_PREFILL_KERNEL is "f16" (this file's kind::f16 path).
+bool prefill_use_fp4(const nvmoe_ffn_args* a) {
+    const char* env = std::getenv("NVMOE_PREFILL_KERNEL");
+    return !(env && std::strcmp(env, "f16") == 0) && prefill_fp4_ok(a);
+}
+
 }  // namespace nvmoe
 
 extern "C" size_t nvmoe_moe_ffn_prefill_workspace_size(int n_tok, int top_k, int hidden, int inter,
                                                         int n_slots) {
-    return nvmoe::pf_layout(std::max(n_tok, 1), top_k, hidden, inter, n_slots).total;
+    const size_t f16 = nvmoe::pf_layout(std::max(n_tok, 1), top_k, hidden, inter, n_slots).total;
+    const size_t fp4 = (hidden % 512 == 0 && inter % 256 == 0)
+                           ? nvmoe::prefill_fp4_workspace(n_tok, top_k, hidden, inter, n_slots)
+                           : 0;
+    return std::max(f16, fp4);
 }
 
 extern "C" int nvmoe_moe_ffn_prefill(const nvmoe_ffn_args* a, nvmoe_stream_t stream) {
@@ -589,6 +607,7 @@ extern "C" int nvmoe_moe_ffn_prefill(const nvmoe_ffn_args* a, nvmoe_stream_t str
         (reinterpret_cast<uintptr_t>(a->y) & 7))
         return NVMOE_ERR_INVALID_ARG;
     if (a->n_tok == 0) return NVMOE_OK;
+    if (prefill_use_fp4(a)) return prefill_fp4_run(a, (cudaStream_t)stream);
     PfParams P{};
     P.pool = pool;
     P.has_shared = a->shared ? 1 : 0;

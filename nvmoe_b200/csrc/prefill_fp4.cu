@@ -1,0 +1,639 @@
+// R10 prefill on the block-scaled FP4 tensor cores: the routed-expert FFN for large batches as a
+// token-sorted grouped GEMM of tcgen05.mma kind::mxf4nvf4 (E2M1 x E2M1, one UE4M3 scale per 16
+// on both operands, fp32 accumulators in tensor memory).  The weights go from the slot banks to
+// shared memory by TMA (128-byte swizzle) and into the MMA unchanged; the activations enter as
+// kFp4Terms NVFP4 residual terms per row (the quantiser and layout of fp4_common.cuh), so the
+// result matches the f16 path and the oracle within the FFN tolerance.
+//
+// Same contract as nvmoe_moe_ffn_prefill's f16 path (nvme_offload_cache.py:1957-2013; llama.cpp
+// mul_mat_id for n_tokens > 1, scripts/moe_cache_probe.cpp:1668-1684):
+//   y[t] = sum_j w[t,j] * down_s( silu(gate_s x[t]) * up_s x[t] )  (+ the shared expert).
+// Steps (one stream, kernel boundaries order them):
+//   count / scan / scatter — entries sorted by key (slot, or the shared expert), tiles of <= 32
+//                            entries per key, each entry's (tile, row)
+//   quant_x  — per token: the row exponent, the shared gate, then each 16-block as 4 NVFP4 terms
+//              into the gate_up B image of every tile row that holds the token
+//   gate_up  — persistent: units (tile, 64-row j-block), M = 64 gate + 64 up rows, N = 4 x
+//              entries, K = H; epilogue h = silu(gate) * up (fp32)
+//   act      — per entry: h row exponent, its 16-blocks as NVFP4 terms into the down B image
+//   down     — persistent: units (tile, 128-row block of H), K = I; epilogue y_part[e] = w_e *
+//              row (fp32)
+//   combine  — y[t] = sum over t's entries in the order j = 0..k (shared last) (bf16)
+// Deterministic: every output element is one MMA accumulation and fixed-order sums.
+#include "common.cuh"
+#include "ffn_common.cuh"
+#include "fp4_common.cuh"
+#include "umma.cuh"
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+namespace nvmoe {
+using namespace fp4;
+namespace {
+
+constexpr int kTT = 32;                    // entries per tile: B rows 4 x 32 = 128
+constexpr int kImg = 128 * 144;            // one K stage of a tile image (128 code rows + scales)
+constexpr int kNSt = 5;                    // ring stages
+constexpr int kOffBi = 16384;              // A codes [0, 16 KB), B image, A scales
+constexpr int kOffAs = kOffBi + kImg;
+constexpr int kStg = 36864;                // 1024-aligned stage
+static_assert(kOffAs + 2048 <= kStg && kStg % 1024 == 0, "stage layout");
+constexpr int kGThreads = 320;             // 10 warps
+constexpr int kOffBar = kNSt * kStg;       // mbarriers
+constexpr int kOffMisc = kOffBar + 32 * 8; // tmem base, abort
+constexpr int kOffEnt = kOffMisc + 64;     // per-entry factors of the unit [2][kTT]
+constexpr int kOffXb = kOffEnt + 2 * 4 * kTT;  // up values [64 rows][kTT] fp32
+constexpr int kGSmem = kOffXb + 64 * kTT * 4 + 1024;
+constexpr uint32_t kTmD = 0, kTmSFA = 256, kTmSFB = 256 + 16 * kNSt, kTmCols = 512;
+static_assert(kTmSFB + 16 * kNSt <= kTmCols, "tensor memory");
+
+enum { QH_N_TILES = 0, QH_N_ENT = 1, QH_STATUS = 2 };
+
+struct Pf4Layout {
+    size_t hdr, cnt, base, cursor, tile_base, tiles, ent_tok, ent_w, ent_of, ent_pos, sg, xk, hk,
+        ximg, himg, h32, ypart, total;
+    int n_keys, n_ent_max, max_tiles, ksg, ksd;
+};
+
+__host__ __device__ inline Pf4Layout pf4_layout(int n_tok, int top_k, int H, int I, int n_slots) {
+    Pf4Layout L;
+    L.n_keys = n_slots + 1;  // the shared expert is key n_slots
+    L.n_ent_max = n_tok * (top_k + 1);
+    L.max_tiles = (L.n_ent_max + kTT - 1) / kTT + std::min(L.n_keys, L.n_ent_max);
+    L.ksg = H / 256;
+    L.ksd = I / 256;
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes, 1024);
+        return at;
+    };
+    L.hdr = take(64);
+    L.cnt = take(4 * (size_t)L.n_keys);
+    L.base = take(4 * (size_t)L.n_keys);
+    L.cursor = take(4 * (size_t)L.n_keys);
+    L.tile_base = take(4 * (size_t)L.n_keys);
+    L.tiles = take(12 * (size_t)L.max_tiles);  // {key, entry base, rows}
+    L.ent_tok = take(4 * (size_t)L.n_ent_max);
+    L.ent_w = take(4 * (size_t)L.n_ent_max);
+    L.ent_of = take(4 * (size_t)L.n_ent_max);
+    L.ent_pos = take(4 * (size_t)L.n_ent_max);  // tile << 8 | row
+    L.sg = take(4 * (size_t)n_tok);
+    L.xk = take(4 * (size_t)n_tok);
+    L.hk = take(4 * (size_t)L.n_ent_max);
+    L.ximg = take((size_t)L.max_tiles * L.ksg * kImg);
+    L.himg = take((size_t)L.max_tiles * L.ksd * kImg);
+    L.h32 = take(4 * (size_t)L.n_ent_max * I);
+    L.ypart = take(4 * (size_t)L.n_ent_max * H);
+    L.total = o;
+    return L;
+}
+
+struct __align__(64) Pf4Params {
+    CUtensorMap map[12];  // [routed pool, shared pool][the six maps of fp4_pool_maps]
+    nvmoe_expert_pool pool, shared;
+    int has_shared;
+    const uint16_t* shared_gate;
+    const uint16_t* x;
+    int64_t x_stride;
+    const int32_t* ids;
+    int64_t ids_stride;
+    const float* w;
+    int64_t w_stride;
+    int top_k, n_tok;
+    uint16_t* y;
+    int64_t y_stride;
+    unsigned char* ws;
+    Pf4Layout L;
+    int32_t* status;
+};
+
+template <typename T>
+__device__ __forceinline__ T* qws(const Pf4Params& P, size_t off) {
+    return reinterpret_cast<T*>(P.ws + off);
+}
+
+// ------------------------------------------------------------------ grouping
+__global__ void pf4_count(const __grid_constant__ Pf4Params P) {
+    const int n = P.n_tok * P.top_k, S = P.pool.n_slots;
+    int* cnt = qws<int>(P, P.L.cnt);
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+        const int t = p / P.top_k, j = p - t * P.top_k;
+        const int s = P.ids[(int64_t)t * P.ids_stride + j];
+        if (s >= 0 && s < S)
+            atomicAdd(&cnt[s], 1);
+        else
+            atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_BAD_SLOT);
+    }
+}
+
+// One block: entry bases (exclusive scan over keys) and the tile list.
+__global__ void __launch_bounds__(1024) pf4_scan(const __grid_constant__ Pf4Params P) {
+    __shared__ int warp_sums[33];
+    const int K = P.L.n_keys, S = P.pool.n_slots, tid = threadIdx.x;
+    int* cnt = qws<int>(P, P.L.cnt);
+    int* base = qws<int>(P, P.L.base);
+    int* cursor = qws<int>(P, P.L.cursor);
+    int* tile_base = qws<int>(P, P.L.tile_base);
+    int* tiles = qws<int>(P, P.L.tiles);
+    if (tid == 0) cnt[S] = P.has_shared ? P.n_tok : 0;
+    __syncthreads();
+    int run_e = 0, run_t = 0;
+    for (int b0 = 0; b0 < K; b0 += blockDim.x) {
+        const int s = b0 + tid;
+        const int c = s < K ? cnt[s] : 0;
+        const int nt = (c + kTT - 1) / kTT;
+        int tot_e, tot_t;
+        const int re = block_exclusive_scan(c, warp_sums, &tot_e);
+        const int rt = block_exclusive_scan(nt, warp_sums, &tot_t);
+        if (s < K) {
+            base[s] = run_e + re;
+            cursor[s] = run_e + re;
+            tile_base[s] = run_t + rt;
+            for (int i = 0; i < nt; ++i) {
+                int* tl = tiles + 3 * (run_t + rt + i);
+                tl[0] = s;
+                tl[1] = run_e + re + i * kTT;
+                tl[2] = min(kTT, c - i * kTT);
+            }
+        }
+        run_e += tot_e;
+        run_t += tot_t;
+    }
+    if (tid == 0) {
+        int* hdr = qws<int>(P, P.L.hdr);
+        hdr[QH_N_TILES] = run_t;
+        hdr[QH_N_ENT] = run_e;
+    }
+}
+
+__global__ void pf4_scatter(const __grid_constant__ Pf4Params P) {
+    const int S = P.pool.n_slots, K1 = P.top_k + 1;
+    int* cursor = qws<int>(P, P.L.cursor);
+    const int* base = qws<int>(P, P.L.base);
+    const int* tile_base = qws<int>(P, P.L.tile_base);
+    int* ent_tok = qws<int>(P, P.L.ent_tok);
+    float* ent_w = qws<float>(P, P.L.ent_w);
+    int* ent_of = qws<int>(P, P.L.ent_of);
+    int* ent_pos = qws<int>(P, P.L.ent_pos);
+    const int n = P.n_tok * K1;
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+        const int t = p / K1, j = p - t * K1;
+        int e = -1, key = -1;
+        if (j < P.top_k) {
+            const int s = P.ids[(int64_t)t * P.ids_stride + j];
+            if (s >= 0 && s < S) {
+                e = atomicAdd(&cursor[s], 1);  // order inside a key does not change any result
+                key = s;
+                ent_tok[e] = t;
+                ent_w[e] = P.w[(int64_t)t * P.w_stride + j];
+            }
+        } else if (P.has_shared) {
+            e = base[S] + t;
+            key = S;
+            ent_tok[e] = t;
+            ent_w[e] = 1.0f;
+        }
+        if (e >= 0) {
+            const int r = e - base[key];
+            ent_pos[e] = ((tile_base[key] + r / kTT) << 8) | (r % kTT);
+        }
+        ent_of[p] = e;
+    }
+}
+
+// One block of 128 threads per token: the row exponent and the shared gate, then its 16-blocks
+// as NVFP4 terms (4 lanes per block, 32 blocks per round) into the gate_up image row of every
+// entry of the token.
+__global__ void __launch_bounds__(128) pf4_quant_x(const __grid_constant__ Pf4Params P) {
+    __shared__ float red[8];
+    __shared__ int ents[33];  // top-k (<= 32) + the shared expert
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int H = P.pool.hidden, K1 = P.top_k + 1, KSG = P.L.ksg;
+    const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
+    if (tid < K1) ents[tid] = qws<int>(P, P.L.ent_of)[t * K1 + tid];
+    float am = 0.f, dot = 0.f;
+    for (int i = tid * 8; i < H; i += 128 * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+        const uint16_t* u = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float f = bf16_bits_to_f32(u[k]);
+            am = fmaxf(am, fabsf(f));
+            if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    }
+    if (lane == 0) red[warp] = am, red[4 + warp] = dot;
+    __syncthreads();
+    const int ke = fp4_row_exp(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])));
+    if (tid == 0) {
+        qws<int>(P, P.L.xk)[t] = ke;
+        if (P.shared_gate)
+            qws<float>(P, P.L.sg)[t] = 1.0f / (1.0f + expf(-(red[4] + red[5] + red[6] + red[7])));
+    }
+    const int* ent_pos = qws<int>(P, P.L.ent_pos);
+    uint8_t* ximg = P.ws + P.L.ximg;
+    for (int b0 = 0; b0 < H / 16; b0 += 32) {
+        const int b = b0 + (tid >> 2), q = tid & 3;  // H / 16 is a multiple of 32 (H % 512 == 0)
+        const uint2 xv = *reinterpret_cast<const uint2*>(xr + b * 16 + 4 * q);
+        float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u),
+                      __uint_as_float(xv.y << 16), __uint_as_float(xv.y & 0xffff0000u)};
+        uint16_t two[kFp4Terms];
+        uint8_t sc[kFp4Terms];
+        quant4_terms(v, ke, two, sc);
+        for (int j = 0; j < K1; ++j) {
+            const int e = ents[j];
+            if (e < 0) continue;
+            const int pos = ent_pos[e];
+            uint8_t* img = ximg + ((int64_t)(pos >> 8) * KSG + b / 16) * kImg;
+            put4(img, 128, pos & 0xff, b % 16, two, sc);
+        }
+    }
+}
+
+// One block of 128 threads per entry: the h row's exponent, then its 16-blocks as NVFP4 terms
+// into the entry's row of the down image (thread tid: values 4 tid + 512 m .. + 4).
+__global__ void __launch_bounds__(128) pf4_act(const __grid_constant__ Pf4Params P) {
+    __shared__ float red[4];
+    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (e >= qws<int>(P, P.L.hdr)[QH_N_ENT]) return;
+    const int I = P.pool.inter, KSD = P.L.ksd, MC = (I + 511) / 512;
+    const float* hrow = qws<float>(P, P.L.h32) + (int64_t)e * I;
+    float4 hv[3];  // I <= 1536
+    float am = 0.f;
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+        hv[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m < MC && 4 * tid + 512 * m < I) hv[m] = *reinterpret_cast<const float4*>(hrow + 512 * m + 4 * tid);
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(hv[m].x), fabsf(hv[m].y)), fmaxf(fabsf(hv[m].z), fabsf(hv[m].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (lane == 0) red[warp] = am;
+    __syncthreads();
+    const int kh = fp4_row_exp(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])));
+    if (tid == 0) qws<int>(P, P.L.hk)[e] = kh;
+    const int pos = qws<int>(P, P.L.ent_pos)[e];
+    uint8_t* himg = P.ws + P.L.himg;
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+        if (m >= MC) break;
+        const bool valid = 4 * tid + 512 * m < I;
+        const int blk = valid ? (tid >> 2) + 32 * m : 0;
+        float v[4] = {hv[m].x, hv[m].y, hv[m].z, hv[m].w};
+        uint16_t two[kFp4Terms];
+        uint8_t sc[kFp4Terms];
+        quant4_terms(v, kh, two, sc);
+        if (valid) {
+            uint8_t* img = himg + ((int64_t)(pos >> 8) * KSD + blk / 16) * kImg;
+            put4(img, 128, pos & 0xff, blk % 16, two, sc);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ the grouped GEMMs
+// Persistent, one CTA per SM; units dealt round-robin (u = c, c + G, ...).  PH = 0: gate_up
+// units (tile, j-block of 64), PH = 1: down units (tile, 128 rows of H).  Warps 0-3 epilogue
+// (TMEM lane quadrants), 4-7 scale factors, 8 producer (TMA weights + the tile's B image
+// stage), 9 MMA issuer.
+template <int PH>
+__global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__ Pf4Params P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* sf_full = full + kNSt;
+    uint64_t* empty = full + 2 * kNSt;
+    uint64_t* d_full = full + 3 * kNSt;
+    uint64_t* d_empty = d_full + 2;
+    uint32_t* tmem_p = reinterpret_cast<uint32_t*>(sm + kOffMisc);
+    volatile int* abort = reinterpret_cast<int*>(sm + kOffMisc) + 1;
+    float* efac = reinterpret_cast<float*>(sm + kOffEnt);         // [kTT] per-entry factor
+    int* eexp = reinterpret_cast<int*>(sm + kOffEnt) + kTT;        // [kTT] per-entry exponent
+    float* xbuf = reinterpret_cast<float*>(sm + kOffXb);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x, G = gridDim.x;
+    const int H = P.pool.hidden, I = P.pool.inter, S = P.pool.n_slots;
+    const int UPT = PH ? H / 128 : I / 64;         // units per tile
+    const int KS = PH ? P.L.ksd : P.L.ksg;         // K stages per unit
+
+    if (tid == 0) {
+        for (int s = 0; s < kNSt; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&sf_full[s], 4);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&d_full[b], 1);
+            mbar_init(&d_empty[b], 4);
+        }
+        *abort = 0;
+        mbar_init_fence();
+    }
+    if (warp == 9) umma::tmem_alloc(tmem_p, kTmCols);
+    if (warp == 8 && lane < 12) prefetch_map(&P.map[lane]);
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tm = *tmem_p;
+
+    const int n_tiles = qws<int>(P, P.L.hdr)[QH_N_TILES];
+    const int* tiles = qws<int>(P, P.L.tiles);
+    const int n_units = n_tiles * UPT;
+    const int my_units = n_units > c ? (n_units - 1 - c) / G + 1 : 0;
+    const uint8_t* img = P.ws + (PH ? P.L.himg : P.L.ximg);
+    bool ok = true;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            int it = 0;
+            for (int k = 0; k < my_units && ok; ++k) {
+                const int u = c + k * G, tile = u / UPT, sub = u - tile * UPT;
+                const int key = tiles[3 * tile];
+                const bool sh = key == S;
+                const int slot = sh ? 0 : key;
+                const CUtensorMap* m = P.map + (sh ? 6 : 0);
+                for (int ks = 0; ks < KS; ++ks, ++it) {
+                    const int s = it % kNSt;
+                    if (it >= kNSt && !wait_bar(&empty[s], ((it / kNSt) + 1) & 1, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = sm + s * kStg;
+                    mbar_arrive_expect_tx(&full[s], 16384 + 2048 + kImg);
+                    if (PH == 0) {
+                        tma_load_3d(st, m + M_GATE, ks * 128, sub * 64, slot, &full[s], pol);
+                        tma_load_3d(st + 8192, m + M_UP, ks * 128, sub * 64, slot, &full[s], pol);
+                        tma_load_3d(st + kOffAs, m + M_GATE_SF, ks * 16, sub * 64, slot, &full[s], pol);
+                        tma_load_3d(st + kOffAs + 1024, m + M_UP_SF, ks * 16, sub * 64, slot, &full[s], pol);
+                    } else {
+                        tma_load_3d(st, m + M_DOWN, ks * 128, sub * 128, slot, &full[s], pol);
+                        tma_load_3d(st + kOffAs, m + M_DOWN_SF, ks * 16, sub * 128, slot, &full[s], pol);
+                    }
+                    bulk_g2s(st + kOffBi, img + ((int64_t)tile * KS + ks) * kImg, kImg, &full[s]);
+                }
+            }
+            if (!ok) {
+                for (int k = std::max(0, it - kNSt); k < it; ++k)
+                    mbar_wait_bounded(&full[k % kNSt], (k / kNSt) & 1, 1u << 16);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 9) {
+        int it = 0;
+        for (int k = 0; k < my_units && ok; ++k) {
+            const int u = c + k * G, tile = u / UPT;
+            const int nr = tiles[3 * tile + 2];
+            const uint32_t idesc = umma::idesc_mxf4(128, npad_of(nr));
+            const int db = k & 1;
+            if (k >= 2 && !wait_bar(&d_empty[db], ((k >> 1) + 1) & 1, abort)) {
+                ok = false;
+                break;
+            }
+            umma::fence_after_sync();
+            for (int ks = 0; ks < KS; ++ks, ++it) {
+                const int s = it % kNSt;
+                if (!wait_bar(&sf_full[s], (it / kNSt) & 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                umma::fence_after_sync();
+                if (lane == 0) {
+                    const uint32_t sa = smem_u32(sm + s * kStg);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        umma::mma_mxf4(tm + kTmD + db * 128, umma::smem_desc_sw128(sa + 32 * i),
+                                       umma::smem_desc_sw128(sa + kOffBi + 32 * i), idesc,
+                                       tm + kTmSFA + s * 16 + 4 * i, tm + kTmSFB + s * 16 + 4 * i,
+                                       (ks == 0 && i == 0) ? 0u : 1u);
+                    umma::commit(&empty[s]);
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (lane == 0) umma::commit(&d_full[db]);
+            __syncwarp();
+        }
+    } else if (warp >= 4) {
+        // scale factors: A (weights) and B (image rows), 128 rows each -> column 4 i + r / 32,
+        // lane r % 32 of every quadrant
+        const int qd = warp - 4;
+        int it = 0;
+        for (int k = 0; k < my_units && ok; ++k) {
+            for (int ks = 0; ks < KS; ++ks, ++it) {
+                const int s = it % kNSt;
+                if (!wait_bar(&full[s], (it / kNSt) & 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* st = sm + s * kStg;
+                uint32_t va[16], vb[16];
+#pragma unroll
+                for (int m1 = 0; m1 < 4; ++m1) {
+                    const uint4 a = *reinterpret_cast<const uint4*>(st + kOffAs + (32 * m1 + lane) * 16);
+                    const uint4 b = *reinterpret_cast<const uint4*>(st + kOffBi + 128 * 128 + (32 * m1 + lane) * 16);
+                    va[m1] = a.x, va[4 + m1] = a.y, va[8 + m1] = a.z, va[12 + m1] = a.w;
+                    vb[m1] = b.x, vb[4 + m1] = b.y, vb[8 + m1] = b.z, vb[12 + m1] = b.w;
+                }
+                umma::st_x16(tm + ((uint32_t)(qd * 32) << 16) + kTmSFA + s * 16, va);
+                umma::st_x16(tm + ((uint32_t)(qd * 32) << 16) + kTmSFB + s * 16, vb);
+                umma::wait_st();
+                umma::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sf_full[s]);
+            }
+        }
+    } else {
+        // epilogue: row r of the unit's D (a weight row), one column group of 4 per entry
+        const int r = tid;
+        const int* ent_tok = qws<int>(P, P.L.ent_tok);
+        const float* ent_w = qws<float>(P, P.L.ent_w);
+        const int* xk = qws<int>(P, P.L.xk);
+        const int* hk = qws<int>(P, P.L.hk);
+        const float* sgv = P.shared_gate ? qws<float>(P, P.L.sg) : nullptr;
+        float* h32 = qws<float>(P, P.L.h32);
+        float* ypart = qws<float>(P, P.L.ypart);
+        for (int k = 0; k < my_units && ok; ++k) {
+            const int u = c + k * G, tile = u / UPT, sub = u - tile * UPT;
+            const int key = tiles[3 * tile], eb = tiles[3 * tile + 1], nr = tiles[3 * tile + 2];
+            const bool sh = key == S;
+            const nvmoe_expert_pool& pool = sh ? P.shared : P.pool;
+            const int slot = sh ? 0 : key;
+            // per-entry exponent and factor of this unit (loaded while its MMAs run)
+            if (tid < nr) {
+                const int e = eb + tid;
+                if (PH == 0) {
+                    eexp[tid] = xk[ent_tok[e]];
+                } else {
+                    eexp[tid] = hk[e];
+                    float f = ent_w[e] * global_of(pool.down, slot);
+                    if (sh && sgv) f *= sgv[ent_tok[e]];
+                    efac[tid] = f;
+                }
+            }
+            const float gl = PH ? 0.f : global_of(r < 64 ? pool.gate : pool.up, slot);
+            named_bar_sync(1, 128);
+            const int db = k & 1;
+            if (!wait_bar(&d_full[db], (k >> 1) & 1, abort)) {
+                ok = false;
+                break;
+            }
+            umma::fence_after_sync();
+            const int nchunk = (4 * nr + 15) / 16;  // 4 entries per 16 columns
+            float v[kTT];
+#pragma unroll
+            for (int ch = 0; ch < kTT / 4; ++ch) {
+                if (ch >= nchunk) break;
+                uint32_t d[16];
+                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + db * 128 + 16 * ch), d);
+                umma::wait_ld();
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float a = 0.f;
+#pragma unroll
+                    for (int t = kFp4Terms - 1; t >= 0; --t)
+                        a = fmaf(__uint_as_float(d[kFp4Terms * q + t]), fp4_exp2(-2 * t), a);
+                    v[4 * ch + q] = a;
+                }
+            }
+            umma::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d_empty[db]);
+            if (PH == 0) {
+                // rows 0-63 gate, 64-127 up of j = 64 sub + r % 64
+                if (r >= 64) {
+#pragma unroll
+                    for (int i = 0; i < kTT; ++i)
+                        if (i < nr) xbuf[(r - 64) * kTT + i] = v[i] * fp4_exp2(-eexp[i]) * gl;
+                }
+                named_bar_sync(1, 128);
+                if (r < 64) {
+#pragma unroll
+                    for (int i = 0; i < kTT; ++i)
+                        if (i < nr)
+                            h32[(int64_t)(eb + i) * I + sub * 64 + r] =
+                                silu(v[i] * fp4_exp2(-eexp[i]) * gl) * xbuf[r * kTT + i];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kTT; ++i)
+                    if (i < nr)
+                        ypart[(int64_t)(eb + i) * H + sub * 128 + r] = v[i] * fp4_exp2(-eexp[i]) * efac[i];
+            }
+            named_bar_sync(1, 128);  // eexp / efac / xbuf are rewritten by the next unit
+        }
+    }
+    if (!ok && tid % 32 == 0) atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_TIMEOUT);
+
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 9) {
+        umma::fence_after_sync();
+        umma::tmem_dealloc(tm, kTmCols);
+    }
+}
+
+// y[t] = sum_j y_part[ent_of[t, j]] in the order j = 0..k-1, shared; 4 columns per thread.
+__global__ void pf4_combine(const __grid_constant__ Pf4Params P) {
+    const int H = P.pool.hidden, K1 = P.top_k + 1;
+    const int* ent_of = qws<int>(P, P.L.ent_of);
+    const float* yp = qws<float>(P, P.L.ypart);
+    const int64_t n4 = (int64_t)P.n_tok * (H / 4);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / (H / 4)), cc = (int)(i % (H / 4)) * 4;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < K1; ++j) {
+            const int e = ent_of[t * K1 + j];
+            if (e < 0) continue;
+            const float4 v = *reinterpret_cast<const float4*>(yp + (int64_t)e * H + cc);
+            s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
+        }
+        uint2 o;
+        o.x = (uint32_t)f32_to_bf16_bits(s.x) | ((uint32_t)f32_to_bf16_bits(s.y) << 16);
+        o.y = (uint32_t)f32_to_bf16_bits(s.z) | ((uint32_t)f32_to_bf16_bits(s.w) << 16);
+        *reinterpret_cast<uint2*>(P.y + (int64_t)t * P.y_stride + cc) = o;
+    }
+}
+
+__global__ void pf4_status(const __grid_constant__ Pf4Params P) {
+    if (P.status) *P.status = qws<int>(P, P.L.hdr)[QH_STATUS];
+}
+
+}  // namespace
+
+// Shapes and banks the FP4 prefill covers (NVFP4, H a multiple of 512, I of 256 up to 1536,
+// every bank usable by TMA).
+bool prefill_fp4_ok(const nvmoe_ffn_args* a) {
+    const nvmoe_expert_pool& p = *a->pool;
+    if (p.quant != NVMOE_Q_NVFP4 || p.hidden % 512 != 0 || p.inter % 256 != 0 ||
+        p.inter > 1536 || a->top_k > 32)
+        return false;
+    CUtensorMap m[6];
+    if (!fp4_pool_maps(p, m)) return false;
+    if (a->shared && !fp4_pool_maps(*a->shared, m)) return false;
+    return true;
+}
+
+size_t prefill_fp4_workspace(int n_tok, int top_k, int H, int I, int n_slots) {
+    return pf4_layout(std::max(n_tok, 1), top_k, H, I, n_slots).total;
+}
+
+// Validated arguments (the caller checked pointers, alignment and shapes).
+int prefill_fp4_run(const nvmoe_ffn_args* a, cudaStream_t st) {
+    Pf4Params P;
+    std::memset(&P, 0, sizeof(P));
+    const nvmoe_expert_pool& pool = *a->pool;
+    if (!fp4_pool_maps(pool, P.map)) return NVMOE_ERR_UNSUPPORTED;
+    if (!fp4_pool_maps(a->shared ? *a->shared : pool, P.map + 6)) return NVMOE_ERR_UNSUPPORTED;
+    const int H = pool.hidden, I = pool.inter;
+    P.pool = pool;
+    P.has_shared = a->shared ? 1 : 0;
+    P.shared = a->shared ? *a->shared : pool;
+    P.shared_gate = a->shared ? a->shared_gate : nullptr;
+    P.x = a->x;
+    P.x_stride = a->x_row_stride;
+    P.ids = a->slot_ids;
+    P.ids_stride = a->ids_row_stride;
+    P.w = a->weights;
+    P.w_stride = a->weights_row_stride;
+    P.top_k = a->top_k;
+    P.n_tok = a->n_tok;
+    P.y = a->y;
+    P.y_stride = a->y_row_stride;
+    P.L = pf4_layout(a->n_tok, a->top_k, H, I, pool.n_slots);
+    P.status = a->status;
+    if (!a->workspace || a->workspace_bytes < P.L.total ||
+        (reinterpret_cast<uintptr_t>(a->workspace) & 255))
+        return NVMOE_ERR_WORKSPACE;
+    P.ws = static_cast<unsigned char*>(a->workspace);
+    int dev = 0, sms = 0;
+    NVMOE_CUDA_TRY(cudaGetDevice(&dev));
+    NVMOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    NVMOE_CUDA_TRY(cudaMemsetAsync(P.ws + P.L.hdr, 0, P.L.base - P.L.hdr, st));
+    const int n_sel = a->n_tok * a->top_k;
+    pf4_count<<<std::max(1, std::min(4 * sms, (n_sel + 255) / 256)), 256, 0, st>>>(P);
+    pf4_scan<<<1, 1024, 0, st>>>(P);
+    const int n_all = a->n_tok * (a->top_k + 1);
+    pf4_scatter<<<std::max(1, std::min(4 * sms, (n_all + 255) / 256)), 256, 0, st>>>(P);
+    pf4_quant_x<<<a->n_tok, 128, 0, st>>>(P);
+    NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf4_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
+    NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf4_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
+    pf4_gemm<0><<<sms, kGThreads, kGSmem, st>>>(P);
+    pf4_act<<<P.L.n_ent_max, 128, 0, st>>>(P);
+    pf4_gemm<1><<<sms, kGThreads, kGSmem, st>>>(P);
+    const int64_t n4 = (int64_t)a->n_tok * (H / 4);
+    pf4_combine<<<(int)std::min<int64_t>(8 * sms, (n4 + 255) / 256), 256, 0, st>>>(P);
+    pf4_status<<<1, 1, 0, st>>>(P);
+    NVMOE_CUDA_TRY(cudaGetLastError());
+    return NVMOE_OK;
+}
+
+}  // namespace nvmoe

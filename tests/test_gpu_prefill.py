@@ -1,6 +1,6 @@
-"""R10 prefill (nvmoe_moe_ffn_prefill: token-sorted tcgen05 grouped GEMM) against the fp32
-oracle on a small batch, against the decode kernel on a batch whose slots span several
-128-entry tiles, its determinism, and its bad-slot status."""
+"""R10 prefill (nvmoe_moe_ffn_prefill: token-sorted tcgen05 grouped GEMM, f16 and block-scaled
+FP4 kernels) against the fp32 oracle on a small batch, against the decode kernel on a batch
+whose slots span several tiles, its determinism, and its bad-slot status."""
 import numpy as np
 import pytest
 import torch
@@ -11,6 +11,14 @@ from oracle import ref_numpy as R
 
 pytestmark = pytest.mark.gpu
 H, I = 2048, 512
+
+
+@pytest.fixture(autouse=True, params=["f16", "fp4"])
+def prefill_kernel(request, monkeypatch):
+    """Every test runs on both prefill kernels: block-scaled FP4 (the default) and tcgen05
+    kind::f16 on weights dequantised into tensor memory (NVMOE_PREFILL_KERNEL=f16)."""
+    monkeypatch.setenv("NVMOE_PREFILL_KERNEL", request.param)
+    return request.param
 
 
 def _dense(w, which, s):
