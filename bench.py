@@ -33,6 +33,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-layer decode tokens/s (Qwen3.8-shaped NVFP4 layer, 128-slot VRAM expert cache)"
 UNIT = "layer-tokens/s"
+FP4_TERMS = 4              # NVFP4 residual terms per activation row in the FP4 prefill
+FP4_NOMINAL_TFLOPS = 9000.0  # B200 dense FP4, nominal
 
 
 def parse():
@@ -327,10 +329,21 @@ def run_prefill(a, dev, peaks):
     tf = flop / (ms / 1e3) / 1e12
     bf16 = peaks["bf16_tflops"] if peaks else 1590.0
     del pool, shared
-    return {"tokens": T, "ms_per_layer": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
-            "algorithmic_tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / bf16, 4),
-            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback",
-            "kernel": "tcgen05 kind::f16 grouped GEMM, weights dequantised into tensor memory"}
+    fp4 = os.environ.get("NVMOE_PREFILL_KERNEL", "fp4") != "f16"
+    out = {"tokens": T, "ms_per_layer": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
+           "algorithmic_tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / bf16, 4),
+           "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback"}
+    if fp4:
+        # the activations enter the MMA as FP4_TERMS residual NVFP4 terms: the tensor cores do
+        # FP4_TERMS x the algorithmic products; no FP4 peak is measured, 9 PFLOP/s is nominal
+        mma_tf = tf * FP4_TERMS
+        out.update({"kernel": "tcgen05 kind::mxf4nvf4 block-scaled FP4 grouped GEMM (weights "
+                              "unchanged from the slot banks, activations as %d NVFP4 terms)" % FP4_TERMS,
+                    "mma_tflops_fp4": round(mma_tf, 1),
+                    "frac_of_fp4_nominal_dense": round(mma_tf / FP4_NOMINAL_TFLOPS, 4)})
+    else:
+        out["kernel"] = "tcgen05 kind::f16 grouped GEMM, weights dequantised into tensor memory"
+    return out
 
 
 def _traffic_from_profiles():

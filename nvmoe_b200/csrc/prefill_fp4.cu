@@ -35,25 +35,30 @@ namespace {
 
 constexpr int kTT = 32;                    // entries per tile: B rows 4 x 32 = 128
 constexpr int kImg = 128 * 144;            // one K stage of a tile image (128 code rows + scales)
-constexpr int kNSt = 5;                    // ring stages
-constexpr int kOffBi = 16384;              // A codes [0, 16 KB), B image, A scales
+// One ring stage (K = 256): two 128-row weight blocks A0, A1 (the MMAs of a stage share the
+// tile's B image), the B image, then the A0 and A1 scales.
+constexpr int kNSt = 4;
+constexpr int kOffA1 = 16384;
+constexpr int kOffBi = 32768;
 constexpr int kOffAs = kOffBi + kImg;
-constexpr int kStg = 36864;                // 1024-aligned stage
-static_assert(kOffAs + 2048 <= kStg && kStg % 1024 == 0, "stage layout");
-constexpr int kGThreads = 320;             // 10 warps
+constexpr int kStg = kOffAs + 4096;        // 55296, every byte of it arrives by TMA
+static_assert(kStg % 1024 == 0, "stage layout");
+constexpr int kEpiWarps = 8;               // two per TMEM lane quadrant, 16 entries each
+constexpr int kGThreads = 32 * (kEpiWarps + 6);  // + 4 scale-factor warps, producer, MMA issuer
+constexpr int kWSf = kEpiWarps, kWProd = kEpiWarps + 4, kWMma = kEpiWarps + 5;
 constexpr int kOffBar = kNSt * kStg;       // mbarriers
-constexpr int kOffMisc = kOffBar + 32 * 8; // tmem base, abort
+constexpr int kOffMisc = kOffBar + 16 * 8; // tmem base, abort
 constexpr int kOffEnt = kOffMisc + 64;     // per-entry factors of the unit [2][kTT]
-constexpr int kOffXb = kOffEnt + 2 * 4 * kTT;  // up values [64 rows][kTT] fp32
-constexpr int kGSmem = kOffXb + 64 * kTT * 4 + 1024;
-constexpr uint32_t kTmD = 0, kTmSFA = 256, kTmSFB = 256 + 16 * kNSt, kTmCols = 512;
-static_assert(kTmSFB + 16 * kNSt <= kTmCols, "tensor memory");
+constexpr int kGSmem = kOffEnt + 2 * 4 * kTT + 1024;
+// tensor memory: D0 | D1 (128 columns each), then per stage 48 scale columns (A0, A1, B)
+constexpr uint32_t kTmD = 0, kTmSF = 256, kTmCols = 512;
+static_assert(kTmSF + 48 * kNSt <= kTmCols, "tensor memory");
 
 enum { QH_N_TILES = 0, QH_N_ENT = 1, QH_STATUS = 2 };
 
 struct Pf4Layout {
-    size_t hdr, cnt, base, cursor, tile_base, tiles, ent_tok, ent_w, ent_of, ent_pos, sg, xk, hk,
-        ximg, himg, h32, ypart, total;
+    size_t hdr, cnt, base, cursor, tile_base, tiles, ent_tok, ent_w, ent_of, ent_pos, ent_xk,
+        ent_fac, hk, ximg, himg, h32, ypart, total;
     int n_keys, n_ent_max, max_tiles, ksg, ksd;
 };
 
@@ -80,8 +85,8 @@ __host__ __device__ inline Pf4Layout pf4_layout(int n_tok, int top_k, int H, int
     L.ent_w = take(4 * (size_t)L.n_ent_max);
     L.ent_of = take(4 * (size_t)L.n_ent_max);
     L.ent_pos = take(4 * (size_t)L.n_ent_max);  // tile << 8 | row
-    L.sg = take(4 * (size_t)n_tok);
-    L.xk = take(4 * (size_t)n_tok);
+    L.ent_xk = take(4 * (size_t)L.n_ent_max);   // the entry's token row exponent
+    L.ent_fac = take(4 * (size_t)L.n_ent_max);  // router weight (x shared gate)
     L.hk = take(4 * (size_t)L.n_ent_max);
     L.ximg = take((size_t)L.max_tiles * L.ksg * kImg);
     L.himg = take((size_t)L.max_tiles * L.ksd * kImg);
@@ -233,10 +238,13 @@ __global__ void __launch_bounds__(128) pf4_quant_x(const __grid_constant__ Pf4Pa
     if (lane == 0) red[warp] = am, red[4 + warp] = dot;
     __syncthreads();
     const int ke = fp4_row_exp(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])));
-    if (tid == 0) {
-        qws<int>(P, P.L.xk)[t] = ke;
-        if (P.shared_gate)
-            qws<float>(P, P.L.sg)[t] = 1.0f / (1.0f + expf(-(red[4] + red[5] + red[6] + red[7])));
+    if (tid < K1 && ents[tid] >= 0) {
+        const int e = ents[tid];
+        float f = qws<float>(P, P.L.ent_w)[e];
+        if (tid == P.top_k && P.shared_gate)
+            f *= 1.0f / (1.0f + expf(-(red[4] + red[5] + red[6] + red[7])));
+        qws<int>(P, P.L.ent_xk)[e] = ke;
+        qws<float>(P, P.L.ent_fac)[e] = f;
     }
     const int* ent_pos = qws<int>(P, P.L.ent_pos);
     uint8_t* ximg = P.ws + P.L.ximg;
@@ -258,51 +266,49 @@ __global__ void __launch_bounds__(128) pf4_quant_x(const __grid_constant__ Pf4Pa
     }
 }
 
-// One block of 128 threads per entry: the h row's exponent, then its 16-blocks as NVFP4 terms
-// into the entry's row of the down image (thread tid: values 4 tid + 512 m .. + 4).
-__global__ void __launch_bounds__(128) pf4_act(const __grid_constant__ Pf4Params P) {
-    __shared__ float red[4];
-    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (e >= qws<int>(P, P.L.hdr)[QH_N_ENT]) return;
-    const int I = P.pool.inter, KSD = P.L.ksd, MC = (I + 511) / 512;
+// One warp per entry (8 per block): the h row's exponent, then its 16-blocks as NVFP4 terms into
+// the entry's row of the down image (lane l: values 128 m + 4 l .. + 4, m < I / 128).
+constexpr int kActWarps = 8;
+__global__ void __launch_bounds__(32 * kActWarps) pf4_act(const __grid_constant__ Pf4Params P) {
+    const int e = blockIdx.x * kActWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (e >= qws<int>(P, P.L.hdr)[QH_N_ENT]) return;  // the whole warp: the quantiser shuffles
+    const int I = P.pool.inter, KSD = P.L.ksd, MC = I / 128;
     const float* hrow = qws<float>(P, P.L.h32) + (int64_t)e * I;
-    float4 hv[3];  // I <= 1536
+    float4 hv[12];  // I <= 1536
     float am = 0.f;
 #pragma unroll
-    for (int m = 0; m < 3; ++m) {
+    for (int m = 0; m < 12; ++m) {
         hv[m] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < MC && 4 * tid + 512 * m < I) hv[m] = *reinterpret_cast<const float4*>(hrow + 512 * m + 4 * tid);
+        if (m < MC) hv[m] = *reinterpret_cast<const float4*>(hrow + 128 * m + 4 * lane);
         am = fmaxf(am, fmaxf(fmaxf(fabsf(hv[m].x), fabsf(hv[m].y)), fmaxf(fabsf(hv[m].z), fabsf(hv[m].w))));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    if (lane == 0) red[warp] = am;
-    __syncthreads();
-    const int kh = fp4_row_exp(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])));
-    if (tid == 0) qws<int>(P, P.L.hk)[e] = kh;
+    const int kh = fp4_row_exp(am);
+    if (lane == 0) qws<int>(P, P.L.hk)[e] = kh;
     const int pos = qws<int>(P, P.L.ent_pos)[e];
     uint8_t* himg = P.ws + P.L.himg;
 #pragma unroll
-    for (int m = 0; m < 3; ++m) {
+    for (int m = 0; m < 12; ++m) {
         if (m >= MC) break;
-        const bool valid = 4 * tid + 512 * m < I;
-        const int blk = valid ? (tid >> 2) + 32 * m : 0;
+        const int blk = (lane >> 2) + 8 * m;
         float v[4] = {hv[m].x, hv[m].y, hv[m].z, hv[m].w};
         uint16_t two[kFp4Terms];
         uint8_t sc[kFp4Terms];
         quant4_terms(v, kh, two, sc);
-        if (valid) {
-            uint8_t* img = himg + ((int64_t)(pos >> 8) * KSD + blk / 16) * kImg;
-            put4(img, 128, pos & 0xff, blk % 16, two, sc);
-        }
+        uint8_t* img = himg + ((int64_t)(pos >> 8) * KSD + blk / 16) * kImg;
+        put4(img, 128, pos & 0xff, blk % 16, two, sc);
     }
 }
 
 // ------------------------------------------------------------------ the grouped GEMMs
-// Persistent, one CTA per SM; units dealt round-robin (u = c, c + G, ...).  PH = 0: gate_up
-// units (tile, j-block of 64), PH = 1: down units (tile, 128 rows of H).  Warps 0-3 epilogue
-// (TMEM lane quadrants), 4-7 scale factors, 8 producer (TMA weights + the tile's B image
-// stage), 9 MMA issuer.
+// Persistent, one CTA per SM; units dealt round-robin (u = c, c + G, ...), so the units of one
+// tile, and the tiles of one expert, run side by side and share their loads in L2.  A unit is
+// two 128-row weight blocks against one tile: PH = 0 (gate_up) the gate and the up rows of a
+// 128-row j-block, so one thread holds gate and up of the same j; PH = 1 (down) 256 rows of H.
+// Warps 0-7 epilogue (two per TMEM lane quadrant, 16 entries each), 8-11 scale factors, 12
+// producer (TMA weights + the tile's B image stage), 13 MMA issuer.  One D buffer: the MMAs of
+// the next unit start when the epilogue has read D out, while the ring keeps loading.
 template <int PH>
 __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__ Pf4Params P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -311,17 +317,16 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
     uint64_t* sf_full = full + kNSt;
     uint64_t* empty = full + 2 * kNSt;
     uint64_t* d_full = full + 3 * kNSt;
-    uint64_t* d_empty = d_full + 2;
+    uint64_t* d_empty = d_full + 1;
     uint32_t* tmem_p = reinterpret_cast<uint32_t*>(sm + kOffMisc);
     volatile int* abort = reinterpret_cast<int*>(sm + kOffMisc) + 1;
-    float* efac = reinterpret_cast<float*>(sm + kOffEnt);         // [kTT] per-entry factor
-    int* eexp = reinterpret_cast<int*>(sm + kOffEnt) + kTT;        // [kTT] per-entry exponent
-    float* xbuf = reinterpret_cast<float*>(sm + kOffXb);
+    float* efac = reinterpret_cast<float*>(sm + kOffEnt);    // [kTT] per-entry factor
+    int* eexp = reinterpret_cast<int*>(sm + kOffEnt) + kTT;   // [kTT] per-entry exponent
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, G = gridDim.x;
     const int H = P.pool.hidden, I = P.pool.inter, S = P.pool.n_slots;
-    const int UPT = PH ? H / 128 : I / 64;         // units per tile
-    const int KS = PH ? P.L.ksd : P.L.ksg;         // K stages per unit
+    const int UPT = PH ? H / 256 : I / 128;  // units per tile
+    const int KS = PH ? P.L.ksd : P.L.ksg;   // K stages per unit
 
     if (tid == 0) {
         for (int s = 0; s < kNSt; ++s) {
@@ -329,15 +334,13 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
             mbar_init(&sf_full[s], 4);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&d_full[b], 1);
-            mbar_init(&d_empty[b], 4);
-        }
+        mbar_init(d_full, 1);
+        mbar_init(d_empty, kEpiWarps);
         *abort = 0;
         mbar_init_fence();
     }
-    if (warp == 9) umma::tmem_alloc(tmem_p, kTmCols);
-    if (warp == 8 && lane < 12) prefetch_map(&P.map[lane]);
+    if (warp == kWMma) umma::tmem_alloc(tmem_p, kTmCols);
+    if (warp == kWProd && lane < 12) prefetch_map(&P.map[lane]);
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
     const uint8_t* img = P.ws + (PH ? P.L.himg : P.L.ximg);
     bool ok = true;
 
-    if (warp == 8) {
+    if (warp == kWProd) {
         if (lane == 0) {
             const uint64_t pol = l2_evict_first_policy();
             int it = 0;
@@ -367,15 +370,23 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                         break;
                     }
                     uint8_t* st = sm + s * kStg;
-                    mbar_arrive_expect_tx(&full[s], 16384 + 2048 + kImg);
-                    if (PH == 0) {
-                        tma_load_3d(st, m + M_GATE, ks * 128, sub * 64, slot, &full[s], pol);
-                        tma_load_3d(st + 8192, m + M_UP, ks * 128, sub * 64, slot, &full[s], pol);
-                        tma_load_3d(st + kOffAs, m + M_GATE_SF, ks * 16, sub * 64, slot, &full[s], pol);
-                        tma_load_3d(st + kOffAs + 1024, m + M_UP_SF, ks * 16, sub * 64, slot, &full[s], pol);
+                    mbar_arrive_expect_tx(&full[s], kStg);
+                    if (PH == 0) {  // gate and up boxes are 64 rows: two per block
+                        const int y = sub * 128;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            tma_load_3d(st + 8192 * h, m + M_GATE, ks * 128, y + 64 * h, slot, &full[s], pol);
+                            tma_load_3d(st + kOffA1 + 8192 * h, m + M_UP, ks * 128, y + 64 * h, slot, &full[s], pol);
+                            tma_load_3d(st + kOffAs + 1024 * h, m + M_GATE_SF, ks * 16, y + 64 * h, slot, &full[s], pol);
+                            tma_load_3d(st + kOffAs + 2048 + 1024 * h, m + M_UP_SF, ks * 16, y + 64 * h, slot, &full[s], pol);
+                        }
                     } else {
-                        tma_load_3d(st, m + M_DOWN, ks * 128, sub * 128, slot, &full[s], pol);
-                        tma_load_3d(st + kOffAs, m + M_DOWN_SF, ks * 16, sub * 128, slot, &full[s], pol);
+                        const int y = sub * 256;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            tma_load_3d(st + kOffA1 * h, m + M_DOWN, ks * 128, y + 128 * h, slot, &full[s], pol);
+                            tma_load_3d(st + kOffAs + 2048 * h, m + M_DOWN_SF, ks * 16, y + 128 * h, slot, &full[s], pol);
+                        }
                     }
                     bulk_g2s(st + kOffBi, img + ((int64_t)tile * KS + ks) * kImg, kImg, &full[s]);
                 }
@@ -386,14 +397,13 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
             }
         }
         __syncwarp();
-    } else if (warp == 9) {
+    } else if (warp == kWMma) {
         int it = 0;
         for (int k = 0; k < my_units && ok; ++k) {
             const int u = c + k * G, tile = u / UPT;
             const int nr = tiles[3 * tile + 2];
             const uint32_t idesc = umma::idesc_mxf4(128, npad_of(nr));
-            const int db = k & 1;
-            if (k >= 2 && !wait_bar(&d_empty[db], ((k >> 1) + 1) & 1, abort)) {
+            if (k >= 1 && !wait_bar(d_empty, (k - 1) & 1, abort)) {
                 ok = false;
                 break;
             }
@@ -407,24 +417,28 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                 umma::fence_after_sync();
                 if (lane == 0) {
                     const uint32_t sa = smem_u32(sm + s * kStg);
+                    const uint32_t sf = tm + kTmSF + 48 * s;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        umma::mma_mxf4(tm + kTmD + db * 128, umma::smem_desc_sw128(sa + 32 * i),
-                                       umma::smem_desc_sw128(sa + kOffBi + 32 * i), idesc,
-                                       tm + kTmSFA + s * 16 + 4 * i, tm + kTmSFB + s * 16 + 4 * i,
-                                       (ks == 0 && i == 0) ? 0u : 1u);
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t acc = (ks == 0 && i == 0) ? 0u : 1u;
+                        const uint64_t bd = umma::smem_desc_sw128(sa + kOffBi + 32 * i);
+                        umma::mma_mxf4(tm + kTmD, umma::smem_desc_sw128(sa + 32 * i), bd, idesc,
+                                       sf + 4 * i, sf + 32 + 4 * i, acc);
+                        umma::mma_mxf4(tm + kTmD + 128, umma::smem_desc_sw128(sa + kOffA1 + 32 * i),
+                                       bd, idesc, sf + 16 + 4 * i, sf + 32 + 4 * i, acc);
+                    }
                     umma::commit(&empty[s]);
                 }
                 __syncwarp();
             }
             if (!ok) break;
-            if (lane == 0) umma::commit(&d_full[db]);
+            if (lane == 0) umma::commit(d_full);
             __syncwarp();
         }
-    } else if (warp >= 4) {
-        // scale factors: A (weights) and B (image rows), 128 rows each -> column 4 i + r / 32,
-        // lane r % 32 of every quadrant
-        const int qd = warp - 4;
+    } else if (warp >= kWSf) {
+        // scale factors of A0, A1 and B, 128 rows each -> column 4 i + r / 32, lane r % 32 of
+        // every quadrant
+        const int qd = warp & 3;
         int it = 0;
         for (int k = 0; k < my_units && ok; ++k) {
             for (int ks = 0; ks < KS; ++ks, ++it) {
@@ -434,16 +448,21 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                     break;
                 }
                 const uint8_t* st = sm + s * kStg;
-                uint32_t va[16], vb[16];
+                uint32_t va0[16], va1[16], vb[16];
 #pragma unroll
                 for (int m1 = 0; m1 < 4; ++m1) {
-                    const uint4 a = *reinterpret_cast<const uint4*>(st + kOffAs + (32 * m1 + lane) * 16);
-                    const uint4 b = *reinterpret_cast<const uint4*>(st + kOffBi + 128 * 128 + (32 * m1 + lane) * 16);
-                    va[m1] = a.x, va[4 + m1] = a.y, va[8 + m1] = a.z, va[12 + m1] = a.w;
+                    const int row = 32 * m1 + lane;
+                    const uint4 a0 = *reinterpret_cast<const uint4*>(st + kOffAs + row * 16);
+                    const uint4 a1 = *reinterpret_cast<const uint4*>(st + kOffAs + 2048 + row * 16);
+                    const uint4 b = *reinterpret_cast<const uint4*>(st + kOffBi + 128 * 128 + row * 16);
+                    va0[m1] = a0.x, va0[4 + m1] = a0.y, va0[8 + m1] = a0.z, va0[12 + m1] = a0.w;
+                    va1[m1] = a1.x, va1[4 + m1] = a1.y, va1[8 + m1] = a1.z, va1[12 + m1] = a1.w;
                     vb[m1] = b.x, vb[4 + m1] = b.y, vb[8 + m1] = b.z, vb[12 + m1] = b.w;
                 }
-                umma::st_x16(tm + ((uint32_t)(qd * 32) << 16) + kTmSFA + s * 16, va);
-                umma::st_x16(tm + ((uint32_t)(qd * 32) << 16) + kTmSFB + s * 16, vb);
+                const uint32_t ta = tm + ((uint32_t)(qd * 32) << 16) + kTmSF + 48 * s;
+                umma::st_x16(ta, va0);
+                umma::st_x16(ta + 16, va1);
+                umma::st_x16(ta + 32, vb);
                 umma::wait_st();
                 umma::fence_before_sync();
                 __syncwarp();
@@ -451,13 +470,12 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
             }
         }
     } else {
-        // epilogue: row r of the unit's D (a weight row), one column group of 4 per entry
-        const int r = tid;
-        const int* ent_tok = qws<int>(P, P.L.ent_tok);
-        const float* ent_w = qws<float>(P, P.L.ent_w);
-        const int* xk = qws<int>(P, P.L.xk);
+        // epilogue: row r of the unit's two D blocks (the same weight row index in A0 and A1),
+        // entries 16 hh .. 16 hh + 15 (a column group of 4 terms each)
+        const int r = 32 * (warp & 3) + lane, hh = warp >> 2, i0 = 16 * hh;
+        const int* ent_xk = qws<int>(P, P.L.ent_xk);
+        const float* ent_fac = qws<float>(P, P.L.ent_fac);
         const int* hk = qws<int>(P, P.L.hk);
-        const float* sgv = P.shared_gate ? qws<float>(P, P.L.sg) : nullptr;
         float* h32 = qws<float>(P, P.L.h32);
         float* ypart = qws<float>(P, P.L.ypart);
         for (int k = 0; k < my_units && ok; ++k) {
@@ -468,73 +486,71 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
             const int slot = sh ? 0 : key;
             // per-entry exponent and factor of this unit (loaded while its MMAs run)
             if (tid < nr) {
-                const int e = eb + tid;
-                if (PH == 0) {
-                    eexp[tid] = xk[ent_tok[e]];
-                } else {
-                    eexp[tid] = hk[e];
-                    float f = ent_w[e] * global_of(pool.down, slot);
-                    if (sh && sgv) f *= sgv[ent_tok[e]];
-                    efac[tid] = f;
-                }
+                eexp[tid] = PH ? hk[eb + tid] : ent_xk[eb + tid];
+                if (PH) efac[tid] = ent_fac[eb + tid];
             }
-            const float gl = PH ? 0.f : global_of(r < 64 ? pool.gate : pool.up, slot);
-            named_bar_sync(1, 128);
-            const int db = k & 1;
-            if (!wait_bar(&d_full[db], (k >> 1) & 1, abort)) {
+            const float ga = global_of(PH ? pool.down : pool.gate, slot);
+            const float gb = PH ? ga : global_of(pool.up, slot);
+            named_bar_sync(1, 32 * kEpiWarps);
+            if (!wait_bar(d_full, k & 1, abort)) {
                 ok = false;
                 break;
             }
             umma::fence_after_sync();
-            const int nchunk = (4 * nr + 15) / 16;  // 4 entries per 16 columns
-            float v[kTT];
+            float v0[16], v1[16];
 #pragma unroll
-            for (int ch = 0; ch < kTT / 4; ++ch) {
-                if (ch >= nchunk) break;
-                uint32_t d[16];
-                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + db * 128 + 16 * ch), d);
+            for (int ch = 0; ch < 4; ++ch) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v0[4 * ch + q] = v1[4 * ch + q] = 0.f;
+                if (i0 + 4 * ch >= nr) continue;
+                uint32_t d0[16], d1[16];
+                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + 64 * hh + 16 * ch), d0);
+                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + 128 + 64 * hh + 16 * ch), d1);
                 umma::wait_ld();
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    float a = 0.f;
+                    float a = 0.f, b = 0.f;
 #pragma unroll
-                    for (int t = kFp4Terms - 1; t >= 0; --t)
-                        a = fmaf(__uint_as_float(d[kFp4Terms * q + t]), fp4_exp2(-2 * t), a);
-                    v[4 * ch + q] = a;
+                    for (int t = kFp4Terms - 1; t >= 0; --t) {
+                        a = fmaf(__uint_as_float(d0[kFp4Terms * q + t]), fp4_exp2(-2 * t), a);
+                        b = fmaf(__uint_as_float(d1[kFp4Terms * q + t]), fp4_exp2(-2 * t), b);
+                    }
+                    v0[4 * ch + q] = a;
+                    v1[4 * ch + q] = b;
                 }
             }
             umma::fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&d_empty[db]);
+            if (lane == 0) mbar_arrive(d_empty);
             if (PH == 0) {
-                // rows 0-63 gate, 64-127 up of j = 64 sub + r % 64
-                if (r >= 64) {
 #pragma unroll
-                    for (int i = 0; i < kTT; ++i)
-                        if (i < nr) xbuf[(r - 64) * kTT + i] = v[i] * fp4_exp2(-eexp[i]) * gl;
-                }
-                named_bar_sync(1, 128);
-                if (r < 64) {
-#pragma unroll
-                    for (int i = 0; i < kTT; ++i)
-                        if (i < nr)
-                            h32[(int64_t)(eb + i) * I + sub * 64 + r] =
-                                silu(v[i] * fp4_exp2(-eexp[i]) * gl) * xbuf[r * kTT + i];
+                for (int i = 0; i < 16; ++i) {
+                    const int e = i0 + i;
+                    if (e < nr) {
+                        const float f = fp4_exp2(-eexp[e]);
+                        h32[(int64_t)(eb + e) * I + sub * 128 + r] = silu(v0[i] * f * ga) * (v1[i] * f * gb);
+                    }
                 }
             } else {
 #pragma unroll
-                for (int i = 0; i < kTT; ++i)
-                    if (i < nr)
-                        ypart[(int64_t)(eb + i) * H + sub * 128 + r] = v[i] * fp4_exp2(-eexp[i]) * efac[i];
+                for (int i = 0; i < 16; ++i) {
+                    const int e = i0 + i;
+                    if (e < nr) {
+                        const float f = fp4_exp2(-eexp[e]) * efac[e] * ga;
+                        float* yp = ypart + (int64_t)(eb + e) * H + sub * 256 + r;
+                        yp[0] = v0[i] * f;
+                        yp[128] = v1[i] * f;
+                    }
+                }
             }
-            named_bar_sync(1, 128);  // eexp / efac / xbuf are rewritten by the next unit
+            named_bar_sync(1, 32 * kEpiWarps);  // eexp / efac are rewritten by the next unit
         }
     }
     if (!ok && tid % 32 == 0) atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_TIMEOUT);
 
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == kWMma) {
         umma::fence_after_sync();
         umma::tmem_dealloc(tm, kTmCols);
     }
@@ -627,7 +643,7 @@ int prefill_fp4_run(const nvmoe_ffn_args* a, cudaStream_t st) {
     NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf4_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
     NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf4_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
     pf4_gemm<0><<<sms, kGThreads, kGSmem, st>>>(P);
-    pf4_act<<<P.L.n_ent_max, 128, 0, st>>>(P);
+    pf4_act<<<(P.L.n_ent_max + kActWarps - 1) / kActWarps, 32 * kActWarps, 0, st>>>(P);
     pf4_gemm<1><<<sms, kGThreads, kGSmem, st>>>(P);
     const int64_t n4 = (int64_t)a->n_tok * (H / 4);
     pf4_combine<<<(int)std::min<int64_t>(8 * sms, (n4 + 255) / 256), 256, 0, st>>>(P);
