@@ -44,12 +44,21 @@ constexpr int kOffAs = kOffBi + kImg;
 constexpr int kStg = kOffAs + 4096;        // 55296, every byte of it arrives by TMA
 static_assert(kStg % 1024 == 0, "stage layout");
 constexpr int kEpiWarps = 8;               // two per TMEM lane quadrant, 16 entries each
-constexpr int kGThreads = 32 * (kEpiWarps + 6);  // + 4 scale-factor warps, producer, MMA issuer
-constexpr int kWSf = kEpiWarps, kWProd = kEpiWarps + 4, kWMma = kEpiWarps + 5;
+// + 4 scale-factor warps, the producer, the MMA issuer and the unit-info warp
+constexpr int kGThreads = 32 * (kEpiWarps + 7);
+constexpr int kWSf = kEpiWarps, kWProd = kEpiWarps + 4, kWMma = kEpiWarps + 5, kWInfo = kEpiWarps + 6;
+// What the epilogue needs of a unit, prepared ahead by the unit-info warp in a ring of kInfoN.
+struct UnitInfo {
+    int eb, nr;
+    float ga, gb;       // global scales of the A0 and A1 blocks
+    int eexp[kTT];      // per entry: the row exponent of its B rows
+    float efac[kTT];    // per entry: router weight (x shared gate), down phase
+};
+constexpr int kInfoN = 4;
 constexpr int kOffBar = kNSt * kStg;       // mbarriers
-constexpr int kOffMisc = kOffBar + 16 * 8; // tmem base, abort
-constexpr int kOffEnt = kOffMisc + 64;     // per-entry factors of the unit [2][kTT]
-constexpr int kGSmem = kOffEnt + 2 * 4 * kTT + 1024;
+constexpr int kOffMisc = kOffBar + 32 * 8; // tmem base, abort
+constexpr int kOffInfo = kOffMisc + 64;
+constexpr int kGSmem = kOffInfo + kInfoN * (int)sizeof(UnitInfo) + 1024;
 // tensor memory: D0 | D1 (128 columns each), then per stage 48 scale columns (A0, A1, B)
 constexpr uint32_t kTmD = 0, kTmSF = 256, kTmCols = 512;
 static_assert(kTmSF + 48 * kNSt <= kTmCols, "tensor memory");
@@ -269,17 +278,17 @@ __global__ void __launch_bounds__(128) pf4_quant_x(const __grid_constant__ Pf4Pa
 // One warp per entry (8 per block): the h row's exponent, then its 16-blocks as NVFP4 terms into
 // the entry's row of the down image (lane l: values 128 m + 4 l .. + 4, m < I / 128).
 constexpr int kActWarps = 8;
+template <int MC>  // I / 128
 __global__ void __launch_bounds__(32 * kActWarps) pf4_act(const __grid_constant__ Pf4Params P) {
     const int e = blockIdx.x * kActWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (e >= qws<int>(P, P.L.hdr)[QH_N_ENT]) return;  // the whole warp: the quantiser shuffles
-    const int I = P.pool.inter, KSD = P.L.ksd, MC = I / 128;
+    const int I = 128 * MC, KSD = P.L.ksd;
     const float* hrow = qws<float>(P, P.L.h32) + (int64_t)e * I;
-    float4 hv[12];  // I <= 1536
+    float4 hv[MC];
     float am = 0.f;
 #pragma unroll
-    for (int m = 0; m < 12; ++m) {
-        hv[m] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < MC) hv[m] = *reinterpret_cast<const float4*>(hrow + 128 * m + 4 * lane);
+    for (int m = 0; m < MC; ++m) {
+        hv[m] = *reinterpret_cast<const float4*>(hrow + 128 * m + 4 * lane);
         am = fmaxf(am, fmaxf(fmaxf(fabsf(hv[m].x), fabsf(hv[m].y)), fmaxf(fabsf(hv[m].z), fabsf(hv[m].w))));
     }
 #pragma unroll
@@ -289,8 +298,7 @@ __global__ void __launch_bounds__(32 * kActWarps) pf4_act(const __grid_constant_
     const int pos = qws<int>(P, P.L.ent_pos)[e];
     uint8_t* himg = P.ws + P.L.himg;
 #pragma unroll
-    for (int m = 0; m < 12; ++m) {
-        if (m >= MC) break;
+    for (int m = 0; m < MC; ++m) {
         const int blk = (lane >> 2) + 8 * m;
         float v[4] = {hv[m].x, hv[m].y, hv[m].z, hv[m].w};
         uint16_t two[kFp4Terms];
@@ -318,10 +326,11 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
     uint64_t* empty = full + 2 * kNSt;
     uint64_t* d_full = full + 3 * kNSt;
     uint64_t* d_empty = d_full + 1;
+    uint64_t* info_full = d_full + 2;
+    uint64_t* info_empty = info_full + kInfoN;
     uint32_t* tmem_p = reinterpret_cast<uint32_t*>(sm + kOffMisc);
     volatile int* abort = reinterpret_cast<int*>(sm + kOffMisc) + 1;
-    float* efac = reinterpret_cast<float*>(sm + kOffEnt);    // [kTT] per-entry factor
-    int* eexp = reinterpret_cast<int*>(sm + kOffEnt) + kTT;   // [kTT] per-entry exponent
+    UnitInfo* info = reinterpret_cast<UnitInfo*>(sm + kOffInfo);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, G = gridDim.x;
     const int H = P.pool.hidden, I = P.pool.inter, S = P.pool.n_slots;
@@ -336,6 +345,10 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
         }
         mbar_init(d_full, 1);
         mbar_init(d_empty, kEpiWarps);
+        for (int b = 0; b < kInfoN; ++b) {
+            mbar_init(&info_full[b], 1);
+            mbar_init(&info_empty[b], kEpiWarps);
+        }
         *abort = 0;
         mbar_init_fence();
     }
@@ -357,9 +370,11 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
         if (lane == 0) {
             const uint64_t pol = l2_evict_first_policy();
             int it = 0;
+            int key_next = my_units > 0 ? tiles[3 * (c / UPT)] : 0;
             for (int k = 0; k < my_units && ok; ++k) {
                 const int u = c + k * G, tile = u / UPT, sub = u - tile * UPT;
-                const int key = tiles[3 * tile];
+                const int key = key_next;
+                if (k + 1 < my_units) key_next = tiles[3 * ((u + G) / UPT)];
                 const bool sh = key == S;
                 const int slot = sh ? 0 : key;
                 const CUtensorMap* m = P.map + (sh ? 6 : 0);
@@ -399,9 +414,11 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
         __syncwarp();
     } else if (warp == kWMma) {
         int it = 0;
+        int nr_next = my_units > 0 ? tiles[3 * (c / UPT) + 2] : 0;
         for (int k = 0; k < my_units && ok; ++k) {
-            const int u = c + k * G, tile = u / UPT;
-            const int nr = tiles[3 * tile + 2];
+            const int u = c + k * G;
+            const int nr = nr_next;
+            if (k + 1 < my_units) nr_next = tiles[3 * ((u + G) / UPT) + 2];
             const uint32_t idesc = umma::idesc_mxf4(128, npad_of(nr));
             if (k >= 1 && !wait_bar(d_empty, (k - 1) & 1, abort)) {
                 ok = false;
@@ -434,6 +451,41 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
             if (!ok) break;
             if (lane == 0) umma::commit(d_full);
             __syncwarp();
+        }
+    } else if (warp == kWInfo) {
+        const int* ent_xk = qws<int>(P, P.L.ent_xk);
+        const float* ent_fac = qws<float>(P, P.L.ent_fac);
+        const int* hk = qws<int>(P, P.L.hk);
+        int4 tn = make_int4(0, 0, 0, 0);  // the next unit's tile record
+        if (my_units > 0) tn = make_int4(tiles[3 * (c / UPT)], tiles[3 * (c / UPT) + 1], tiles[3 * (c / UPT) + 2], 0);
+        for (int k = 0; k < my_units && ok; ++k) {
+            const int b = k % kInfoN, u = c + k * G;
+            const int key = tn.x, eb = tn.y, nr = tn.z;
+            if (k + 1 < my_units) {
+                const int t1 = (u + G) / UPT;
+                tn = make_int4(tiles[3 * t1], tiles[3 * t1 + 1], tiles[3 * t1 + 2], 0);
+            }
+            const bool sh = key == S;
+            const nvmoe_expert_pool& pool = sh ? P.shared : P.pool;
+            const int slot = sh ? 0 : key;
+            int ex = 0;
+            float fa = 0.f;
+            if (lane < nr) {
+                ex = PH ? hk[eb + lane] : ent_xk[eb + lane];
+                if (PH) fa = ent_fac[eb + lane];
+            }
+            const float ga = global_of(PH ? pool.down : pool.gate, slot);
+            const float gb = PH ? ga : global_of(pool.up, slot);
+            if (k >= kInfoN && !wait_bar(&info_empty[b], ((k / kInfoN) + 1) & 1, abort)) {
+                ok = false;
+                break;
+            }
+            UnitInfo& in = info[b];
+            in.eexp[lane] = ex;
+            in.efac[lane] = fa;
+            if (lane == 0) in.eb = eb, in.nr = nr, in.ga = ga, in.gb = gb;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&info_full[b]);
         }
     } else if (warp >= kWSf) {
         // scale factors of A0, A1 and B, 128 rows each -> column 4 i + r / 32, lane r % 32 of
@@ -473,25 +525,17 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
         // epilogue: row r of the unit's two D blocks (the same weight row index in A0 and A1),
         // entries 16 hh .. 16 hh + 15 (a column group of 4 terms each)
         const int r = 32 * (warp & 3) + lane, hh = warp >> 2, i0 = 16 * hh;
-        const int* ent_xk = qws<int>(P, P.L.ent_xk);
-        const float* ent_fac = qws<float>(P, P.L.ent_fac);
-        const int* hk = qws<int>(P, P.L.hk);
         float* h32 = qws<float>(P, P.L.h32);
         float* ypart = qws<float>(P, P.L.ypart);
         for (int k = 0; k < my_units && ok; ++k) {
-            const int u = c + k * G, tile = u / UPT, sub = u - tile * UPT;
-            const int key = tiles[3 * tile], eb = tiles[3 * tile + 1], nr = tiles[3 * tile + 2];
-            const bool sh = key == S;
-            const nvmoe_expert_pool& pool = sh ? P.shared : P.pool;
-            const int slot = sh ? 0 : key;
-            // per-entry exponent and factor of this unit (loaded while its MMAs run)
-            if (tid < nr) {
-                eexp[tid] = PH ? hk[eb + tid] : ent_xk[eb + tid];
-                if (PH) efac[tid] = ent_fac[eb + tid];
+            const int b = k % kInfoN, u = c + k * G, sub = u % UPT;
+            if (!wait_bar(&info_full[b], (k / kInfoN) & 1, abort)) {
+                ok = false;
+                break;
             }
-            const float ga = global_of(PH ? pool.down : pool.gate, slot);
-            const float gb = PH ? ga : global_of(pool.up, slot);
-            named_bar_sync(1, 32 * kEpiWarps);
+            const UnitInfo& in = info[b];
+            const int eb = in.eb, nr = in.nr;
+            const float ga = in.ga, gb = in.gb;
             if (!wait_bar(d_full, k & 1, abort)) {
                 ok = false;
                 break;
@@ -527,7 +571,7 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                 for (int i = 0; i < 16; ++i) {
                     const int e = i0 + i;
                     if (e < nr) {
-                        const float f = fp4_exp2(-eexp[e]);
+                        const float f = fp4_exp2(-in.eexp[e]);
                         h32[(int64_t)(eb + e) * I + sub * 128 + r] = silu(v0[i] * f * ga) * (v1[i] * f * gb);
                     }
                 }
@@ -536,14 +580,15 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                 for (int i = 0; i < 16; ++i) {
                     const int e = i0 + i;
                     if (e < nr) {
-                        const float f = fp4_exp2(-eexp[e]) * efac[e] * ga;
+                        const float f = fp4_exp2(-in.eexp[e]) * in.efac[e] * ga;
                         float* yp = ypart + (int64_t)(eb + e) * H + sub * 256 + r;
                         yp[0] = v0[i] * f;
                         yp[128] = v1[i] * f;
                     }
                 }
             }
-            named_bar_sync(1, 32 * kEpiWarps);  // eexp / efac are rewritten by the next unit
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&info_empty[b]);
         }
     }
     if (!ok && tid % 32 == 0) atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_TIMEOUT);
@@ -643,7 +688,15 @@ int prefill_fp4_run(const nvmoe_ffn_args* a, cudaStream_t st) {
     NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf4_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
     NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf4_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
     pf4_gemm<0><<<sms, kGThreads, kGSmem, st>>>(P);
-    pf4_act<<<(P.L.n_ent_max + kActWarps - 1) / kActWarps, 32 * kActWarps, 0, st>>>(P);
+    const int act_blocks = (P.L.n_ent_max + kActWarps - 1) / kActWarps;
+    switch (I / 128) {  // I is a multiple of 256 up to 1536
+        case 2: pf4_act<2><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        case 4: pf4_act<4><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        case 6: pf4_act<6><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        case 8: pf4_act<8><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        case 10: pf4_act<10><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        default: pf4_act<12><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+    }
     pf4_gemm<1><<<sms, kGThreads, kGSmem, st>>>(P);
     const int64_t n4 = (int64_t)a->n_tok * (H / 4);
     pf4_combine<<<(int)std::min<int64_t>(8 * sms, (n4 + 255) / 256), 256, 0, st>>>(P);
