@@ -2,7 +2,7 @@
 // token-sorted grouped GEMM of tcgen05.mma kind::mxf4nvf4 (E2M1 x E2M1, one UE4M3 scale per 16
 // on both operands, fp32 accumulators in tensor memory).  The weights go from the slot banks to
 // shared memory by TMA (128-byte swizzle) and into the MMA unchanged; the activations enter as
-// kFp4Terms NVFP4 residual terms per row (the quantiser and layout of fp4_common.cuh), so the
+// kNT NVFP4 residual terms per row (the quantiser of fp4_common.cuh, two lanes per block), so the
 // result matches the f16 path and the oracle within the FFN tolerance.
 //
 // Same contract as nvmoe_moe_ffn_prefill's f16 path (nvme_offload_cache.py:1957-2013; llama.cpp
@@ -64,6 +64,74 @@ constexpr uint32_t kTmD = 0, kTmSF = 256, kTmCols = 512;
 static_assert(kTmSF + 48 * kNSt <= kTmCols, "tensor memory");
 
 enum { QH_N_TILES = 0, QH_N_ENT = 1, QH_STATUS = 2 };
+
+constexpr int kNT = kFp4Terms;  // NVFP4 terms per activation row: B rows kNT i + t
+
+// ---- activation quantiser for the tile images: a warp quantises one K stage (256 values, 16
+// blocks) of one row; lanes 2 blk and 2 blk + 1 hold values 8 hf .. 8 hf + 7 of block blk.
+// kNT residual terms as in fp4_common.cuh: per term the block maximum, a UE4M3 scale rounded up
+// (times 2^(ke + 2 t)), E2M1 round-to-nearest.  code[t] = this lane's 4 code bytes of term t,
+// byte t of scw = the block's scale code of term t.
+__device__ __forceinline__ void quant_pair_terms(float (&v)[8], int ke, uint32_t (&code)[kNT],
+                                                 uint32_t& scw) {
+    scw = 0;
+#pragma unroll
+    for (int t = 0; t < kNT; ++t) {
+        float am = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) am = fmaxf(am, fabsf(v[k]));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        const float target = am * (1.0f / 6.0f) * fp4_exp2(ke + 2 * t);
+        uint32_t c8 = e4m3_code(target);
+        float sv = e4m3_value(c8);
+        if (sv < target && c8 < 0x7eu) sv = e4m3_value(++c8);  // round the scale up
+        const float sc = sv * fp4_exp2(-(ke + 2 * t));
+        const float inv = sc > 0.f ? 1.0f / sc : 0.f;
+        uint32_t w;
+        asm("{ .reg .b8 b0, b1, b2, b3;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+            "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+            "mov.b32 %0, {b0, b1, b2, b3}; }"
+            : "=r"(w)
+            : "f"(v[0] * inv), "f"(v[1] * inv), "f"(v[2] * inv), "f"(v[3] * inv),
+              "f"(v[4] * inv), "f"(v[5] * inv), "f"(v[6] * inv), "f"(v[7] * inv));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t h2 = e2m1x2_to_f16x2((uint16_t)((w >> (8 * j)) & 0xffu));
+            const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+            v[2 * j] = fmaf(-d.x, sc, v[2 * j]);
+            v[2 * j + 1] = fmaf(-d.y, sc, v[2 * j + 1]);
+        }
+        code[t] = w;
+        scw |= c8 << (8 * t);
+    }
+}
+// Lane 4 t + L (t < kNT) collects the term-t scale codes of blocks 4 L .. 4 L + 3.
+__device__ __forceinline__ uint32_t gather_scales(uint32_t scw) {
+    const int lane = threadIdx.x & 31, t = (lane >> 2) & 3, L = lane & 3;
+    uint32_t g = 0;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const uint32_t w = __shfl_sync(0xffffffffu, scw, 2 * (4 * L + m));
+        g |= ((w >> (8 * t)) & 0xffu) << (8 * m);
+    }
+    return g;
+}
+// Rows kNT i + t of one stage of a tile image (128 rows, 128-byte swizzle, scales after the code
+// rows): each term row is one full 128-byte line (a 4-byte store per lane); the kNT rows' scale
+// records are 16 kNT contiguous bytes, lanes 4 t + L store 4 each.
+__device__ __forceinline__ void put_pair_rows(uint8_t* img, int i, const uint32_t (&code)[kNT],
+                                              uint32_t gsc) {
+    const int lane = threadIdx.x & 31, blk = lane >> 1, hf = lane & 1;
+#pragma unroll
+    for (int t = 0; t < kNT; ++t) {
+        const int n = kNT * i + t;
+        *reinterpret_cast<uint32_t*>(img + n * 128 + (((blk >> 1) ^ (n & 7)) << 4) + ((blk & 1) << 3) + 4 * hf) = code[t];
+    }
+    if (lane < 4 * kNT) *reinterpret_cast<uint32_t*>(img + 128 * 128 + kNT * i * 16 + 4 * lane) = gsc;
+}
 
 struct Pf4Layout {
     size_t hdr, cnt, base, cursor, tile_base, tiles, ent_tok, ent_w, ent_of, ent_pos, ent_xk,
@@ -136,10 +204,10 @@ __global__ void pf4_count(const __grid_constant__ Pf4Params P) {
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
         const int t = p / P.top_k, j = p - t * P.top_k;
         const int s = P.ids[(int64_t)t * P.ids_stride + j];
-        if (s >= 0 && s < S)
-            atomicAdd(&cnt[s], 1);
-        else
-            atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_BAD_SLOT);
+        const bool ok = s >= 0 && s < S;
+        const unsigned same = __match_any_sync(__activemask(), ok ? s : -1);
+        if (ok && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&cnt[s], __popc(same));
+        if (!ok) atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_BAD_SLOT);
     }
 }
 
@@ -198,8 +266,16 @@ __global__ void pf4_scatter(const __grid_constant__ Pf4Params P) {
         int e = -1, key = -1;
         if (j < P.top_k) {
             const int s = P.ids[(int64_t)t * P.ids_stride + j];
-            if (s >= 0 && s < S) {
-                e = atomicAdd(&cursor[s], 1);  // order inside a key does not change any result
+            const bool ok = s >= 0 && s < S;
+            // one atomic per distinct slot of the warp; the order of entries inside a key
+            // changes no result
+            const unsigned same = __match_any_sync(__activemask(), ok ? s : -1);
+            const int lead = __ffs(same) - 1, ln = threadIdx.x & 31;
+            int e0 = 0;
+            if (ok && ln == lead) e0 = atomicAdd(&cursor[s], __popc(same));
+            e0 = __shfl_sync(same, e0, lead);
+            if (ok) {
+                e = e0 + __popc(same & ((1u << ln) - 1u));
                 key = s;
                 ent_tok[e] = t;
                 ent_w[e] = P.w[(int64_t)t * P.w_stride + j];
@@ -218,25 +294,37 @@ __global__ void pf4_scatter(const __grid_constant__ Pf4Params P) {
     }
 }
 
-// One block of 128 threads per token: the row exponent and the shared gate, then its 16-blocks
-// as NVFP4 terms (4 lanes per block, 32 blocks per round) into the gate_up image row of every
-// entry of the token.
+// One block of 128 threads per token: the row exponent and the shared gate, then each K stage
+// (warp w: stages w, w + 4, ...) as kNT NVFP4 terms into the gate_up image row of every entry
+// of the token.  The values stay in registers between the two passes; the entries' image
+// positions sit in shared memory.
 __global__ void __launch_bounds__(128) pf4_quant_x(const __grid_constant__ Pf4Params P) {
     __shared__ float red[8];
-    __shared__ int ents[33];  // top-k (<= 32) + the shared expert
+    __shared__ int epos[33];  // image position (tile << 8 | row) of each entry, -1: none
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int H = P.pool.hidden, K1 = P.top_k + 1, KSG = P.L.ksg;
+    const int K1 = P.top_k + 1, KSG = P.L.ksg;  // KSG = H / 256 <= 32
     const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
-    if (tid < K1) ents[tid] = qws<int>(P, P.L.ent_of)[t * K1 + tid];
+    int ent = -1;
+    if (tid < K1) {
+        ent = qws<int>(P, P.L.ent_of)[t * K1 + tid];
+        epos[tid] = ent >= 0 ? qws<int>(P, P.L.ent_pos)[ent] : -1;
+    }
+    uint4 xv[8];
     float am = 0.f, dot = 0.f;
-    for (int i = tid * 8; i < H; i += 128 * 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
-        const uint16_t* u = reinterpret_cast<const uint16_t*>(&v);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float f = bf16_bits_to_f32(u[k]);
-            am = fmaxf(am, fabsf(f));
-            if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
+    for (int m = 0; m < 8; ++m) {
+        const int st = warp + 4 * m;
+        xv[m] = make_uint4(0u, 0u, 0u, 0u);
+        if (st < KSG) {
+            const int off = 256 * st + 8 * lane;
+            xv[m] = *reinterpret_cast<const uint4*>(xr + off);
+            const uint32_t w4[4] = {xv[m].x, xv[m].y, xv[m].z, xv[m].w};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float f = __uint_as_float(k & 1 ? w4[k >> 1] & 0xffff0000u : w4[k >> 1] << 16);
+                am = fmaxf(am, fabsf(f));
+                if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[off + k]), dot);
+            }
         }
     }
 #pragma unroll
@@ -247,48 +335,47 @@ __global__ void __launch_bounds__(128) pf4_quant_x(const __grid_constant__ Pf4Pa
     if (lane == 0) red[warp] = am, red[4 + warp] = dot;
     __syncthreads();
     const int ke = fp4_row_exp(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])));
-    if (tid < K1 && ents[tid] >= 0) {
-        const int e = ents[tid];
-        float f = qws<float>(P, P.L.ent_w)[e];
+    if (ent >= 0) {
+        float f = qws<float>(P, P.L.ent_w)[ent];
         if (tid == P.top_k && P.shared_gate)
             f *= 1.0f / (1.0f + expf(-(red[4] + red[5] + red[6] + red[7])));
-        qws<int>(P, P.L.ent_xk)[e] = ke;
-        qws<float>(P, P.L.ent_fac)[e] = f;
+        qws<int>(P, P.L.ent_xk)[ent] = ke;
+        qws<float>(P, P.L.ent_fac)[ent] = f;
     }
-    const int* ent_pos = qws<int>(P, P.L.ent_pos);
     uint8_t* ximg = P.ws + P.L.ximg;
-    for (int b0 = 0; b0 < H / 16; b0 += 32) {
-        const int b = b0 + (tid >> 2), q = tid & 3;  // H / 16 is a multiple of 32 (H % 512 == 0)
-        const uint2 xv = *reinterpret_cast<const uint2*>(xr + b * 16 + 4 * q);
-        float v[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xffff0000u),
-                      __uint_as_float(xv.y << 16), __uint_as_float(xv.y & 0xffff0000u)};
-        uint16_t two[kFp4Terms];
-        uint8_t sc[kFp4Terms];
-        quant4_terms(v, ke, two, sc);
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const int st = warp + 4 * m;
+        if (st >= KSG) break;
+        const uint32_t w4[4] = {xv[m].x, xv[m].y, xv[m].z, xv[m].w};
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            v[k] = __uint_as_float(k & 1 ? w4[k >> 1] & 0xffff0000u : w4[k >> 1] << 16);
+        uint32_t code[kNT], scw;
+        quant_pair_terms(v, ke, code, scw);
+        const uint32_t gsc = gather_scales(scw);
         for (int j = 0; j < K1; ++j) {
-            const int e = ents[j];
-            if (e < 0) continue;
-            const int pos = ent_pos[e];
-            uint8_t* img = ximg + ((int64_t)(pos >> 8) * KSG + b / 16) * kImg;
-            put4(img, 128, pos & 0xff, b % 16, two, sc);
+            const int pos = epos[j];
+            if (pos < 0) continue;
+            put_pair_rows(ximg + ((int64_t)(pos >> 8) * KSG + st) * kImg, pos & 0xff, code, gsc);
         }
     }
 }
 
-// One warp per entry (8 per block): the h row's exponent, then its 16-blocks as NVFP4 terms into
-// the entry's row of the down image (lane l: values 128 m + 4 l .. + 4, m < I / 128).
+// One warp per entry (8 per block): the h row's exponent, then each K stage of the row as kNT
+// NVFP4 terms into the entry's row of the down image (lane l: values 256 s + 8 l .. + 8).
 constexpr int kActWarps = 8;
-template <int MC>  // I / 128
+template <int NS>  // I / 256
 __global__ void __launch_bounds__(32 * kActWarps) pf4_act(const __grid_constant__ Pf4Params P) {
     const int e = blockIdx.x * kActWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (e >= qws<int>(P, P.L.hdr)[QH_N_ENT]) return;  // the whole warp: the quantiser shuffles
-    const int I = 128 * MC, KSD = P.L.ksd;
-    const float* hrow = qws<float>(P, P.L.h32) + (int64_t)e * I;
-    float4 hv[MC];
+    const float* hrow = qws<float>(P, P.L.h32) + (int64_t)e * (256 * NS);
+    float4 hv[2 * NS];
     float am = 0.f;
 #pragma unroll
-    for (int m = 0; m < MC; ++m) {
-        hv[m] = *reinterpret_cast<const float4*>(hrow + 128 * m + 4 * lane);
+    for (int m = 0; m < 2 * NS; ++m) {
+        hv[m] = *reinterpret_cast<const float4*>(hrow + 256 * (m >> 1) + 8 * lane + 4 * (m & 1));
         am = fmaxf(am, fmaxf(fmaxf(fabsf(hv[m].x), fabsf(hv[m].y)), fmaxf(fabsf(hv[m].z), fabsf(hv[m].w))));
     }
 #pragma unroll
@@ -298,14 +385,12 @@ __global__ void __launch_bounds__(32 * kActWarps) pf4_act(const __grid_constant_
     const int pos = qws<int>(P, P.L.ent_pos)[e];
     uint8_t* himg = P.ws + P.L.himg;
 #pragma unroll
-    for (int m = 0; m < MC; ++m) {
-        const int blk = (lane >> 2) + 8 * m;
-        float v[4] = {hv[m].x, hv[m].y, hv[m].z, hv[m].w};
-        uint16_t two[kFp4Terms];
-        uint8_t sc[kFp4Terms];
-        quant4_terms(v, kh, two, sc);
-        uint8_t* img = himg + ((int64_t)(pos >> 8) * KSD + blk / 16) * kImg;
-        put4(img, 128, pos & 0xff, blk % 16, two, sc);
+    for (int s = 0; s < NS; ++s) {
+        float v[8] = {hv[2 * s].x, hv[2 * s].y, hv[2 * s].z, hv[2 * s].w,
+                      hv[2 * s + 1].x, hv[2 * s + 1].y, hv[2 * s + 1].z, hv[2 * s + 1].w};
+        uint32_t code[kNT], scw;
+        quant_pair_terms(v, kh, code, scw);
+        put_pair_rows(himg + ((int64_t)(pos >> 8) * NS + s) * kImg, pos & 0xff, code, gather_scales(scw));
     }
 }
 
@@ -555,9 +640,9 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                 for (int q = 0; q < 4; ++q) {
                     float a = 0.f, b = 0.f;
 #pragma unroll
-                    for (int t = kFp4Terms - 1; t >= 0; --t) {
-                        a = fmaf(__uint_as_float(d0[kFp4Terms * q + t]), fp4_exp2(-2 * t), a);
-                        b = fmaf(__uint_as_float(d1[kFp4Terms * q + t]), fp4_exp2(-2 * t), b);
+                    for (int t = kNT - 1; t >= 0; --t) {
+                        a = fmaf(__uint_as_float(d0[kNT * q + t]), fp4_exp2(-2 * t), a);
+                        b = fmaf(__uint_as_float(d1[kNT * q + t]), fp4_exp2(-2 * t), b);
                     }
                     v0[4 * ch + q] = a;
                     v1[4 * ch + q] = b;
@@ -630,11 +715,11 @@ __global__ void pf4_status(const __grid_constant__ Pf4Params P) {
 
 }  // namespace
 
-// Shapes and banks the FP4 prefill covers (NVFP4, H a multiple of 512, I of 256 up to 1536,
+// Shapes and banks the FP4 prefill covers (NVFP4, H a multiple of 512 up to 8192, I of 256 up to 1536,
 // every bank usable by TMA).
 bool prefill_fp4_ok(const nvmoe_ffn_args* a) {
     const nvmoe_expert_pool& p = *a->pool;
-    if (p.quant != NVMOE_Q_NVFP4 || p.hidden % 512 != 0 || p.inter % 256 != 0 ||
+    if (p.quant != NVMOE_Q_NVFP4 || p.hidden % 512 != 0 || p.hidden > 8192 || p.inter % 256 != 0 ||
         p.inter > 1536 || a->top_k > 32)
         return false;
     CUtensorMap m[6];
@@ -689,13 +774,13 @@ int prefill_fp4_run(const nvmoe_ffn_args* a, cudaStream_t st) {
     NVMOE_CUDA_TRY(cudaFuncSetAttribute(pf4_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
     pf4_gemm<0><<<sms, kGThreads, kGSmem, st>>>(P);
     const int act_blocks = (P.L.n_ent_max + kActWarps - 1) / kActWarps;
-    switch (I / 128) {  // I is a multiple of 256 up to 1536
+    switch (I / 256) {  // I is a multiple of 256 up to 1536
+        case 1: pf4_act<1><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
         case 2: pf4_act<2><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        case 3: pf4_act<3><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
         case 4: pf4_act<4><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
-        case 6: pf4_act<6><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
-        case 8: pf4_act<8><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
-        case 10: pf4_act<10><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
-        default: pf4_act<12><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        case 5: pf4_act<5><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
+        default: pf4_act<6><<<act_blocks, 32 * kActWarps, 0, st>>>(P); break;
     }
     pf4_gemm<1><<<sms, kGThreads, kGSmem, st>>>(P);
     const int64_t n4 = (int64_t)a->n_tok * (H / 4);
