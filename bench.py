@@ -33,7 +33,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "MoE-layer decode tokens/s (Qwen3.8-shaped NVFP4 layer, 128-slot VRAM expert cache)"
 UNIT = "layer-tokens/s"
-FP4_TERMS = 4              # NVFP4 residual terms per activation row in the FP4 prefill
+FP4_TERMS = 3              # NVFP4 residual terms per activation row in the FP4 prefill
 FP4_NOMINAL_TFLOPS = 9000.0  # B200 dense FP4, nominal
 
 

@@ -2,22 +2,23 @@
 // token-sorted grouped GEMM of tcgen05.mma kind::mxf4nvf4 (E2M1 x E2M1, one UE4M3 scale per 16
 // on both operands, fp32 accumulators in tensor memory).  The weights go from the slot banks to
 // shared memory by TMA (128-byte swizzle) and into the MMA unchanged; the activations enter as
-// kNT NVFP4 residual terms per row (the quantiser of fp4_common.cuh, two lanes per block), so the
-// result matches the f16 path and the oracle within the FFN tolerance.
+// kNT = 3 NVFP4 residual terms per row (about bf16 precision: each term quantises what the
+// earlier ones left, two lanes per 16-block), so the result matches the f16 path and the oracle
+// within the FFN tolerance.
 //
 // Same contract as nvmoe_moe_ffn_prefill's f16 path (nvme_offload_cache.py:1957-2013; llama.cpp
 // mul_mat_id for n_tokens > 1, scripts/moe_cache_probe.cpp:1668-1684):
 //   y[t] = sum_j w[t,j] * down_s( silu(gate_s x[t]) * up_s x[t] )  (+ the shared expert).
 // Steps (one stream, kernel boundaries order them):
-//   count / scan / scatter — entries sorted by key (slot, or the shared expert), tiles of <= 32
+//   count / scan / scatter — entries sorted by key (slot, or the shared expert), tiles of <= 42
 //                            entries per key, each entry's (tile, row)
-//   quant_x  — per token: the row exponent, the shared gate, then each 16-block as 4 NVFP4 terms
+//   quant_x  — per token: the row exponent, the shared gate, then each K stage as 3 NVFP4 terms
 //              into the gate_up B image of every tile row that holds the token
-//   gate_up  — persistent: units (tile, 64-row j-block), M = 64 gate + 64 up rows, N = 4 x
-//              entries, K = H; epilogue h = silu(gate) * up (fp32)
-//   act      — per entry: h row exponent, its 16-blocks as NVFP4 terms into the down B image
-//   down     — persistent: units (tile, 128-row block of H), K = I; epilogue y_part[e] = w_e *
-//              row (fp32)
+//   gate_up  — persistent: units (tile, 128-row j-block), gate and up blocks of M = 128 against
+//              one B image, N = 3 x entries, K = H; epilogue h = silu(gate) * up (fp32)
+//   act      — per entry: h row exponent, its K stages as NVFP4 terms into the down B image
+//   down     — persistent: units (tile, 256 rows of H as two M = 128 blocks), K = I; epilogue
+//              y_part[e] = w_e * row (fp32)
 //   combine  — y[t] = sum over t's entries in the order j = 0..k (shared last) (bf16)
 // Deterministic: every output element is one MMA accumulation and fixed-order sums.
 #include "common.cuh"
@@ -33,7 +34,8 @@ namespace nvmoe {
 using namespace fp4;
 namespace {
 
-constexpr int kTT = 32;                    // entries per tile: B rows 4 x 32 = 128
+constexpr int kNT = 3;                     // NVFP4 terms per activation row: B rows kNT i + t
+constexpr int kTT = 42;                    // entries per tile: B rows 3 x 42 = 126 of 128
 constexpr int kImg = 128 * 144;            // one K stage of a tile image (128 code rows + scales)
 // One ring stage (K = 256): two 128-row weight blocks A0, A1 (the MMAs of a stage share the
 // tile's B image), the B image, then the A0 and A1 scales.
@@ -43,7 +45,7 @@ constexpr int kOffBi = 32768;
 constexpr int kOffAs = kOffBi + kImg;
 constexpr int kStg = kOffAs + 4096;        // 55296, every byte of it arrives by TMA
 static_assert(kStg % 1024 == 0, "stage layout");
-constexpr int kEpiWarps = 8;               // two per TMEM lane quadrant, 16 entries each
+constexpr int kEpiWarps = 8;               // two per TMEM lane quadrant, 21 entries each
 // + 4 scale-factor warps, the producer, the MMA issuer and the unit-info warp
 constexpr int kGThreads = 32 * (kEpiWarps + 7);
 constexpr int kWSf = kEpiWarps, kWProd = kEpiWarps + 4, kWMma = kEpiWarps + 5, kWInfo = kEpiWarps + 6;
@@ -65,7 +67,8 @@ static_assert(kTmSF + 48 * kNSt <= kTmCols, "tensor memory");
 
 enum { QH_N_TILES = 0, QH_N_ENT = 1, QH_STATUS = 2 };
 
-constexpr int kNT = kFp4Terms;  // NVFP4 terms per activation row: B rows kNT i + t
+
+__device__ __forceinline__ int pf4_npad(int nr) { return (kNT * nr + 7) & ~7; }  // MMA N
 
 // ---- activation quantiser for the tile images: a warp quantises one K stage (256 values, 16
 // blocks) of one row; lanes 2 blk and 2 blk + 1 hold values 8 hf .. 8 hf + 7 of block blk.
@@ -504,7 +507,7 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
             const int u = c + k * G;
             const int nr = nr_next;
             if (k + 1 < my_units) nr_next = tiles[3 * ((u + G) / UPT) + 2];
-            const uint32_t idesc = umma::idesc_mxf4(128, npad_of(nr));
+            const uint32_t idesc = umma::idesc_mxf4(128, pf4_npad(nr));
             if (k >= 1 && !wait_bar(d_empty, (k - 1) & 1, abort)) {
                 ok = false;
                 break;
@@ -553,11 +556,15 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
             const bool sh = key == S;
             const nvmoe_expert_pool& pool = sh ? P.shared : P.pool;
             const int slot = sh ? 0 : key;
-            int ex = 0;
-            float fa = 0.f;
-            if (lane < nr) {
-                ex = PH ? hk[eb + lane] : ent_xk[eb + lane];
-                if (PH) fa = ent_fac[eb + lane];
+            int ex[2] = {0, 0};
+            float fa[2] = {0.f, 0.f};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int i = lane + 32 * h;
+                if (i < nr) {
+                    ex[h] = PH ? hk[eb + i] : ent_xk[eb + i];
+                    if (PH) fa[h] = ent_fac[eb + i];
+                }
             }
             const float ga = global_of(PH ? pool.down : pool.gate, slot);
             const float gb = PH ? ga : global_of(pool.up, slot);
@@ -566,8 +573,13 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                 break;
             }
             UnitInfo& in = info[b];
-            in.eexp[lane] = ex;
-            in.efac[lane] = fa;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (lane + 32 * h < kTT) {
+                    in.eexp[lane + 32 * h] = ex[h];
+                    in.efac[lane + 32 * h] = fa[h];
+                }
+            }
             if (lane == 0) in.eb = eb, in.nr = nr, in.ga = ga, in.gb = gb;
             __syncwarp();
             if (lane == 0) mbar_arrive(&info_full[b]);
@@ -626,52 +638,56 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                 break;
             }
             umma::fence_after_sync();
-            float v0[16], v1[16];
+            // Columns 3 e + t.  Half hh reads its own group of 16 entries (columns 48 hh ..
+            // 48 hh + 47) and the last group (entries 32..41, columns 96..125), whose entries
+            // 32 + 5 hh .. + 4 it stores.
+            float g0[16], g1[16], x0[10], x1[10];
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
+            for (int i = 0; i < 16; ++i) g0[i] = g1[i] = 0.f;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) v0[4 * ch + q] = v1[4 * ch + q] = 0.f;
-                if (i0 + 4 * ch >= nr) continue;
+            for (int i = 0; i < 10; ++i) x0[i] = x1[i] = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < 5; ++ch) {
+                const int cl = ch < 3 ? ch : ch - 3;  // chunk within its group
+                const int cb = ch < 3 ? 48 * hh + 16 * cl : 96 + 16 * cl;
+                if ((ch < 3 ? i0 : 32) + (16 * cl) / 3 >= nr) continue;
                 uint32_t d0[16], d1[16];
-                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + 64 * hh + 16 * ch), d0);
-                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + 128 + 64 * hh + 16 * ch), d1);
+                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + cb), d0);
+                umma::ld_x16(umma::lane_addr(tm, warp, kTmD + 128 + cb), d1);
                 umma::wait_ld();
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float a = 0.f, b = 0.f;
-#pragma unroll
-                    for (int t = kNT - 1; t >= 0; --t) {
-                        a = fmaf(__uint_as_float(d0[kNT * q + t]), fp4_exp2(-2 * t), a);
-                        b = fmaf(__uint_as_float(d1[kNT * q + t]), fp4_exp2(-2 * t), b);
+                for (int j = 0; j < 16; ++j) {
+                    const int col = 16 * cl + j, le = col / 3;
+                    const float f = fp4_exp2(-2 * (col % 3));
+                    if (ch < 3) {
+                        g0[le] = fmaf(__uint_as_float(d0[j]), f, g0[le]);
+                        g1[le] = fmaf(__uint_as_float(d1[j]), f, g1[le]);
+                    } else if (le < 10) {
+                        x0[le] = fmaf(__uint_as_float(d0[j]), f, x0[le]);
+                        x1[le] = fmaf(__uint_as_float(d1[j]), f, x1[le]);
                     }
-                    v0[4 * ch + q] = a;
-                    v1[4 * ch + q] = b;
                 }
             }
             umma::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(d_empty);
-            if (PH == 0) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int e = i0 + i;
-                    if (e < nr) {
-                        const float f = fp4_exp2(-in.eexp[e]);
-                        h32[(int64_t)(eb + e) * I + sub * 128 + r] = silu(v0[i] * f * ga) * (v1[i] * f * gb);
-                    }
+            auto emit = [&](int e, float a, float bb) {
+                if (PH == 0) {
+                    const float f = fp4_exp2(-in.eexp[e]);
+                    h32[(int64_t)(eb + e) * I + sub * 128 + r] = silu(a * f * ga) * (bb * f * gb);
+                } else {
+                    const float f = fp4_exp2(-in.eexp[e]) * in.efac[e] * ga;
+                    float* yp = ypart + (int64_t)(eb + e) * H + sub * 256 + r;
+                    yp[0] = a * f;
+                    yp[128] = bb * f;
                 }
-            } else {
+            };
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int e = i0 + i;
-                    if (e < nr) {
-                        const float f = fp4_exp2(-in.eexp[e]) * in.efac[e] * ga;
-                        float* yp = ypart + (int64_t)(eb + e) * H + sub * 256 + r;
-                        yp[0] = v0[i] * f;
-                        yp[128] = v1[i] * f;
-                    }
-                }
-            }
+            for (int i = 0; i < 16; ++i)
+                if (i0 + i < nr) emit(i0 + i, g0[i], g1[i]);
+#pragma unroll
+            for (int i = 0; i < 10; ++i)
+                if (i / 5 == hh && 32 + i < nr) emit(32 + i, x0[i], x1[i]);
             __syncwarp();
             if (lane == 0) mbar_arrive(&info_empty[b]);
         }
