@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--cpu-baseline-seconds", type=float, default=12.0)
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="also time one prefill layer of this many tokens (0: skip)")
+    ap.add_argument("--only-prefill", action="store_true",
+                    help="time the prefill layer alone on one GPU and print its object")
     return ap.parse_args()
 
 
@@ -122,6 +124,11 @@ class ClockSampler:
         loaded = [r for r in rows if r[2] > 200.0] or rows
         return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": rows[0][1],
                 "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    return json.loads(p.read_text()) if p.exists() else None
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -259,8 +266,7 @@ def run_nvmoe(a, rank, world, local_rank):
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(tt.item())
 
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (
-        ROOT / "MEASURED_PEAKS.json").exists() else None
+    peaks = load_peaks()
     hbm_peak = peaks["hbm_gbs"] if peaks else 6650.0
     achieved = (ffn_bytes / n_ffn) / ((ffn_ms / n_ffn) / 1e3) / 1e9
     step_bytes = float(((U[a.warmup:] + 1) * stack.bytes_per_expert).sum()) / a.steps
@@ -439,6 +445,12 @@ def main():
             print(json.dumps(run_reference(a)), flush=True)
         return
     import torch
+    if a.only_prefill:
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        if rank == 0:
+            print(json.dumps({"prefill": run_prefill(a, dev, load_peaks())}), flush=True)
+        return
     if world > 1:
         import datetime
         torch.cuda.set_device(local_rank)
