@@ -46,8 +46,8 @@ __device__ __forceinline__ void cp_async_wait_all() {
 
 // Shared-memory layout of the front kernel (ints unless noted).
 struct FrontSmem {
-    int sor, ris, lu, first, uniq, uslot, miss_r, act, cnt, gbase, sids, sw, ent_tok, ent_w, keys,
-        total;
+    int sor, ris, lu, first, uniq, uslot, miss_r, act, cnt, gbase, aidx, sids, sw, pe, ent_tok,
+        ent_w, keys, total;
 };
 __host__ __device__ inline FrontSmem front_smem(int E, int S, int n, int n_ent) {
     int s2 = 1;
@@ -76,9 +76,13 @@ __host__ __device__ inline FrontSmem front_smem(int E, int S, int n, int n_ent) 
     o += 4 * S;
     L.gbase = o;
     o += 4 * S;
+    L.aidx = o;
+    o += 4 * S;
     L.sids = o;
     o += 4 * n;
     L.sw = o;
+    o += 4 * n;
+    L.pe = o;
     o += 4 * n;
     L.ent_tok = o;
     o += 4 * n_ent;
@@ -89,7 +93,7 @@ __host__ __device__ inline FrontSmem front_smem(int E, int S, int n, int n_ent) 
 }
 
 // Token rows -> f16 and the shared-expert gate, one warp per token (no block barrier).
-__device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, int lane, bool dry) {
+__device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, int lane) {
     const int H = P.pool.hidden;
     const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
     __half* x16 = wsp<__half>(P, P.L.x16) + (int64_t)t * H;
@@ -105,17 +109,17 @@ __device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, i
             amax = fmaxf(amax, fabsf(f));
             if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
         }
-        if (!P.use_fp4 && !dry) *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+        if (!P.use_fp4) *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
     }
     if (P.use_fp4) {  // the row's FP4 term exponent
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0 && !dry) wsp<int>(P, P.L.xk)[t] = fp4_row_exp(amax);
+        if (lane == 0) wsp<int>(P, P.L.xk)[t] = fp4_row_exp(amax);
     }
     if (P.shared_gate) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        if (lane == 0 && !dry) wsp<float>(P, P.L.sg)[t] = 1.0f / (1.0f + expf(-dot));
+        if (lane == 0) wsp<float>(P, P.L.sg)[t] = 1.0f / (1.0f + expf(-dot));
     }
 }
 
@@ -149,20 +153,19 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     float* sw = reinterpret_cast<float*>(smem + L.sw);
     int* ent_tok_s = reinterpret_cast<int*>(smem + L.ent_tok);
     float* ent_w_s = reinterpret_cast<float*>(smem + L.ent_w);
+    int* aidx = reinterpret_cast<int*>(smem + L.aidx);
+    int* pe = reinterpret_cast<int*>(smem + L.pe);
 
-    // The whole step runs twice through the same code (a loop, not unrolled): first dry, every
-    // global store suppressed, while the kernel before this one is still running, which brings
-    // this code into the SM's instruction cache (it is evicted between layer steps); then for
-    // real once that kernel's results exist.
+    // Everything but the FFN workspace runs before the dependency wait, while the kernel before
+    // this one (normally the previous layer's FFN, which leaves an SM free for this CTA) is
+    // still running: routing, the remap with its table / miss-list / slot-id writes, and the
+    // grouping in shared memory.  None of that is read by the kernels in flight: the tables,
+    // slot ids and weights belong to this layer, and the miss list was consumed by a refill
+    // that completed before the previous FFN passed its own wait.  The router logits must be
+    // complete when the previous kernel triggers its dependents.  After the wait: the token
+    // rows (read only now) and the workspace the previous FFN reads.
     grid_dep_launch();
-#pragma unroll 1
-    for (int pass = 0; pass < 2; ++pass) {
-    const bool dry = pass == 0;
-    if (!dry) {
-        __syncthreads();
-        grid_dep_wait();
-    }
-    // ---- A. one round trip: table prefetch (async), logits (router), token rows (convert)
+    // ---- A. one round trip: table prefetch (async) while the warps route their tokens
     for (int e = tid; e < E; e += nthr) cp_async4(sor + e, F.rp.t.slot_of_real + id_base + e);
     for (int s = tid; s < S; s += nthr) {
         cp_async4(ris + s, F.rp.t.real_in_slot + s);
@@ -175,22 +178,13 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         s_err = NVMOE_OK;
         s_step = (int)(*F.rp.t.current_step + 1u);
     }
-    const int n_route_warps = min(nw, n_tok);
-    if (warp < n_route_warps) {
-        for (int t = warp; t < n_tok; t += n_route_warps)
-            router_topk_warp(F.logits + (int64_t)t * F.lstride, E, K, F.mode, F.bias,
-                             F.norm_topk, F.scaling, sids + t * K, sw + t * K);
-    }
-    {  // token conversion by the warps the router leaves idle (all warps if none are idle)
-        const int c0 = (n_route_warps < nw) ? n_route_warps : 0;
-        const int nconv = nw - c0;
-        if (warp >= c0)
-            for (int t = warp - c0; t < n_tok; t += nconv) front_convert_token(P, t, lane, dry);
-    }
+    for (int t = warp; t < n_tok; t += nw)
+        router_topk_warp(F.logits + (int64_t)t * F.lstride, E, K, F.mode, F.bias, F.norm_topk,
+                         F.scaling, sids + t * K, sw + t * K);
     cp_async_wait_all();
     __syncthreads();
 
-    // ---- B. remap in shared memory
+    // ---- B. remap in shared memory; this layer's tables and the miss list are written here
     for (int p = tid; p < n; p += nthr) {
         const int id = sids[p];
         if (id < 0 || id >= E)
@@ -253,13 +247,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
                 const int s = (int)(keys[j] & 0xffffffull);
                 const int ev = ris[s];
                 uslot[r] = s;
-                if (!dry) {
-                    if (ev >= 0) F.rp.t.slot_of_real[ev] = -1;
-                    F.rp.t.real_in_slot[s] = id_base + e;
-                    M.miss_ids[j] = e;
-                    M.miss_slots[j] = s;
-                    M.evicted_ids[j] = ev;
-                }
+                if (ev >= 0) F.rp.t.slot_of_real[ev] = -1;
+                F.rp.t.real_in_slot[s] = id_base + e;
+                M.miss_ids[j] = e;
+                M.miss_slots[j] = s;
+                M.evicted_ids[j] = ev;
             }
             __syncthreads();
         }
@@ -267,27 +259,23 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         const nvmoe_miss_list& M = F.rp.m;
         for (int r = tid; r < nuniq; r += nthr) {
             const int e = uniq[r], s = uslot[r];
-            if (!dry) {
-                F.rp.t.slot_of_real[id_base + e] = s;
-                F.rp.t.slot_last_used[s] = step;
-                M.unique_ids[r] = e;
-                M.unique_slot[r] = s;
-            }
+            F.rp.t.slot_of_real[id_base + e] = s;
+            F.rp.t.slot_last_used[s] = step;
+            M.unique_ids[r] = e;
+            M.unique_slot[r] = s;
         }
-        for (int r = tid; r < nuniq && !dry; r += nthr) M.unique_hit[r] = 1;
+        for (int r = tid; r < nuniq; r += nthr) M.unique_hit[r] = 1;
         __syncthreads();
-        for (int j = tid; j < nmiss && !dry; j += nthr) M.unique_hit[miss_r[j]] = 0;
+        for (int j = tid; j < nmiss; j += nthr) M.unique_hit[miss_r[j]] = 0;
         for (int p = tid; p < n; p += nthr) {
             const int sl = uslot[first[sids[p]]];
             sids[p] = sl;
-            if (!dry) {
-                F.rp.out[p] = sl;
-                F.weights[p] = sw[p];
-            }
+            F.rp.out[p] = sl;
+            F.weights[p] = sw[p];
         }
-        if (tid == 0 && !dry) *F.rp.t.current_step = step;
+        if (tid == 0) *F.rp.t.current_step = step;
     }
-    if (tid == 0 && !dry) {
+    if (tid == 0) {
         F.rp.m.counts[0] = status == NVMOE_ERR_BAD_EXPERT_ID ? 0 : nuniq;
         F.rp.m.counts[1] = status == NVMOE_OK ? nmiss : 0;
         F.rp.m.counts[2] = status;
@@ -295,22 +283,21 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     }
     int* hdr = wsp<int>(P, P.L.hdr);
     if (status != NVMOE_OK) {  // the FFN gets nothing to do (y = 0) and the status
-        if (tid == 0 && !dry) {
+        grid_dep_wait();
+        if (tid == 0) {
             hdr[HDR_N_GROUPS] = 0;
             hdr[HDR_N_ACTIVE] = 0;
             hdr[HDR_N_ENT] = 0;
             hdr[HDR_STATUS] = status;
             if (P.status) *P.status = status;
         }
-        continue;  // (the real pass is the last)
+        return;
     }
     __syncthreads();
 
-    // ---- C. FFN grouping from the slot ids in shared memory (ffn_group_block, staged)
-    if (!dry) reset_phase_counters(P);
+    // ---- C. FFN grouping from the slot ids, in shared memory (ffn_group_block, staged)
     for (int p = tid; p < n; p += nthr) atomicAdd(&cnt[sids[p]], 1);
     __syncthreads();
-    int* desc = wsp<int>(P, P.L.grp_desc);
     int n_act = 0, n_ent = 0, n_grp = 0;
     for (int base = 0; base < S; base += nthr) {
         const int s = base + tid;
@@ -320,59 +307,64 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
         const int re = block_exclusive_scan(c, warp_sums, &tot_e);
         const int rg = block_exclusive_scan(ng, warp_sums, &tot_g);
-        if (s < S) act[s] = c > 0 ? n_ent + re : -1;  // entry base of the slot
-        if (s < S) gbase[s] = n_grp + rg;               // first group of the slot
-        if (c > 0) {
-            cnt[s] = n_ent + re;  // scatter cursor
-            if (!dry) {
-                wsp<int>(P, P.L.active_slot)[n_act + ra] = s;
-                wsp<int>(P, P.L.tok_cnt)[n_act + ra] = c;
-            }
-            for (int i = 0; i < ng && !dry; ++i) {
-                int* d = desc + (int64_t)(n_grp + rg + i) * kDescInts;
-                d[GD_SLOT] = s;
-                d[GD_POOL] = 0;
-                d[GD_E0] = n_ent + re + i * P.grp_tok;
-                d[GD_NT] = min(P.grp_tok, c - i * P.grp_tok);
-            }
+        if (s < S) {
+            act[s] = c > 0 ? n_ent + re : -1;  // entry base of the slot
+            gbase[s] = n_grp + rg;              // first group of the slot
+            aidx[s] = n_act + ra;               // its place in the active-slot list
         }
+        if (c > 0) cnt[s] = n_ent + re;  // scatter cursor
         n_act += tot_a;
         n_ent += tot_e;
         n_grp += tot_g;
     }
     __syncthreads();
-    int* ent_of = wsp<int>(P, P.L.ent_of);
     for (int p = tid; p < n; p += nthr) {
-        const int t = p / K, j = p - t * K;
         const int e = atomicAdd(&cnt[sids[p]], 1);
-        ent_tok_s[e] = t;
+        ent_tok_s[e] = p / K;
         ent_w_s[e] = sw[p];
-        if (!dry) ent_of[t * (K + 1) + j] = e;
+        pe[p] = e;
     }
     __syncthreads();
-    for (int e = tid; e < n_ent && !dry; e += nthr) {
-        wsp<int>(P, P.L.ent_tok)[e] = ent_tok_s[e];
-        wsp<float>(P, P.L.ent_w)[e] = ent_w_s[e];
-    }
-    for (int s = tid; s < S; s += nthr) {  // complete the routed groups' records
+
+    // ---- D. after the previous kernel: token rows and the FFN workspace
+    grid_dep_wait();
+    reset_phase_counters(P);
+    for (int t = warp; t < n_tok; t += nw) front_convert_token(P, t, lane);
+    int* desc = wsp<int>(P, P.L.grp_desc);
+    int* ent_of = wsp<int>(P, P.L.ent_of);
+    for (int s = tid; s < S; s += nthr) {  // the routed groups' records
         const int eb = act[s];
         if (eb < 0) continue;
         const int c = cnt[s] - eb;  // the cursor ended at base + count
-        for (int i = 0; i * P.grp_tok < c && !dry; ++i) {
+        wsp<int>(P, P.L.active_slot)[aidx[s]] = s;
+        wsp<int>(P, P.L.tok_cnt)[aidx[s]] = c;
+        for (int i = 0; i * P.grp_tok < c; ++i) {
             int* d = desc + (int64_t)(gbase[s] + i) * kDescInts;
+            d[GD_SLOT] = s;
+            d[GD_POOL] = 0;
+            d[GD_E0] = eb + i * P.grp_tok;
+            d[GD_NT] = min(P.grp_tok, c - i * P.grp_tok);
             finish_record(P, gbase[s] + i, d, ent_tok_s + eb + i * P.grp_tok,
                           ent_w_s + eb + i * P.grp_tok);
         }
     }
+    for (int p = tid; p < n; p += nthr) {
+        const int t = p / K, j = p - t * K;
+        ent_of[t * (K + 1) + j] = pe[p];
+    }
+    for (int e = tid; e < n_ent; e += nthr) {
+        wsp<int>(P, P.L.ent_tok)[e] = ent_tok_s[e];
+        wsp<float>(P, P.L.ent_w)[e] = ent_w_s[e];
+    }
     if (P.has_shared) {
         const int ngs = (n_tok + P.grp_tok - 1) / P.grp_tok;
-        for (int t = tid; t < n_tok && !dry; t += nthr) {
+        for (int t = tid; t < n_tok; t += nthr) {
             const int e = n_ent + t;
             wsp<int>(P, P.L.ent_tok)[e] = t;
             wsp<float>(P, P.L.ent_w)[e] = 1.0f;
             ent_of[t * (K + 1) + K] = e;
         }
-        for (int i = tid; i < ngs && !dry; i += nthr) {
+        for (int i = tid; i < ngs; i += nthr) {
             int* d = desc + (int64_t)(n_grp + i) * kDescInts;
             const int nt = min(P.grp_tok, n_tok - i * P.grp_tok);
             d[GD_SLOT] = 0;
@@ -384,7 +376,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
             for (int k = 0; k < kGroupMaxTok; ++k) toks[k] = i * P.grp_tok + k;
             finish_record(P, n_grp + i, d, toks, nullptr);
         }
-        if (tid == 0 && !dry) {
+        if (tid == 0) {
             wsp<int>(P, P.L.active_slot)[n_act] = 0;
             wsp<int>(P, P.L.tok_cnt)[n_act] = n_tok;
         }
@@ -392,16 +384,15 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         n_ent += n_tok;
         n_grp += ngs;
     } else {
-        for (int t = tid; t < n_tok && !dry; t += nthr) ent_of[t * (K + 1) + K] = -1;
+        for (int t = tid; t < n_tok; t += nthr) ent_of[t * (K + 1) + K] = -1;
     }
-    if (tid == 0 && !dry) {
+    if (tid == 0) {
         hdr[HDR_N_GROUPS] = n_grp;
         hdr[HDR_N_ACTIVE] = n_act;
         hdr[HDR_N_ENT] = n_ent;
         hdr[HDR_STATUS] = NVMOE_OK;
         if (P.status) *P.status = NVMOE_OK;
     }
-    }  // pass
 }
 
 }  // namespace
@@ -465,6 +456,7 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
     const size_t smem = (size_t)front_smem(t.n_expert, t.cache_size, (int)n, (int)n + a->n_tok).total;
     if (smem > 200 * 1024) return NVMOE_ERR_UNSUPPORTED;
     cudaStream_t st = (cudaStream_t)stream;
+    F.fp.spare_sm = 1;
     if (smem > 48 * 1024)
         NVMOE_CUDA_TRY(cudaFuncSetAttribute(decode_front_kernel,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

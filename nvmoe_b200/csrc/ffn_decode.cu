@@ -691,8 +691,9 @@ int launch_fmt(FfnParams& P, cudaStream_t st) {
     NVMOE_CUDA_TRY(
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FL.total));
     // at most one CTA per SM and no more CTAs than SMs: every CTA is resident, so the down
-    // phase's waits on other CTAs' gate_up rows always end
-    const int grid = sms;
+    // phase's waits on other CTAs' gate_up rows always end.  In a decode layer step one SM is
+    // left to the next step's front kernel, which then runs while this FFN does.
+    const int grid = sms - (P.spare_sm && sms > 1 ? 1 : 0);
     const cudaError_t e =
         launch_pdl(kern, dim3(grid), dim3(kFusedThreads), (size_t)FL.total, st, true, P, FL);
     return cuda_status("ffn_fused launch", e);
