@@ -22,9 +22,9 @@ enum {
     GD_TOK = 4,     // token of each entry (8)
     GD_RT = 12,     // (stage copies only) row tile of the work item
     GD_GID = 13,    // (stage copies only) group index
-    GD_GGLOB = 16,  // float: gate global scale of the slot (1 when the bank has none)
-    GD_UGLOB = 17,  // float: up global scale
-    GD_DGLOB = 18,  // float: down global scale
+    GD_GGLOB = 16,  // unused (the FFN reads the slot's global scales from the pool when it
+    GD_UGLOB = 17,  //   runs, after any refill of the slot; the grouping may run before it)
+    GD_DGLOB = 18,
     GD_W = 20,      // float: router weight of each entry (8); 1 for the shared expert
 };
 
@@ -141,12 +141,12 @@ __device__ __forceinline__ float global_of(const nvmoe_matrix_bank& b, int slot)
 
 // Completes group record d (slot, pool, e0, nt already set): token of each entry, router weight
 // of each entry (w_of_entry: the group's entries' weights, or null for the shared expert, whose
-// weight is 1 and whose sigmoid gate is applied per token by the down phase), global scales,
-// and resets the group's completion counter.
+// weight is 1 and whose sigmoid gate is applied per token by the down phase), and resets the
+// group's completion counter.  No global scale: in a decode layer step the grouping runs
+// before the refill that may replace the slot's expert.
 __device__ inline void finish_record(const FfnParams& P, int grp, int* d, const int* tok_of_entry,
                                      const float* w_of_entry) {
-    const nvmoe_expert_pool& pool = d[GD_POOL] ? P.shared : P.pool;
-    const int slot = d[GD_SLOT], nt = d[GD_NT];
+    const int nt = d[GD_NT];
     float* f = reinterpret_cast<float*>(d);
     for (int k = 0; k < kGroupMaxTok; ++k) {
         d[GD_TOK + k] = k < nt ? tok_of_entry[k] : 0;
@@ -155,9 +155,7 @@ __device__ inline void finish_record(const FfnParams& P, int grp, int* d, const 
     d[GD_RT] = 0;
     d[GD_GID] = grp;
     d[14] = d[15] = d[19] = 0;
-    f[GD_GGLOB] = global_of(pool.gate, slot);
-    f[GD_UGLOB] = global_of(pool.up, slot);
-    f[GD_DGLOB] = global_of(pool.down, slot);
+    f[GD_GGLOB] = f[GD_UGLOB] = f[GD_DGLOB] = 0.f;
     for (int k = 28; k < kDescInts; ++k) d[k] = 0;
     wsp<int>(P, P.L.grp_done)[grp] = 0;
     wsp<int>(P, P.L.gcnt)[2 * grp] = 0;

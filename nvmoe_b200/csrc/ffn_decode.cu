@@ -467,7 +467,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 const uint8_t* stg = smem + (size_t)st * FL.stage_gu;
                 const int* hdr = reinterpret_cast<const int*>(stg);
                 mv[0] = hdr[GD_E0], mv[1] = hdr[GD_NT], mv[2] = hdr[GD_RT], mv[3] = hdr[GD_GID];
-                mv[4] = hdr[GD_GGLOB], mv[5] = hdr[GD_UGLOB];
+                {  // the slot's global scales from the pool itself: a refill between the
+                   // grouping and this kernel may have replaced the slot's expert
+                    const nvmoe_expert_pool& pl = hdr[GD_POOL] ? P.shared : P.pool;
+                    mv[4] = __float_as_int(global_of(pl.gate, hdr[GD_SLOT]));
+                    mv[5] = __float_as_int(global_of(pl.up, hdr[GD_SLOT]));
+                }
                 const bool has_tok = g < mv[1];
                 // B rows: the resident row of the lane's token, or the staged row g
                 const uint8_t* xb = FL.x_res ? smem + FL.off_x + (has_tok ? hdr[GD_TOK + g] : 0) * xrow
@@ -548,7 +553,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 const uint8_t* stg = dn_stage(st);
                 const int* hdr = reinterpret_cast<const int*>(stg);
                 e0 = hdr[GD_E0], nt = hdr[GD_NT];
-                dglob = __int_as_float(hdr[GD_DGLOB]);
+                dglob = global_of((hdr[GD_POOL] ? P.shared : P.pool).down, hdr[GD_SLOT]);
                 w_lo = __int_as_float(hdr[GD_W + 2 * q]);
                 w_hi = __int_as_float(hdr[GD_W + 2 * q + 1]);
                 if (hdr[GD_POOL] && sgate) {

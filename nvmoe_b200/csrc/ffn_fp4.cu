@@ -488,7 +488,9 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fp4_kernel(const __grid_const
                 tok[i] = i < nt ? __ldcg(d + GD_TOK + i) : 0;
                 wgt[i] = i < nt ? __int_as_float(__ldcg(d + GD_W + i)) : 0.f;
             }
-            const float gl = __int_as_float(__ldcg(d + (ph ? GD_DGLOB : (r < 64 ? GD_GGLOB : GD_UGLOB))));
+            const nvmoe_expert_pool& pl = pool ? P.shared : P.pool;  // (after any refill)
+            const int slot = S.g_sp[g] & 0xffffff;
+            const float gl = global_of(ph ? pl.down : (r < 64 ? pl.gate : pl.up), slot);
             const int db = k % kND;
             if (!wait_bar(&S.d_full[db], (k / kND) & 1, abort)) {
                 ok = false;
