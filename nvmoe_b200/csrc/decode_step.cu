@@ -156,14 +156,13 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     int* aidx = reinterpret_cast<int*>(smem + L.aidx);
     int* pe = reinterpret_cast<int*>(smem + L.pe);
 
-    // Everything but the FFN workspace runs before the dependency wait, while the kernel before
-    // this one (normally the previous layer's FFN, which leaves an SM free for this CTA) is
-    // still running: routing, the remap with its table / miss-list / slot-id writes, and the
-    // grouping in shared memory.  None of that is read by the kernels in flight: the tables,
-    // slot ids and weights belong to this layer, and the miss list was consumed by a refill
-    // that completed before the previous FFN passed its own wait.  The router logits must be
-    // complete when the previous kernel triggers its dependents.  After the wait: the token
-    // rows (read only now) and the workspace the previous FFN reads.
+    // Everything but the buffers shared with the kernel before this one runs before the
+    // dependency wait, while that kernel (normally the previous layer's FFN, which leaves an SM
+    // free for this CTA) is still running: routing, the remap with this layer's table, slot-id
+    // and weight writes, and the grouping in shared memory.  The router logits must be complete
+    // when the previous kernel triggers its dependents.  After the wait: the miss list (shared
+    // by the layers; the FFN before this kernel reads it while copying its own misses in), the
+    // token rows (read only now) and the FFN workspace.
     grid_dep_launch();
     // ---- A. one round trip: table prefetch (async) while the warps route their tokens
     for (int e = tid; e < E; e += nthr) cp_async4(sor + e, F.rp.t.slot_of_real + id_base + e);
@@ -241,7 +240,6 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
                     }
                     __syncthreads();
                 }
-            const nvmoe_miss_list& M = F.rp.m;
             for (int j = tid; j < nmiss; j += nthr) {
                 const int r = miss_r[j], e = uniq[r];
                 const int s = (int)(keys[j] & 0xffffffull);
@@ -249,24 +247,17 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
                 uslot[r] = s;
                 if (ev >= 0) F.rp.t.slot_of_real[ev] = -1;
                 F.rp.t.real_in_slot[s] = id_base + e;
-                M.miss_ids[j] = e;
-                M.miss_slots[j] = s;
-                M.evicted_ids[j] = ev;
+                lu[j] = (uint32_t)ev;  // the evicted id, for the miss list after the wait
             }
             __syncthreads();
         }
-        // write back: tables, distinct-id report, slot ids and weights
-        const nvmoe_miss_list& M = F.rp.m;
+        // write back: this layer's tables, slot ids and weights (the miss list, shared by the
+        // layers and read by the FFN before this kernel, is written after the wait)
         for (int r = tid; r < nuniq; r += nthr) {
             const int e = uniq[r], s = uslot[r];
             F.rp.t.slot_of_real[id_base + e] = s;
             F.rp.t.slot_last_used[s] = step;
-            M.unique_ids[r] = e;
-            M.unique_slot[r] = s;
         }
-        for (int r = tid; r < nuniq; r += nthr) M.unique_hit[r] = 1;
-        __syncthreads();
-        for (int j = tid; j < nmiss; j += nthr) M.unique_hit[miss_r[j]] = 0;
         for (int p = tid; p < n; p += nthr) {
             const int sl = uslot[first[sids[p]]];
             sids[p] = sl;
@@ -275,15 +266,18 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         }
         if (tid == 0) *F.rp.t.current_step = step;
     }
-    if (tid == 0) {
-        F.rp.m.counts[0] = status == NVMOE_ERR_BAD_EXPERT_ID ? 0 : nuniq;
-        F.rp.m.counts[1] = status == NVMOE_OK ? nmiss : 0;
-        F.rp.m.counts[2] = status;
-        F.rp.m.counts[3] = n;
-    }
+    auto write_counts = [&]() {
+        if (tid == 0) {
+            F.rp.m.counts[0] = status == NVMOE_ERR_BAD_EXPERT_ID ? 0 : nuniq;
+            F.rp.m.counts[1] = status == NVMOE_OK ? nmiss : 0;
+            F.rp.m.counts[2] = status;
+            F.rp.m.counts[3] = n;
+        }
+    };
     int* hdr = wsp<int>(P, P.L.hdr);
     if (status != NVMOE_OK) {  // the FFN gets nothing to do (y = 0) and the status
         grid_dep_wait();
+        write_counts();
         if (tid == 0) {
             hdr[HDR_N_GROUPS] = 0;
             hdr[HDR_N_ACTIVE] = 0;
@@ -295,27 +289,41 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     }
     __syncthreads();
 
-    // ---- C. FFN grouping from the slot ids, in shared memory (ffn_group_block, staged)
+    // ---- C. FFN grouping from the slot ids, in shared memory (ffn_group_block, staged).
+    // Groups in the order: hit slots, the shared expert, slots refilled in this step (so the
+    // FFN's refill copies overlap the rest).
+    int* missof = ris;  // miss index of each slot, -1: hit (the real_in_slot copy is done with)
+    for (int s = tid; s < S; s += nthr) missof[s] = -1;
+    __syncthreads();
+    for (int j = tid; j < nmiss; j += nthr) missof[uslot[miss_r[j]]] = j;
     for (int p = tid; p < n; p += nthr) atomicAdd(&cnt[sids[p]], 1);
     __syncthreads();
-    int n_act = 0, n_ent = 0, n_grp = 0;
-    for (int base = 0; base < S; base += nthr) {
-        const int s = base + tid;
-        const int c = s < S ? cnt[s] : 0;
-        const int ng = (c + P.grp_tok - 1) / P.grp_tok;
-        int tot_a, tot_e, tot_g;
-        const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
-        const int re = block_exclusive_scan(c, warp_sums, &tot_e);
-        const int rg = block_exclusive_scan(ng, warp_sums, &tot_g);
-        if (s < S) {
-            act[s] = c > 0 ? n_ent + re : -1;  // entry base of the slot
-            gbase[s] = n_grp + rg;              // first group of the slot
-            aidx[s] = n_act + ra;               // its place in the active-slot list
+    const int ngs = P.has_shared ? (n_tok + P.grp_tok - 1) / P.grp_tok : 0;
+    int n_act = 0, n_ent = 0, n_grp = 0, g_shared = 0;
+    for (int cls = 0; cls < 2; ++cls) {
+        if (cls == 1) {
+            g_shared = n_grp;
+            n_grp += ngs;
         }
-        if (c > 0) cnt[s] = n_ent + re;  // scatter cursor
-        n_act += tot_a;
-        n_ent += tot_e;
-        n_grp += tot_g;
+        for (int base = 0; base < S; base += nthr) {
+            const int s = base + tid;
+            const bool mine = s < S && ((missof[s] >= 0) == (cls == 1));
+            const int c = mine ? cnt[s] : 0;
+            const int ng = (c + P.grp_tok - 1) / P.grp_tok;
+            int tot_a, tot_e, tot_g;
+            const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
+            const int re = block_exclusive_scan(c, warp_sums, &tot_e);
+            const int rg = block_exclusive_scan(ng, warp_sums, &tot_g);
+            if (mine) {
+                act[s] = c > 0 ? n_ent + re : -1;  // entry base of the slot
+                gbase[s] = n_grp + rg;              // first group of the slot
+                aidx[s] = n_act + ra;               // its place in the active-slot list
+                if (c > 0) cnt[s] = n_ent + re;     // scatter cursor
+            }
+            n_act += tot_a;
+            n_ent += tot_e;
+            n_grp += tot_g;
+        }
     }
     __syncthreads();
     for (int p = tid; p < n; p += nthr) {
@@ -326,8 +334,23 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     }
     __syncthreads();
 
-    // ---- D. after the previous kernel: token rows and the FFN workspace
+    // ---- D. after the previous kernel: the miss list, token rows and the FFN workspace
     grid_dep_wait();
+    {
+        const nvmoe_miss_list& M = F.rp.m;
+        for (int r = tid; r < nuniq; r += nthr) {
+            M.unique_ids[r] = uniq[r];
+            M.unique_slot[r] = uslot[r];
+            M.unique_hit[r] = missof[uslot[r]] < 0 ? 1 : 0;
+        }
+        for (int j = tid; j < nmiss; j += nthr) {
+            const int r = miss_r[j];
+            M.miss_ids[j] = uniq[r];
+            M.miss_slots[j] = uslot[r];
+            M.evicted_ids[j] = (int)lu[j];
+        }
+        write_counts();
+    }
     reset_phase_counters(P);
     for (int t = warp; t < n_tok; t += nw) front_convert_token(P, t, lane);
     int* desc = wsp<int>(P, P.L.grp_desc);
@@ -346,8 +369,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
             d[GD_NT] = min(P.grp_tok, c - i * P.grp_tok);
             finish_record(P, gbase[s] + i, d, ent_tok_s + eb + i * P.grp_tok,
                           ent_w_s + eb + i * P.grp_tok);
+            if (P.rf.n_banks > 0) d[GD_MISS] = missof[s] + 1;
         }
     }
+    for (int j = tid; j < nmiss; j += nthr) wsp<int>(P, P.L.rdy)[j] = 0;
     for (int p = tid; p < n; p += nthr) {
         const int t = p / K, j = p - t * K;
         ent_of[t * (K + 1) + j] = pe[p];
@@ -357,7 +382,6 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         wsp<float>(P, P.L.ent_w)[e] = ent_w_s[e];
     }
     if (P.has_shared) {
-        const int ngs = (n_tok + P.grp_tok - 1) / P.grp_tok;
         for (int t = tid; t < n_tok; t += nthr) {
             const int e = n_ent + t;
             wsp<int>(P, P.L.ent_tok)[e] = t;
@@ -365,7 +389,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
             ent_of[t * (K + 1) + K] = e;
         }
         for (int i = tid; i < ngs; i += nthr) {
-            int* d = desc + (int64_t)(n_grp + i) * kDescInts;
+            int* d = desc + (int64_t)(g_shared + i) * kDescInts;
             const int nt = min(P.grp_tok, n_tok - i * P.grp_tok);
             d[GD_SLOT] = 0;
             d[GD_POOL] = 1;
@@ -374,7 +398,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
             int toks[kGroupMaxTok];
 #pragma unroll
             for (int k = 0; k < kGroupMaxTok; ++k) toks[k] = i * P.grp_tok + k;
-            finish_record(P, n_grp + i, d, toks, nullptr);
+            finish_record(P, g_shared + i, d, toks, nullptr);
         }
         if (tid == 0) {
             wsp<int>(P, P.L.active_slot)[n_act] = 0;
@@ -382,7 +406,6 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         }
         n_act += 1;
         n_ent += n_tok;
-        n_grp += ngs;
     } else {
         for (int t = tid; t < n_tok; t += nthr) ent_of[t * (K + 1) + K] = -1;
     }
@@ -457,6 +480,38 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
     if (smem > 200 * 1024) return NVMOE_ERR_UNSUPPORTED;
     cudaStream_t st = (cudaStream_t)stream;
     F.fp.spare_sm = 1;
+    // The mma.sync FFN copies the misses in itself, overlapped with the hit groups; the FP4
+    // tensor-core FFN runs after a separate gather kernel.
+    bool in_kernel_refill = false;
+    if (a->refill_banks && a->n_refill_banks > 0) {
+        if (!a->host_slot_of_id || !m.miss_ids || !m.miss_slots) return NVMOE_ERR_INVALID_ARG;
+        for (int b = 0; b < a->n_refill_banks; ++b) {
+            const nvmoe_refill_bank& B = a->refill_banks[b];
+            if (!B.dst || !B.src || B.row_bytes < 0) return NVMOE_ERR_INVALID_ARG;
+        }
+        if (!F.fp.use_fp4 && a->n_refill_banks <= kRefillMaxBanks) {
+            FfnRefill& R = F.fp.rf;
+            R.n_banks = a->n_refill_banks;
+            R.pbase[0] = 0;
+            for (int b = 0; b < R.n_banks; ++b) {
+                const nvmoe_refill_bank& B = a->refill_banks[b];
+                R.banks[b] = B;
+                const uint64_t bits = (uint64_t)B.row_bytes | (uint64_t)B.dst_slot_stride |
+                                      (uint64_t)B.src_slot_stride |
+                                      reinterpret_cast<uintptr_t>(B.dst) |
+                                      reinterpret_cast<uintptr_t>(B.src);
+                R.vec16[b] = (bits & 15) == 0;  // pieces start at multiples of 16 bytes
+                R.vec4[b] = (bits & 3) == 0;
+                R.pbase[b + 1] = R.pbase[b] + (int)((B.row_bytes + kRefillPiece - 1) / kRefillPiece);
+            }
+            R.counts = m.counts;
+            R.miss_ids = m.miss_ids;
+            R.miss_slots = m.miss_slots;
+            R.host_slot_of_id = a->host_slot_of_id;
+            R.n_gpu_slots = t.cache_size;
+            in_kernel_refill = true;
+        }
+    }
     if (smem > 48 * 1024)
         NVMOE_CUDA_TRY(cudaFuncSetAttribute(decode_front_kernel,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -464,7 +519,7 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
     const int threads = a->n_tok <= 8 ? 256 : kFrontThreads;
     cudaError_t e = launch_pdl(decode_front_kernel, dim3(1), dim3(threads), smem, st, true, F);
     if (e != cudaSuccess) return cuda_status("decode_front launch", e);
-    if (a->refill_banks && a->n_refill_banks > 0) {
+    if (a->refill_banks && a->n_refill_banks > 0 && !in_kernel_refill) {
         rc = nvmoe_refill_gather(a->refill_banks, a->n_refill_banks, &a->misses,
                                  a->host_slot_of_id, t.cache_size, stream);
         if (rc != NVMOE_OK) return rc;

@@ -22,6 +22,7 @@ enum {
     GD_TOK = 4,     // token of each entry (8)
     GD_RT = 12,     // (stage copies only) row tile of the work item
     GD_GID = 13,    // (stage copies only) group index
+    GD_MISS = 14,   // miss index + 1 when this FFN call refills the slot's expert, else 0
     GD_GGLOB = 16,  // unused (the FFN reads the slot's global scales from the pool when it
     GD_UGLOB = 17,  //   runs, after any refill of the slot; the grouping may run before it)
     GD_DGLOB = 18,
@@ -37,7 +38,7 @@ constexpr int kFp4MaxCtas = 160;
 
 struct WsLayout {
     size_t hdr, active_slot, tok_cnt, grp_desc, grp_done, ent_tok, ent_w, ent_of, x16, sg, h16,
-        ypart, bimg, ximg, xk, hk, h32, gcnt, phase, total;
+        ypart, bimg, ximg, xk, hk, h32, gcnt, phase, rdy, total;
     int a_max, n_ent_max, g_max;
     int jb, rb, ks_gu, ks_dn;  // FP4 path: 64-row j-blocks, 128-row H blocks, K stages (0: off)
 };
@@ -98,11 +99,29 @@ __host__ __device__ inline WsLayout ws_layout(int n_tok, int top_k, int H, int I
     o = align_up(o + 8 * (size_t)L.g_max, 256);
     L.phase = o;  // grid phase counters of the FP4 kernel (4 ints)
     o = align_up(o + 16, 256);
+    L.rdy = o;  // per miss refilled by the FFN: pieces copied
+    o = align_up(o + 4 * (size_t)L.a_max, 256);
     L.total = o;
     return L;
 }
 
 enum { HDR_N_ACTIVE = 0, HDR_N_ENT = 1, HDR_STATUS = 2, HDR_N_GROUPS = 3 };
+
+// Misses the FFN kernel copies in from the pinned host tier itself (decode layer step), so the
+// copies overlap the hit groups: rows of each bank of each miss in pieces of kRefillPiece bytes.
+constexpr int kRefillMaxBanks = 8;
+constexpr int kRefillPiece = 8192;
+struct FfnRefill {
+    nvmoe_refill_bank banks[kRefillMaxBanks];
+    int pbase[kRefillMaxBanks + 1];  // first piece of each bank within a miss; pbase[n] = per miss
+    unsigned char vec16[kRefillMaxBanks], vec4[kRefillMaxBanks];
+    int n_banks;                     // 0: no refill in this call
+    int32_t* counts;                 // miss list: [1] misses, [2] status
+    const int32_t* miss_ids;
+    const int32_t* miss_slots;
+    const int32_t* host_slot_of_id;
+    int32_t n_gpu_slots;
+};
 
 struct FfnParams {
     nvmoe_expert_pool pool;
@@ -127,6 +146,7 @@ struct FfnParams {
     int ypart_smem;        // 1: the down phase keeps y_part in shared memory
     int use_fp4;           // 1: the block-scaled FP4 tensor-core kernel runs this call (NVFP4)
     int spare_sm;          // 1: the FFN grid leaves one SM free (for the next layer's front)
+    FfnRefill rf;          // misses this call copies in (rf.n_banks = 0: none)
 };
 
 template <typename T>

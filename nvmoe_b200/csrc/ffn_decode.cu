@@ -60,6 +60,76 @@ __device__ __forceinline__ void report_timeout(const FfnParams& P) {
     if (P.status) atomicExch(P.status, NVMOE_ERR_TIMEOUT);
 }
 
+// ------------------------------------------------------------------ in-kernel refill
+// The misses of a decode layer step are copied from the pinned host tier by one warp of every
+// CTA while the other warps run the hit groups (the grouping orders missed groups last); each
+// piece ends with a release on the miss's counter, and a producer about to stage a missed
+// slot's rows acquires it first.  Generic-proxy stores read later by bulk copies (async proxy):
+// a proxy fence on both sides.
+__device__ __forceinline__ void proxy_fence_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void refill_pieces(const FfnParams& P, int lane) {
+    const FfnRefill& R = P.rf;
+    const int ppm = R.pbase[R.n_banks];
+    const int n_miss = __ldcg(R.counts + 1);
+    int* rdy = wsp<int>(P, P.L.rdy);
+    for (int p = blockIdx.x; p < n_miss * ppm; p += gridDim.x) {
+        const int m = p / ppm, q = p - m * ppm;
+        int b = 0;
+        while (b + 1 < R.n_banks && q >= R.pbase[b + 1]) ++b;
+        const nvmoe_refill_bank& B = R.banks[b];
+        const int gs = __ldcg(R.miss_slots + m);
+        const int id = __ldcg(R.miss_ids + m);
+        const int hs = id >= 0 ? __ldcg(R.host_slot_of_id + id) : -1;
+        if (hs < 0 || gs < 0 || gs >= R.n_gpu_slots) {
+            if (lane == 0) atomicExch(R.counts + 2, NVMOE_ERR_HOST_LOAD);
+        } else {
+            const int64_t beg = (int64_t)(q - R.pbase[b]) * kRefillPiece;
+            const int len = (int)min((int64_t)kRefillPiece, B.row_bytes - beg);
+            const char* src = static_cast<const char*>(B.src) + (int64_t)hs * B.src_slot_stride + beg;
+            char* dst = static_cast<char*>(B.dst) + (int64_t)gs * B.dst_slot_stride + beg;
+            if (R.vec16[b]) {  // all of a piece's loads in flight at once (PCIe latency)
+                const uint4* s16 = reinterpret_cast<const uint4*>(src);
+                uint4* d16 = reinterpret_cast<uint4*>(dst);
+                const int n16 = len >> 4;
+                uint4 v[kRefillPiece / 16 / 32];
+#pragma unroll
+                for (int i = 0; i < kRefillPiece / 16 / 32; ++i)
+                    if (lane + 32 * i < n16) v[i] = s16[lane + 32 * i];
+#pragma unroll
+                for (int i = 0; i < kRefillPiece / 16 / 32; ++i)
+                    if (lane + 32 * i < n16) d16[lane + 32 * i] = v[i];
+            } else if (R.vec4[b]) {  // e.g. the fp32 global-scale bank
+                for (int i = lane; i < (len >> 2); i += 32)
+                    reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
+            } else {
+                for (int i = lane; i < len; i += 32) dst[i] = src[i];
+            }
+        }
+        proxy_fence_global();
+        __threadfence();
+        __syncwarp();
+        if (lane == 0)  // also after a bad slot, so that no waiter runs into its limit
+            asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(rdy + m) : "memory");
+    }
+}
+// A producer's wait for missed slot mi to be complete (bounded).
+__device__ __forceinline__ bool refill_wait(const FfnParams& P, int mi) {
+    const int* c = wsp<int>(P, P.L.rdy) + mi;
+    const int ppm = P.rf.pbase[P.rf.n_banks];
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+        if (v >= ppm) {
+            proxy_fence_global();
+            return true;
+        }
+        if (i > 16) __nanosleep(i < 1024 ? 64 : 256);
+    }
+    return false;
+}
+
 // Copies `rows` rows of `row_bytes` from a bank (row stride `stride`) into contiguous smem.
 __device__ __forceinline__ void bulk_rows(uint8_t* dst, const uint8_t* src, int rows,
                                           int row_bytes, int64_t stride, uint64_t* bar) {
@@ -216,7 +286,8 @@ constexpr int kCW = kConsumerWarps;       // MMA warps
 constexpr int kProdGU = kCW;              // bulk-copy producer of the gate_up items
 constexpr int kEpiWarp = kCW + 1;         // gate/up cross-warp sum + SwiGLU + h store
 constexpr int kProdDN = kCW + 2;          // bulk-copy producer of the down slabs
-constexpr int kFusedThreads = (kCW + 3) * 32;
+constexpr int kRefillWarp = kCW + 3;      // copies this call's misses in from the host tier
+constexpr int kFusedThreads = (kCW + 4) * 32;
 
 // Persistent expert FFN, one CTA per SM.  CTA c runs
 //   gate_up items c, c + G, ... (item = token group x 16 rows of gate and of up, full K = H),
@@ -277,6 +348,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                               : smem + (size_t)(st - FL.nst_dn) * FL.stage_dn;
     };
 
+    if (warp == kRefillWarp) {
+        if (P.rf.n_banks > 0) refill_pieces(P, lane);
+        return;
+    }
+
     if (warp == kProdGU) {
         // the first batch of records is fetched together with the group count (speculative
         // group indices, clamped into the workspace)
@@ -308,6 +384,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                         uint8_t* stg = smem + (size_t)st * FL.stage_gu;
                         int* hdr = reinterpret_cast<int*>(stg);
                         copy_record(hdr, r);
+                        if (hdr[GD_MISS] > 0 && !refill_wait(P, hdr[GD_MISS] - 1)) {
+                            report_timeout(P);
+                            ok = false;
+                        }
                         hdr[GD_RT] = item % tiles_i;
                         hdr[GD_GID] = item / tiles_i;
                         const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
@@ -381,6 +461,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                             uint8_t* stg = dn_stage(st);
                             int* hdr = reinterpret_cast<int*>(stg);
                             copy_record(hdr, r);
+                            if (hdr[GD_MISS] > 0 && !refill_wait(P, hdr[GD_MISS] - 1)) {
+                                report_timeout(P);
+                                ok = false;
+                            }
+                        }
+                        if (ok) {
+                            uint8_t* stg = dn_stage(st);
+                            int* hdr = reinterpret_cast<int*>(stg);
                             hdr[GD_GID] = base + i;
                             const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
                             const int slot = hdr[GD_SLOT];
