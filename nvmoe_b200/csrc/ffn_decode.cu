@@ -430,65 +430,65 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     }
 
     if (warp == kProdDN) {
-        // down slabs: for each of this CTA's row tiles, every group's 16 rows; stages past the
-        // dedicated region wait until the gate_up ring has drained
-        int4 rec[kDescInts / 4];
-        load_record(P, min(lane, P.L.g_max - 1), rec);
+        // down slabs: for each of this CTA's row tiles, every group's 16 rows.  The lanes stage
+        // a batch of consecutive ring uses at once, one group each (a batch never holds a stage
+        // twice): the dedicated stages while gate_up runs, then, once the gate_up ring has
+        // drained, batches of up to the whole ring.
         const int n_groups = __ldcg(hdr_g + HDR_N_GROUPS);
         bool ok = true, drained = false;
-        int j = 0;
+        int j0 = 0;
         for (int rt = G - 1 - (int)blockIdx.x; rt < n_dn && ok; rt += G) {
-            for (int base = 0; base < n_groups && ok; base += 32) {
-                if ((base != 0 || j != 0) && base + lane < n_groups) load_record(P, base + lane, rec);
-                const int n_here = min(32, n_groups - base);
-                for (int i = 0; i < n_here; ++i, ++j) {
-                    int4 r[kDescInts / 4];
-                    shfl_record(r, rec, i);
-                    if (lane == 0) {
-                        const int st = j % NDT;
-                        if (st >= FL.nst_dn && !drained) {
-                            if (!mbar_wait_bounded(gu_drained, 0)) {
-                                report_timeout(P);
-                                ok = false;
-                            }
-                            drained = true;
-                        }
-                        if (ok && !mbar_wait_bounded(&dn_empty[st], ((j / NDT) & 1) ^ 1)) {
+            for (int base = 0; base < n_groups && ok;) {
+                int4 r[kDescInts / 4];
+                if (base + lane < n_groups) load_record(P, base + lane, r);
+                int cap = min(32, NDT);
+                if (!drained) {
+                    const int s0 = j0 % NDT;
+                    cap = s0 < FL.nst_dn ? min(cap, FL.nst_dn - s0) : 0;
+                    if (cap == 0) {
+                        if (lane == 0 && !mbar_wait_bounded(gu_drained, 0)) {
                             report_timeout(P);
                             ok = false;
                         }
-                        if (ok) {
-                            uint8_t* stg = dn_stage(st);
-                            int* hdr = reinterpret_cast<int*>(stg);
-                            copy_record(hdr, r);
-                            if (hdr[GD_MISS] > 0 && !refill_wait(P, hdr[GD_MISS] - 1)) {
-                                report_timeout(P);
-                                ok = false;
-                            }
-                        }
-                        if (ok) {
-                            uint8_t* stg = dn_stage(st);
-                            int* hdr = reinterpret_cast<int*>(stg);
-                            hdr[GD_GID] = base + i;
-                            const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
-                            const int slot = hdr[GD_SLOT];
-                            const int64_t r0 = (int64_t)rt * 16;
-                            mbar_arrive_expect_tx(&dn_full[st], (uint32_t)(16 * (cbd + sbd)));
-                            bulk_rows(stg + kStageHdr,
-                                      (const uint8_t*)pool.down.data +
-                                          slot * pool.down.slot_stride + r0 * pool.down.row_stride,
-                                      16, cbd, pool.down.row_stride, &dn_full[st]);
-                            if (sbd > 0)
-                                bulk_rows(stg + od_sc,
-                                          (const uint8_t*)pool.down.scale +
-                                              slot * pool.down.scale_slot_stride +
-                                              r0 * pool.down.scale_row_stride,
-                                          16, sbd, pool.down.scale_row_stride, &dn_full[st]);
-                        }
+                        ok = __shfl_sync(0xffffffffu, ok, 0);
+                        drained = true;
+                        cap = min(32, NDT);
                     }
-                    ok = __shfl_sync(0xffffffffu, ok, 0);
-                    if (!ok) break;
                 }
+                const int nb = min(cap, n_groups - base);
+                if (ok && lane < nb) {
+                    const int j = j0 + lane, st = j % NDT;
+                    uint8_t* stg = dn_stage(st);
+                    int* hdr = reinterpret_cast<int*>(stg);
+                    bool good = mbar_wait_bounded(&dn_empty[st], ((j / NDT) & 1) ^ 1);
+                    if (good) {
+                        copy_record(hdr, r);
+                        if (hdr[GD_MISS] > 0) good = refill_wait(P, hdr[GD_MISS] - 1);
+                    }
+                    if (good) {
+                        hdr[GD_GID] = base + lane;
+                        const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
+                        const int slot = hdr[GD_SLOT];
+                        const int64_t r0 = (int64_t)rt * 16;
+                        mbar_arrive_expect_tx(&dn_full[st], (uint32_t)(16 * (cbd + sbd)));
+                        bulk_rows(stg + kStageHdr,
+                                  (const uint8_t*)pool.down.data + slot * pool.down.slot_stride +
+                                      r0 * pool.down.row_stride,
+                                  16, cbd, pool.down.row_stride, &dn_full[st]);
+                        if (sbd > 0)
+                            bulk_rows(stg + od_sc,
+                                      (const uint8_t*)pool.down.scale +
+                                          slot * pool.down.scale_slot_stride +
+                                          r0 * pool.down.scale_row_stride,
+                                      16, sbd, pool.down.scale_row_stride, &dn_full[st]);
+                    } else {
+                        report_timeout(P);
+                        ok = false;
+                    }
+                }
+                ok = __all_sync(0xffffffffu, ok);
+                base += nb;
+                j0 += nb;
             }
         }
         return;
