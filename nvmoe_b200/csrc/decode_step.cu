@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
             if (P.rf.n_banks > 0) d[GD_MISS] = missof[s] + 1;
         }
     }
-    for (int j = tid; j < nmiss; j += nthr) wsp<int>(P, P.L.rdy)[j] = 0;
+    for (int j = tid; j < 2 * nmiss; j += nthr) wsp<int>(P, P.L.rdy)[j] = 0;
     for (int p = tid; p < n; p += nthr) {
         const int t = p / K, j = p - t * K;
         ent_of[t * (K + 1) + j] = pe[p];
@@ -493,16 +493,30 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
             FfnRefill& R = F.fp.rf;
             R.n_banks = a->n_refill_banks;
             R.pbase[0] = 0;
+            // the gate/up banks first: a missed group's gate_up starts once they are in
+            const nvmoe_matrix_bank& dn = F.fp.pool.down;
+            auto is_down = [&](const nvmoe_refill_bank& B) {
+                return B.dst == dn.data || (dn.scale && B.dst == dn.scale) ||
+                       (dn.global_scale && B.dst == (const void*)dn.global_scale);
+            };
+            int order[kRefillMaxBanks], no = 0;
+            for (int ph = 0; ph < 2; ++ph)
+                for (int b = 0; b < R.n_banks; ++b)
+                    if ((int)is_down(a->refill_banks[b]) == ph) order[no++] = b;
+            R.pieces_gu = R.pieces_dn = 0;
             for (int b = 0; b < R.n_banks; ++b) {
-                const nvmoe_refill_bank& B = a->refill_banks[b];
+                const nvmoe_refill_bank& B = a->refill_banks[order[b]];
                 R.banks[b] = B;
+                R.down[b] = is_down(B) ? 1 : 0;
                 const uint64_t bits = (uint64_t)B.row_bytes | (uint64_t)B.dst_slot_stride |
                                       (uint64_t)B.src_slot_stride |
                                       reinterpret_cast<uintptr_t>(B.dst) |
                                       reinterpret_cast<uintptr_t>(B.src);
                 R.vec16[b] = (bits & 15) == 0;  // pieces start at multiples of 16 bytes
                 R.vec4[b] = (bits & 3) == 0;
-                R.pbase[b + 1] = R.pbase[b] + (int)((B.row_bytes + kRefillPiece - 1) / kRefillPiece);
+                const int pcs = (int)((B.row_bytes + kRefillPiece - 1) / kRefillPiece);
+                R.pbase[b + 1] = R.pbase[b] + pcs;
+                (R.down[b] ? R.pieces_dn : R.pieces_gu) += pcs;
             }
             R.counts = m.counts;
             R.miss_ids = m.miss_ids;

@@ -99,8 +99,8 @@ __host__ __device__ inline WsLayout ws_layout(int n_tok, int top_k, int H, int I
     o = align_up(o + 8 * (size_t)L.g_max, 256);
     L.phase = o;  // grid phase counters of the FP4 kernel (4 ints)
     o = align_up(o + 16, 256);
-    L.rdy = o;  // per miss refilled by the FFN: pieces copied
-    o = align_up(o + 4 * (size_t)L.a_max, 256);
+    L.rdy = o;  // per miss refilled by the FFN: pieces copied of its gate/up and down banks
+    o = align_up(o + 8 * (size_t)L.a_max, 256);
     L.total = o;
     return L;
 }
@@ -115,6 +115,8 @@ struct FfnRefill {
     nvmoe_refill_bank banks[kRefillMaxBanks];
     int pbase[kRefillMaxBanks + 1];  // first piece of each bank within a miss; pbase[n] = per miss
     unsigned char vec16[kRefillMaxBanks], vec4[kRefillMaxBanks];
+    unsigned char down[kRefillMaxBanks];  // 1: a bank of the down matrix (gate/up banks first)
+    int pieces_gu, pieces_dn;             // pieces per miss of the gate/up and of the down banks
     int n_banks;                     // 0: no refill in this call
     int32_t* counts;                 // miss list: [1] misses, [2] status
     const int32_t* miss_ids;

@@ -111,17 +111,19 @@ __device__ __forceinline__ void refill_pieces(const FfnParams& P, int lane) {
         __threadfence();
         __syncwarp();
         if (lane == 0)  // also after a bad slot, so that no waiter runs into its limit
-            asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(rdy + m) : "memory");
+            asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(rdy + 2 * m + R.down[b])
+                         : "memory");
     }
 }
-// A producer's wait for missed slot mi to be complete (bounded).
-__device__ __forceinline__ bool refill_wait(const FfnParams& P, int mi) {
-    const int* c = wsp<int>(P, P.L.rdy) + mi;
-    const int ppm = P.rf.pbase[P.rf.n_banks];
+// A producer's wait for missed slot mi (bounded): the gate/up banks (down = 0), or every bank
+// (down = 1; a bank the host did not recognise as a down bank counts with the gate/up ones).
+__device__ __forceinline__ bool refill_wait(const FfnParams& P, int mi, int down) {
+    const int* c = wsp<int>(P, P.L.rdy) + 2 * mi;
     for (uint32_t i = 0; i < (1u << 24); ++i) {
-        int v;
-        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
-        if (v >= ppm) {
+        int v0, v1 = 0;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v0) : "l"(c) : "memory");
+        if (down) asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v1) : "l"(c + 1) : "memory");
+        if (v0 >= P.rf.pieces_gu && (!down || v1 >= P.rf.pieces_dn)) {
             proxy_fence_global();
             return true;
         }
@@ -384,7 +386,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                         uint8_t* stg = smem + (size_t)st * FL.stage_gu;
                         int* hdr = reinterpret_cast<int*>(stg);
                         copy_record(hdr, r);
-                        if (hdr[GD_MISS] > 0 && !refill_wait(P, hdr[GD_MISS] - 1)) {
+                        if (hdr[GD_MISS] > 0 && !refill_wait(P, hdr[GD_MISS] - 1, 0)) {
                             report_timeout(P);
                             ok = false;
                         }
@@ -463,7 +465,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                     bool good = mbar_wait_bounded(&dn_empty[st], ((j / NDT) & 1) ^ 1);
                     if (good) {
                         copy_record(hdr, r);
-                        if (hdr[GD_MISS] > 0) good = refill_wait(P, hdr[GD_MISS] - 1);
+                        if (hdr[GD_MISS] > 0) good = refill_wait(P, hdr[GD_MISS] - 1, 1);
                     }
                     if (good) {
                         hdr[GD_GID] = base + lane;
