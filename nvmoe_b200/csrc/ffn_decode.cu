@@ -115,6 +115,19 @@ __device__ __forceinline__ void refill_pieces(const FfnParams& P, int lane) {
                          : "memory");
     }
 }
+// Whether missed slot mi's gate/up banks (down = 0) or all its banks (down = 1) are in; after a
+// true result the caller's bulk copies see them.
+__device__ __forceinline__ bool refill_ready(const FfnParams& P, int mi, int down) {
+    const int* c = wsp<int>(P, P.L.rdy) + 2 * mi;
+    int v0, v1 = 0;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v0) : "l"(c) : "memory");
+    if (down) asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v1) : "l"(c + 1) : "memory");
+    if (v0 >= P.rf.pieces_gu && (!down || v1 >= P.rf.pieces_dn)) {
+        proxy_fence_global();
+        return true;
+    }
+    return false;
+}
 // A producer's wait for missed slot mi (bounded): the gate/up banks (down = 0), or every bank
 // (down = 1; a bank the host did not recognise as a down bank counts with the gate/up ones).
 __device__ __forceinline__ bool refill_wait(const FfnParams& P, int mi, int down) {
@@ -458,17 +471,28 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                     }
                 }
                 const int nb = min(cap, n_groups - base);
-                if (ok && lane < nb) {
-                    const int j = j0 + lane, st = j % NDT;
-                    uint8_t* stg = dn_stage(st);
-                    int* hdr = reinterpret_cast<int*>(stg);
-                    bool good = mbar_wait_bounded(&dn_empty[st], ((j / NDT) & 1) ^ 1);
-                    if (good) {
-                        copy_record(hdr, r);
-                        if (hdr[GD_MISS] > 0) good = refill_wait(P, hdr[GD_MISS] - 1, 1);
+                // every lane polls its own stage (and, for a missed slot, its refill) without
+                // blocking: a lane that waited in a loop of its own would hold back the lanes
+                // whose stages are free at the loop's reconvergence point
+                const int j = j0 + lane, st = j % NDT;
+                uint8_t* stg = dn_stage(st);
+                int* hdr = reinterpret_cast<int*>(stg);
+                int state = (ok && lane < nb) ? 0 : 2;  // 0: stage busy, 1: refill pending, 2: done
+                for (uint32_t w = 0; __any_sync(0xffffffffu, state != 2); ++w) {
+                    if (w == (1u << 22)) {  // seconds: give up
+                        if (state != 2) {
+                            report_timeout(P);
+                            ok = false;
+                        }
+                        break;
                     }
-                    if (good) {
+                    if (state == 0 && mbar_test_wait(&dn_empty[st], ((j / NDT) & 1) ^ 1)) {
+                        copy_record(hdr, r);
                         hdr[GD_GID] = base + lane;
+                        state = hdr[GD_MISS] > 0 ? 1 : 3;
+                    }
+                    if (state == 1 && refill_ready(P, hdr[GD_MISS] - 1, 1)) state = 3;
+                    if (state == 3) {
                         const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
                         const int slot = hdr[GD_SLOT];
                         const int64_t r0 = (int64_t)rt * 16;
@@ -483,10 +507,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                                           slot * pool.down.scale_slot_stride +
                                           r0 * pool.down.scale_row_stride,
                                       16, sbd, pool.down.scale_row_stride, &dn_full[st]);
-                    } else {
-                        report_timeout(P);
-                        ok = false;
+                        state = 2;
                     }
+                    if (w > 8) __nanosleep(w < 1024 ? 32 : 256);
                 }
                 ok = __all_sync(0xffffffffu, ok);
                 base += nb;
