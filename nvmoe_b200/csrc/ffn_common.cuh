@@ -160,6 +160,16 @@ __device__ __forceinline__ T* wsp(const FfnParams& P, size_t off) {
 __device__ __forceinline__ float global_of(const nvmoe_matrix_bank& b, int slot) {
     return b.global_scale ? __ldcg(b.global_scale + (int64_t)slot * b.global_stride) : 1.0f;
 }
+// The same load issued where it stands (not sunk to its first use), for a value needed only at
+// the end of a long stretch of work.
+__device__ __forceinline__ float global_of_early(const nvmoe_matrix_bank& b, int slot) {
+    if (!b.global_scale) return 1.0f;
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];"
+                 : "=f"(v)
+                 : "l"(b.global_scale + (int64_t)slot * b.global_stride));
+    return v;
+}
 
 // Completes group record d (slot, pool, e0, nt already set): token of each entry, router weight
 // of each entry (w_of_entry: the group's entries' weights, or null for the shared expert, whose

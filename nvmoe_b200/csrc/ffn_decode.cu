@@ -268,13 +268,6 @@ __device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
 }
 
 // Bounded wait until the group's h rows are complete (all I/16 gate/up row tiles stored).
-__device__ __forceinline__ bool wait_group_h(const int* done, int target) {
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
-        if (ld_acquire_gpu(done) >= target) return true;
-        if (i > 64) __nanosleep(64);
-    }
-    return false;
-}
 
 __device__ __forceinline__ void copy_record(int* dst, const int4 (&r)[kDescInts / 4]) {
 #pragma unroll
@@ -450,6 +443,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
         // twice): the dedicated stages while gate_up runs, then, once the gate_up ring has
         // drained, batches of up to the whole ring.
         const int n_groups = __ldcg(hdr_g + HDR_N_GROUPS);
+        const float* sgate = (P.has_shared && P.shared_gate) ? wsp<float>(P, P.L.sg) : nullptr;
         bool ok = true, drained = false;
         int j0 = 0;
         for (int rt = G - 1 - (int)blockIdx.x; rt < n_dn && ok; rt += G) {
@@ -477,7 +471,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 const int j = j0 + lane, st = j % NDT;
                 uint8_t* stg = dn_stage(st);
                 int* hdr = reinterpret_cast<int*>(stg);
-                int state = (ok && lane < nb) ? 0 : 2;  // 0: stage busy, 1: refill pending, 2: done
+                // 0: stage busy, 1: refill pending, 3: to stage, 4: h pending, 2: done
+                int state = (ok && lane < nb) ? 0 : 2;
+                float dgl = 1.f;
                 for (uint32_t w = 0; __any_sync(0xffffffffu, state != 2); ++w) {
                     if (w == (1u << 22)) {  // seconds: give up
                         if (state != 2) {
@@ -496,7 +492,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                         const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
                         const int slot = hdr[GD_SLOT];
                         const int64_t r0 = (int64_t)rt * 16;
-                        mbar_arrive_expect_tx(&dn_full[st], (uint32_t)(16 * (cbd + sbd)));
+                        dgl = global_of_early(pool.down, slot);
+                        mbar_expect_tx(&dn_full[st], (uint32_t)(16 * (cbd + sbd)));
                         bulk_rows(stg + kStageHdr,
                                   (const uint8_t*)pool.down.data + slot * pool.down.slot_stride +
                                       r0 * pool.down.row_stride,
@@ -507,6 +504,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                                           slot * pool.down.scale_slot_stride +
                                           r0 * pool.down.scale_row_stride,
                                       16, sbd, pool.down.scale_row_stride, &dn_full[st]);
+                        state = 4;
+                    }
+                    // the stage is released to its MMA warp once the group's h is complete: the
+                    // warp then reads h without an acquire of its own (release -> acquire here,
+                    // then the stage barrier)
+                    if (state == 4 && ld_acquire_gpu(done + base + lane) >= tiles_i) {
+                        hdr[GD_DGLOB] = __float_as_int(dgl);
+                        if (hdr[GD_POOL] && sgate) {
+                            const int nt = hdr[GD_NT];
+                            for (int k = 0; k < nt; ++k)
+                                hdr[GD_W + k] = __float_as_int(__ldcg(sgate + hdr[GD_TOK + k]));
+                        }
+                        mbar_arrive(&dn_full[st]);
                         state = 2;
                     }
                     if (w > 8) __nanosleep(w < 1024 ? 32 : 256);
@@ -583,8 +593,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 {  // the slot's global scales from the pool itself: a refill between the
                    // grouping and this kernel may have replaced the slot's expert
                     const nvmoe_expert_pool& pl = hdr[GD_POOL] ? P.shared : P.pool;
-                    mv[4] = __float_as_int(global_of(pl.gate, hdr[GD_SLOT]));
-                    mv[5] = __float_as_int(global_of(pl.up, hdr[GD_SLOT]));
+                    mv[4] = __float_as_int(global_of_early(pl.gate, hdr[GD_SLOT]));
+                    mv[5] = __float_as_int(global_of_early(pl.up, hdr[GD_SLOT]));
                 }
                 const bool has_tok = g < mv[1];
                 // B rows: the resident row of the lane's token, or the staged row g
@@ -638,7 +648,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     float* ypart = P.ypart_smem ? reinterpret_cast<float*>(smem + FL.off_yp)
                                 : wsp<float>(P, P.L.ypart);
     const int ypstride = P.ypart_smem ? 16 : H;  // floats between entries
-    const float* sgate = (P.has_shared && P.shared_gate) ? wsp<float>(P, P.L.sg) : nullptr;
     const int* ent_of = wsp<int>(P, P.L.ent_of);
     const int K1 = P.top_k + 1;
     int j = 0;
@@ -654,25 +663,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 report_timeout(P);
                 ok = false;
             }
-            if (ok && !wait_group_h(done + grp, tiles_i)) {
-                report_timeout(P);
-                ok = false;
-            }
             __syncwarp();
             float acc[kAcc][4] = {};
             int e0 = 0, nt = 0;
-            float dglob = 0.f, w_lo = 0.f, w_hi = 0.f, s_lo = 1.f, s_hi = 1.f;
-            if (ok) {
+            float dglob = 0.f, w_lo = 0.f, w_hi = 0.f;
+            if (ok) {  // (the producer released the stage after the group's h was complete and
+                       // put the down global scale and, for the shared expert, the gates into it)
                 const uint8_t* stg = dn_stage(st);
                 const int* hdr = reinterpret_cast<const int*>(stg);
                 e0 = hdr[GD_E0], nt = hdr[GD_NT];
-                dglob = global_of((hdr[GD_POOL] ? P.shared : P.pool).down, hdr[GD_SLOT]);
+                dglob = __int_as_float(hdr[GD_DGLOB]);
                 w_lo = __int_as_float(hdr[GD_W + 2 * q]);
                 w_hi = __int_as_float(hdr[GD_W + 2 * q + 1]);
-                if (hdr[GD_POOL] && sgate) {
-                    s_lo = 2 * q < nt ? __ldcg(sgate + hdr[GD_TOK + 2 * q]) : 0.f;
-                    s_hi = 2 * q + 1 < nt ? __ldcg(sgate + hdr[GD_TOK + 2 * q + 1]) : 0.f;
-                }
                 const __half* hrow = g < nt ? h16 + (int64_t)(e0 + g) * I : nullptr;
                 if constexpr (TD > 0) {
                     uint4 hb[TD][Fmt::kSteps / 2];
@@ -702,7 +704,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 const int n = 2 * q + (v & 1);
                 if (n < nt)
                     ypart[(int64_t)(e0 + n) * ypstride + ypcol + row] =
-                        acc[0][v] * dglob * ((v & 1) ? w_hi * s_hi : w_lo * s_lo);
+                        acc[0][v] * dglob * ((v & 1) ? w_hi : w_lo);
             }
         }
         named_bar_sync(1, kConsumers);
