@@ -303,6 +303,11 @@ typedef struct nvmoe_decode_args {
     int32_t n_refill_banks;
     const int32_t* host_slot_of_id;
     nvmoe_ffn_args ffn;
+    /* 1: the workspace (ffn.workspace) and the miss list of this call are not the ones of the
+     * decode step just before it on the stream (a caller running layer after layer alternates
+     * two sets), so the step's front kernel writes them while that step's FFN still runs.
+     * 0: they are written after it (always correct). */
+    int32_t early_outputs;
 } nvmoe_decode_args;
 
 int nvmoe_decode_layer(const nvmoe_decode_args* args, nvmoe_stream_t stream);

@@ -155,6 +155,7 @@ class DecodeArgs(C.Structure):
         ("n_refill_banks", C.c_int32),
         ("host_slot_of_id", C.c_void_p),
         ("ffn", FfnArgs),
+        ("early_outputs", C.c_int32),
     ]
 
 

@@ -34,6 +34,7 @@ struct FrontParams {
     RemapParams rp;  // rp.out: slot ids [n_tok, k] (global), rp.ids unused
     float* weights;
     FfnParams fp;
+    int early;  // the workspace and miss list are not the previous step's: written before the wait
 };
 
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
@@ -160,9 +161,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     // dependency wait, while that kernel (normally the previous layer's FFN, which leaves an SM
     // free for this CTA) is still running: routing, the remap with this layer's table, slot-id
     // and weight writes, and the grouping in shared memory.  The router logits must be complete
-    // when the previous kernel triggers its dependents.  After the wait: the miss list (shared
-    // by the layers; the FFN before this kernel reads it while copying its own misses in), the
-    // token rows (read only now) and the FFN workspace.
+    // when the previous kernel triggers its dependents.  After the wait: the miss list (the FFN
+    // before this kernel may read the same one while copying its own misses in), the token rows
+    // and the FFN workspace; with early outputs (the caller alternates two sets of these
+    // buffers) those too come before the wait, and the token rows must then also be complete
+    // when the previous kernel triggers.
     grid_dep_launch();
     // ---- A. one round trip: table prefetch (async) while the warps route their tokens
     for (int e = tid; e < E; e += nthr) cp_async4(sor + e, F.rp.t.slot_of_real + id_base + e);
@@ -276,7 +279,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     };
     int* hdr = wsp<int>(P, P.L.hdr);
     if (status != NVMOE_OK) {  // the FFN gets nothing to do (y = 0) and the status
-        grid_dep_wait();
+        grid_dep_wait();  // (the error path waits in either mode)
         write_counts();
         if (tid == 0) {
             hdr[HDR_N_GROUPS] = 0;
@@ -334,8 +337,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     }
     __syncthreads();
 
-    // ---- D. after the previous kernel: the miss list, token rows and the FFN workspace
-    grid_dep_wait();
+    // ---- D. the miss list, token rows and the FFN workspace: after the previous kernel, or
+    // (early outputs: a set of buffers the kernel in flight does not use) right away, with the
+    // wait at the end, so that this kernel still completes only after the one before it
+    if (!F.early) grid_dep_wait();
     {
         const nvmoe_miss_list& M = F.rp.m;
         for (int r = tid; r < nuniq; r += nthr) {
@@ -416,6 +421,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         hdr[HDR_STATUS] = NVMOE_OK;
         if (P.status) *P.status = NVMOE_OK;
     }
+    if (F.early) grid_dep_wait();
 }
 
 }  // namespace
@@ -473,6 +479,7 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
     F.rp.n_tok = a->n_tok;
     F.rp.is_decode = a->is_decode;
     F.rp.m = m;
+    F.early = a->early_outputs ? 1 : 0;
 
     if (n > kFrontMaxIds || t.cache_size > kFrontMaxSlots) return NVMOE_ERR_UNSUPPORTED;
     if (F.fp.pool.n_slots < t.cache_size) return NVMOE_ERR_INVALID_ARG;

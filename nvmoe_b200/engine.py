@@ -73,10 +73,13 @@ class MoEStack:
                        if c.shared_expert else [None] * c.n_layers)
         self.tables = [ops.SlotTableGPU(c.n_experts, c.cache_size, d, pinned_k=c.pinned_k)
                        for _ in range(c.n_layers)]
-        self.misses = ops.MissListGPU(c.n_experts, d)
+        # two miss lists and FFN workspaces, alternated layer by layer, so that a layer's front
+        # kernel can fill its set while the previous layer's FFN still reads the other one
+        self.misses_sets = [ops.MissListGPU(c.n_experts, d) for _ in range(2)]
+        self.misses = self.misses_sets[(c.n_layers - 1) % 2]  # the last layer's (its misses)
         self.host_slot_of_id = torch.arange(c.n_experts, dtype=torch.int32, device=d)
         self.banks = [ops.refill_banks(p, self.host) for p in self.pools]
-        self.ws = ops.FfnWorkspace(d)
+        self.ws_sets = [ops.FfnWorkspace(d) for _ in range(2)]
         self._plans: dict[int, list] = {}
 
     @property
@@ -109,11 +112,15 @@ class MoEStack:
         """Per-layer nvmoe_decode_layer argument plans for batches of n_tok tokens."""
         c = self.cfg
         if n_tok not in self._plans:
+            # layer l uses set l % 2; with an odd layer count, layer 0 follows the last layer
+            # on the same set, so its front writes after its wait
             self._plans[n_tok] = [
-                ops.DecodeLayerPlan(self.pools[l], self.tables[l], self.misses, n_tok, c.top_k,
-                                    shared=self.shared[l], refill=self.banks[l],
-                                    host_slot_of_id=self.host_slot_of_id, workspace=self.ws,
-                                    router=c.router, device=self.device)
+                ops.DecodeLayerPlan(self.pools[l], self.tables[l], self.misses_sets[l % 2], n_tok,
+                                    c.top_k, shared=self.shared[l], refill=self.banks[l],
+                                    host_slot_of_id=self.host_slot_of_id,
+                                    workspace=self.ws_sets[l % 2], router=c.router,
+                                    device=self.device,
+                                    early_outputs=not (l == 0 and c.n_layers % 2 == 1))
                 for l in range(c.n_layers)]
         return self._plans[n_tok]
 

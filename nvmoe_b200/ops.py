@@ -362,7 +362,8 @@ class DecodeLayerPlan:
                  shared_gate: torch.Tensor | None = None, refill: list | None = None,
                  host_slot_of_id: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,
                  router: str = "softmax", router_bias: torch.Tensor | None = None,
-                 norm_topk: bool = True, routed_scaling: float = 1.0, device="cuda"):
+                 norm_topk: bool = True, routed_scaling: float = 1.0, device="cuda",
+                 early_outputs: bool = False):
         self.n_tok, self.top_k = n_tok, top_k
         self.pool_s = expert_pool_struct(pool)
         self.shared_s = expert_pool_struct(shared) if shared is not None else None
@@ -396,6 +397,8 @@ class DecodeLayerPlan:
         a.ffn.workspace = self.ws.data_ptr()
         a.ffn.workspace_bytes = self.ws.numel()
         a.ffn.status = self.status.data_ptr()
+        # the caller alternates workspace / miss-list sets between consecutive steps
+        a.early_outputs = int(bool(early_outputs))
         self.args = a
 
     def __call__(self, x: torch.Tensor, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
