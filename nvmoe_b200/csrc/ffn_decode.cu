@@ -312,7 +312,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int H = P.pool.hidden, I = P.pool.inter;
     const int G = gridDim.x;
-    const int NGU = FL.nst_gu, NDT = FL.nst_dn + FL.nst_dn_ext;
+    // (the down producer gives each ring stage to one lane: at most 32 stages are used)
+    const int NGU = FL.nst_gu, NDT = min(FL.nst_dn + FL.nst_dn_ext, 32);
     uint64_t* gu_full = reinterpret_cast<uint64_t*>(smem + FL.off_bar);
     uint64_t* gu_empty = gu_full + NGU;
     uint64_t* dn_full = gu_empty + NGU;
@@ -438,94 +439,78 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     }
 
     if (warp == kProdDN) {
-        // down slabs: for each of this CTA's row tiles, every group's 16 rows.  The lanes stage
-        // a batch of consecutive ring uses at once, one group each (a batch never holds a stage
-        // twice): the dedicated stages while gate_up runs, then, once the gate_up ring has
-        // drained, batches of up to the whole ring.
+        // down slabs: for each of this CTA's row tiles, every group's 16 rows; use j of the ring
+        // is (row tile j / n_groups, group j % n_groups) in stage j % NDT.  Lane i owns stage i
+        // and runs its uses i, i + NDT, ... as a state machine of its own, polled without
+        // blocking (a lane that waited in a loop of its own would hold the others back):
+        //   the gate_up ring drained (stages in its bytes) -> stage free -> missed slot's banks
+        //   in -> rows requested (expect_tx, bulk copies) -> the group's h complete: down global
+        //   scale and shared-expert gates into the stage's record copy, arrive (the MMA warp
+        //   reads h without an acquire of its own: release -> acquire here, then the barrier)
+        enum { S_DRAIN, S_FREE, S_REFILL, S_ISSUE, S_H, S_DONE };
         const int n_groups = __ldcg(hdr_g + HDR_N_GROUPS);
         const float* sgate = (P.has_shared && P.shared_gate) ? wsp<float>(P, P.L.sg) : nullptr;
-        bool ok = true, drained = false;
-        int j0 = 0;
-        for (int rt = G - 1 - (int)blockIdx.x; rt < n_dn && ok; rt += G) {
-            for (int base = 0; base < n_groups && ok;) {
-                int4 r[kDescInts / 4];
-                if (base + lane < n_groups) load_record(P, base + lane, r);
-                int cap = min(32, NDT);
-                if (!drained) {
-                    const int s0 = j0 % NDT;
-                    cap = s0 < FL.nst_dn ? min(cap, FL.nst_dn - s0) : 0;
-                    if (cap == 0) {
-                        if (lane == 0 && !mbar_wait_bounded(gu_drained, 0)) {
-                            report_timeout(P);
-                            ok = false;
-                        }
-                        ok = __shfl_sync(0xffffffffu, ok, 0);
-                        drained = true;
-                        cap = min(32, NDT);
-                    }
+        const int rt0 = G - 1 - (int)blockIdx.x;
+        const int n_rt = rt0 < n_dn ? (n_dn - 1 - rt0) / G + 1 : 0;
+        const int total = n_rt * n_groups;
+        int j = lane;
+        int state = (lane >= NDT || j >= total) ? S_DONE : (lane >= FL.nst_dn ? S_DRAIN : S_FREE);
+        uint8_t* stg = dn_stage(lane < NDT ? lane : 0);
+        int* hdr = reinterpret_cast<int*>(stg);
+        int4 r[kDescInts / 4];
+        if (state != S_DONE) load_record(P, j % n_groups, r);
+        float dgl = 1.f;
+        bool ok = true;
+        for (uint32_t w = 0; __any_sync(0xffffffffu, state != S_DONE); ++w) {
+            if (w == (1u << 24)) {  // about a second: give up
+                if (state != S_DONE) {
+                    report_timeout(P);
+                    ok = false;
                 }
-                const int nb = min(cap, n_groups - base);
-                // every lane polls its own stage (and, for a missed slot, its refill) without
-                // blocking: a lane that waited in a loop of its own would hold back the lanes
-                // whose stages are free at the loop's reconvergence point
-                const int j = j0 + lane, st = j % NDT;
-                uint8_t* stg = dn_stage(st);
-                int* hdr = reinterpret_cast<int*>(stg);
-                // 0: stage busy, 1: refill pending, 3: to stage, 4: h pending, 2: done
-                int state = (ok && lane < nb) ? 0 : 2;
-                float dgl = 1.f;
-                for (uint32_t w = 0; __any_sync(0xffffffffu, state != 2); ++w) {
-                    if (w == (1u << 22)) {  // seconds: give up
-                        if (state != 2) {
-                            report_timeout(P);
-                            ok = false;
-                        }
-                        break;
-                    }
-                    if (state == 0 && mbar_test_wait(&dn_empty[st], ((j / NDT) & 1) ^ 1)) {
-                        copy_record(hdr, r);
-                        hdr[GD_GID] = base + lane;
-                        state = hdr[GD_MISS] > 0 ? 1 : 3;
-                    }
-                    if (state == 1 && refill_ready(P, hdr[GD_MISS] - 1, 1)) state = 3;
-                    if (state == 3) {
-                        const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
-                        const int slot = hdr[GD_SLOT];
-                        const int64_t r0 = (int64_t)rt * 16;
-                        dgl = global_of_early(pool.down, slot);
-                        mbar_expect_tx(&dn_full[st], (uint32_t)(16 * (cbd + sbd)));
-                        bulk_rows(stg + kStageHdr,
-                                  (const uint8_t*)pool.down.data + slot * pool.down.slot_stride +
-                                      r0 * pool.down.row_stride,
-                                  16, cbd, pool.down.row_stride, &dn_full[st]);
-                        if (sbd > 0)
-                            bulk_rows(stg + od_sc,
-                                      (const uint8_t*)pool.down.scale +
-                                          slot * pool.down.scale_slot_stride +
-                                          r0 * pool.down.scale_row_stride,
-                                      16, sbd, pool.down.scale_row_stride, &dn_full[st]);
-                        state = 4;
-                    }
-                    // the stage is released to its MMA warp once the group's h is complete: the
-                    // warp then reads h without an acquire of its own (release -> acquire here,
-                    // then the stage barrier)
-                    if (state == 4 && ld_acquire_gpu(done + base + lane) >= tiles_i) {
-                        hdr[GD_DGLOB] = __float_as_int(dgl);
-                        if (hdr[GD_POOL] && sgate) {
-                            const int nt = hdr[GD_NT];
-                            for (int k = 0; k < nt; ++k)
-                                hdr[GD_W + k] = __float_as_int(__ldcg(sgate + hdr[GD_TOK + k]));
-                        }
-                        mbar_arrive(&dn_full[st]);
-                        state = 2;
-                    }
-                    if (w > 8) __nanosleep(w < 1024 ? 32 : 256);
-                }
-                ok = __all_sync(0xffffffffu, ok);
-                base += nb;
-                j0 += nb;
+                break;
             }
+            if (state == S_DRAIN && mbar_test_wait(gu_drained, 0)) state = S_FREE;
+            if (state == S_FREE && mbar_test_wait(&dn_empty[lane], ((j / NDT) & 1) ^ 1)) {
+                copy_record(hdr, r);
+                hdr[GD_GID] = j % n_groups;
+                state = hdr[GD_MISS] > 0 ? S_REFILL : S_ISSUE;
+            }
+            if (state == S_REFILL && refill_ready(P, hdr[GD_MISS] - 1, 1)) state = S_ISSUE;
+            if (state == S_ISSUE) {
+                const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
+                const int slot = hdr[GD_SLOT];
+                const int64_t r0 = (int64_t)(rt0 + (j / n_groups) * G) * 16;
+                dgl = global_of_early(pool.down, slot);
+                mbar_expect_tx(&dn_full[lane], (uint32_t)(16 * (cbd + sbd)));
+                bulk_rows(stg + kStageHdr,
+                          (const uint8_t*)pool.down.data + slot * pool.down.slot_stride +
+                              r0 * pool.down.row_stride,
+                          16, cbd, pool.down.row_stride, &dn_full[lane]);
+                if (sbd > 0)
+                    bulk_rows(stg + od_sc,
+                              (const uint8_t*)pool.down.scale + slot * pool.down.scale_slot_stride +
+                                  r0 * pool.down.scale_row_stride,
+                              16, sbd, pool.down.scale_row_stride, &dn_full[lane]);
+                state = S_H;
+            }
+            if (state == S_H && ld_acquire_gpu(done + j % n_groups) >= tiles_i) {
+                hdr[GD_DGLOB] = __float_as_int(dgl);
+                if (hdr[GD_POOL] && sgate) {
+                    const int nt = hdr[GD_NT];
+                    for (int k = 0; k < nt; ++k)
+                        hdr[GD_W + k] = __float_as_int(__ldcg(sgate + hdr[GD_TOK + k]));
+                }
+                mbar_arrive(&dn_full[lane]);
+                j += NDT;
+                state = S_DONE;
+                if (j < total) {
+                    load_record(P, j % n_groups, r);  // (used once the stage is free again)
+                    state = S_FREE;
+                }
+            }
+            if (w > 8) __nanosleep(32);
         }
+        (void)ok;
         return;
     }
 
