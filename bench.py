@@ -453,6 +453,9 @@ def main():
         return
     if world > 1:
         import datetime
+        # rank 0's stdout carries exactly one JSON line: no NCCL version banner on it
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
