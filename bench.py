@@ -279,7 +279,8 @@ def run_nvmoe(a, rank, world, local_rank):
         "e2e": {"value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": B * H * 2 + L * B * E * 4,
                 "d2h_bytes_per_step": L * B * H * 2},
-        "gpu_launches": a.steps * L * 4,
+        # per layer step: decode_front_kernel + ffn_fused (misses are copied in by the FFN)
+        "gpu_launches": a.steps * L * 2,
         "roofline": {"bound": "hbm", "kernel": "expert FFN (prep + ffn_fused, one layer)",
                      "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
