@@ -8,9 +8,10 @@ Workload (one "step" = one decode batch through a stack of MoE layers):
   128 slots per layer prewarmed with each layer's most frequent experts; 48 layers with
   distinct slot pools (10.9 GB of pools: inputs larger than L2 between steps); misses refill
   from a pinned host tier holding all 512 experts (shared by the layers' pools).
-  Per layer: router top-k -> slot remap (LRU, miss list) -> SM refill gather from pinned host
-  -> fused FFN (gate/up SwiGLU, down, weighted combine, shared expert).  Every layer reads
-  the same token batch; layers are independent (no norm / attention between them).
+  Per layer: router top-k -> slot remap (LRU, miss list) -> fused FFN (gate/up SwiGLU, down,
+  weighted combine, shared expert) that also copies the misses in from pinned host memory.
+  Every layer reads the same token batch; layers are independent (no norm / attention between
+  them), so a layer's routing and remap overlap the previous layer's FFN.
 
 metric: layer tokens/s = batch * layers / step time (device CUDA events, max over ranks).
 N > 1: independent replicas (one stack per GPU, own batch): weak scaling, no collective on the
@@ -166,7 +167,7 @@ def run_nvmoe(a, rank, world, local_rank):
         for l in range(L):
             U[r, l] = len(np.unique(ids[l]))
 
-    # one captured graph per round: L x nvmoe_decode_layer (router+remap+refill+FFN)
+    # one captured graph per round: L x nvmoe_decode_layer (router + remap + FFN with refill)
     plans = stack.plans(B)
     cap_stream = torch.cuda.Stream(dev)
     stack.forward(xs[0], logits[0], out)  # eager pass: attributes, allocations
