@@ -45,11 +45,15 @@ typedef void* nvmoe_event_t;  /* cudaEvent_t  */
 /* Weight formats of the slot pool.  NVMOE_Q_NVFP4 is the FTW bank layout of the Python
  * engine (nvme_offload_cache.py:824-835): codes [rows, K/2] u8 with w[2b] in the low nibble
  * of byte b, one E4M3 scale per 16 values [rows, K/16], one fp32 global per slot and matrix.
- * NVMOE_Q_Q2_K / NVMOE_Q_IQ2_XXS are ggml super-blocks of 256 values (84 / 66 bytes). */
+ * NVMOE_Q_Q2_K / NVMOE_Q_IQ2_XXS are ggml super-blocks of 256 values (84 / 66 bytes).
+ * NVMOE_Q_BF16 is the Python engine's bf16 weight banks (the CPU-plumbing layer,
+ * nvme_offload_cache.py bank_views); the FFN multiplies them in f16, exact within the f16
+ * range. */
 enum nvmoe_quant {
     NVMOE_Q_NVFP4 = 0,
     NVMOE_Q_Q2_K = 1,
     NVMOE_Q_IQ2_XXS = 2,
+    NVMOE_Q_BF16 = 3, /* plain bf16 rows [rows, K] (2 bytes per value), no scale bank */
 };
 
 /* ---------------------------------------------------------------- error text */

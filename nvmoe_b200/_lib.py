@@ -42,6 +42,7 @@ STATUS_NAMES = {
 NVMOE_Q_NVFP4 = 0
 NVMOE_Q_Q2_K = 1
 NVMOE_Q_IQ2_XXS = 2
+NVMOE_Q_BF16 = 3
 
 NVMOE_ROUTER_SOFTMAX = 0
 NVMOE_ROUTER_SIGMOID_BIAS = 1

@@ -69,6 +69,38 @@ struct FmtNvfp4 {
 };
 
 
+// ------------------------------------------------------------------ bf16 rows
+// [rows, K] bf16, no scale bank.  Lane quarter q owns the 32 values 32 q .. 32 q + 31 of a
+// 128-wide warp tile (64 bytes); step s covers values 4 s .. 4 s + 3.  bf16 -> f16 is exact for
+// magnitudes in the f16 normal range (bf16 has the shorter mantissa).
+struct FmtBf16 {
+    static constexpr int kWarpTileK = 128;
+    static constexpr int kSteps = 8;
+    static constexpr int kAuxBytes = 0;
+    struct Row {
+        uint4 v[4];
+    };
+    __device__ __forceinline__ static void load_smem(Row& r, const uint8_t* base,
+                                                     const uint8_t*, int k0, int q,
+                                                     const uint32_t* = nullptr) {
+        const uint4* p = reinterpret_cast<const uint4*>(base + 2 * k0 + 64 * q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r.v[i] = p[i];
+    }
+    __host__ __device__ static constexpr int code_bytes(int k) { return 2 * k; }
+    __host__ __device__ static constexpr int scale_bytes(int) { return 0; }
+    __device__ __forceinline__ static uint32_t to_f16x2(uint32_t w) {
+        const __half2 h = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    __device__ __forceinline__ static void deq(const Row& r, int s, uint32_t& lo, uint32_t& hi) {
+        const uint4 u = r.v[s >> 1];
+        lo = to_f16x2((s & 1) ? u.z : u.x);
+        hi = to_f16x2((s & 1) ? u.w : u.y);
+    }
+    __device__ __forceinline__ static int kofs(int q, int s) { return 32 * q + 4 * s; }
+};
+
 // ------------------------------------------------------------------ Q2_K (ggml block_q2_K)
 // 84 B per 256 values: scales[16] (low nibble sc, high nibble m), qs[64], fp16 d, fp16 dmin;
 // value e = 128 h + 32 j + 16 l16 + l (l < 16) is (qs[32 h + 16 l16 + l] >> 2 j) & 3 of

@@ -733,6 +733,7 @@ bool pool_aligned(const nvmoe_expert_pool& p) {
     const bool nv = p.quant == NVMOE_Q_NVFP4;
     auto rb = [&](int k) {
         return p.quant == NVMOE_Q_NVFP4 ? k / 2
+             : p.quant == NVMOE_Q_BF16  ? FmtBf16::code_bytes(k)
              : p.quant == NVMOE_Q_Q2_K  ? FmtQ2K::code_bytes(k)
                                         : FmtIQ2XXS::code_bytes(k);
     };
@@ -774,7 +775,8 @@ int launch_fmt(FfnParams& P, cudaStream_t st) {
     const int avail = kSmemCap - fixed - (P.ypart_smem ? yp_bytes : 0);
     // down stage counts are multiples of the 8 MMA warps (see the down phase)
     FL.nst_gu = std::min(4, (avail - kCW * FL.stage_dn) / FL.stage_gu);
-    if (FL.nst_gu < 2) return NVMOE_ERR_UNSUPPORTED;
+    // (one stage only for the widest items, e.g. bf16 rows: loads then do not overlap the math)
+    if (FL.nst_gu < 1) return NVMOE_ERR_UNSUPPORTED;
     FL.nst_dn = std::min(32, (avail - FL.nst_gu * FL.stage_gu) / FL.stage_dn) / kCW * kCW;
     if (FL.nst_dn < kCW) return NVMOE_ERR_UNSUPPORTED;
     FL.nst_dn_ext = std::min(32, FL.nst_gu * FL.stage_gu / FL.stage_dn) / kCW * kCW;
@@ -821,14 +823,14 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
         if (!pool_ok(sp) || sp.quant != pool.quant || sp.hidden != H || sp.inter != I)
             return NVMOE_ERR_INVALID_ARG;
     }
-    const bool nv = pool.quant == NVMOE_Q_NVFP4;
-    if (!nv && pool.quant != NVMOE_Q_Q2_K && pool.quant != NVMOE_Q_IQ2_XXS)
+    const bool nv = pool.quant == NVMOE_Q_NVFP4, bf = pool.quant == NVMOE_Q_BF16;
+    if (!nv && !bf && pool.quant != NVMOE_Q_Q2_K && pool.quant != NVMOE_Q_IQ2_XXS)
         return NVMOE_ERR_UNSUPPORTED;
     // warp tiling: gate_up K = H over 8 warps, down K = I per warp, 16-row tiles; K tiles of
     // 128 values (NVFP4) or one 256-value super-block (Q2_K / IQ2_XXS)
     // (NVFP4 shapes with H and I multiples of 256 also run on the FP4 tensor-core kernel, which
     // has no further constraint; ffn_fp4_eligible decides below)
-    const int tk = nv ? FmtNvfp4::kWarpTileK : FmtQ2K::kWarpTileK;
+    const int tk = nv ? FmtNvfp4::kWarpTileK : bf ? FmtBf16::kWarpTileK : FmtQ2K::kWarpTileK;
     const bool mma_shape = H % (kConsumerWarps * tk) == 0 && I % tk == 0 && I % 16 == 0;
     const bool fp4_shape = nv && H % 256 == 0 && I % 256 == 0;
     if (!mma_shape && !fp4_shape) return NVMOE_ERR_UNSUPPORTED;
@@ -836,10 +838,11 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
         return NVMOE_ERR_INVALID_ARG;
     if (!pool_aligned(pool) || (args->shared && !pool_aligned(*args->shared)))
         return NVMOE_ERR_INVALID_ARG;
-    const int rbh = nv ? H / 2 : (pool.quant == NVMOE_Q_Q2_K ? FmtQ2K::code_bytes(H)
-                                                             : FmtIQ2XXS::code_bytes(H));
-    const int rbi = nv ? I / 2 : (pool.quant == NVMOE_Q_Q2_K ? FmtQ2K::code_bytes(I)
-                                                             : FmtIQ2XXS::code_bytes(I));
+    auto row_bytes = [&](int k) {
+        return nv ? k / 2 : bf ? FmtBf16::code_bytes(k)
+             : pool.quant == NVMOE_Q_Q2_K ? FmtQ2K::code_bytes(k) : FmtIQ2XXS::code_bytes(k);
+    };
+    const int rbh = row_bytes(H), rbi = row_bytes(I);
     if (pool.gate.row_stride < rbh || pool.up.row_stride < rbh || pool.down.row_stride < rbi)
         return NVMOE_ERR_INVALID_ARG;
     if (nv && (pool.gate.scale_row_stride < H / 16 || pool.down.scale_row_stride < I / 16))
@@ -890,6 +893,7 @@ int ffn_launch_main(FfnParams& P, cudaStream_t st) {
     switch (P.pool.quant) {
         case NVMOE_Q_Q2_K: return launch_fmt<FmtQ2K>(P, st);
         case NVMOE_Q_IQ2_XXS: return launch_fmt<FmtIQ2XXS>(P, st);
+        case NVMOE_Q_BF16: return launch_fmt<FmtBf16>(P, st);
         default: return launch_fmt<FmtNvfp4>(P, st);
     }
 }

@@ -9,11 +9,12 @@ Layouts (what the kernels read):
   GGUF block_nvfp4 (36 B / 64 values): 4 UE4M3 scales then 4 x 8 code bytes, byte j of
       sub-block k = (w[16k+j] low, w[16k+j+8] high) (convert_ftw_to_gguf.py:60-69).
   Q2_K (84 B / 256) and IQ2_XXS (66 B / 256): ggml super-blocks, rows of K/256 blocks.
+  bf16: plain rows [S, rows, 2 K] u8 (the bf16 values), the CPU-plumbing layer's weights.
 
 Synthetic distributions follow the benchmark configurations: E2M1 codes uniform over the 16
 values, one E4M3 scale per 16 values drawn 2^U(-8,-2), fp32 global 1/448; Q2_K 2-bit quants,
 4-bit scales and mins uniform, fp16 d, dmin ~ |N(0, 0.01)|; IQ2_XXS codebook indices, sign
-indices and 4-bit scales uniform, fp16 d ~ |N(0, 0.01)|.
+indices and 4-bit scales uniform, fp16 d ~ |N(0, 0.01)|; bf16 weights ~ N(0, 0.02).
 """
 from __future__ import annotations
 
@@ -30,7 +31,7 @@ IQ2XXS_BLOCK_BYTES = 66
 @dataclass
 class QuantMatrix:
     """One matrix bank of a slot pool: data [S, rows, row_bytes] u8 (+ NVFP4 scales/global)."""
-    quant: str                 # "nvfp4" | "q2_k" | "iq2_xxs"
+    quant: str                 # "nvfp4" | "q2_k" | "iq2_xxs" | "bf16"
     rows: int
     cols: int                  # K
     data: torch.Tensor         # u8 [S, rows, row_bytes]
@@ -68,6 +69,8 @@ def row_bytes(quant: str, cols: int) -> int:
         return cols // 256 * Q2K_BLOCK_BYTES
     if quant == "iq2_xxs":
         return cols // 256 * IQ2XXS_BLOCK_BYTES
+    if quant == "bf16":
+        return 2 * cols
     raise ValueError(quant)
 
 
@@ -104,6 +107,10 @@ def random_matrix(quant: str, n_slots: int, rows: int, cols: int, gen: torch.Gen
                              dtype=torch.uint8)
         data = torch.cat([d, body], dim=-1).reshape(n_slots, rows, nb * IQ2XXS_BLOCK_BYTES)
         return QuantMatrix(quant, rows, cols, data.contiguous())
+    if quant == "bf16":  # the CPU-plumbing layer's weights: N(0, 0.02) in bf16
+        w = torch.randn((n_slots, rows, cols), generator=gen, device=device) * 0.02
+        data = w.to(torch.bfloat16).view(torch.uint8).reshape(n_slots, rows, 2 * cols)
+        return QuantMatrix(quant, rows, cols, data.contiguous())
     raise ValueError(quant)
 
 
@@ -133,10 +140,13 @@ class ExpertWeights:
 
     def banks(self) -> tuple[torch.Tensor, ...]:
         """FTW bank order (gate_up_packed, gate_up_scale, gate_up_global, down_packed,
-        down_scale, down_global) for NVFP4, (gate_up, down) for the GGUF formats."""
+        down_scale, down_global) for NVFP4, (gate_up, down) for the GGUF formats and, as bf16
+        tensors [S, 2I, H] / [S, H, I], for bf16."""
         if self.quant == "nvfp4":
             return (self.gate_up.data, self.gate_up.scale, self.gate_up.glob.view(-1, 1),
                     self.down.data, self.down.scale, self.down.glob.view(-1, 1))
+        if self.quant == "bf16":
+            return (self.gate_up.data.view(torch.bfloat16), self.down.data.view(torch.bfloat16))
         return (self.gate_up.data, self.down.data)
 
 

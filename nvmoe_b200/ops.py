@@ -14,7 +14,8 @@ from . import _lib
 from ._lib import check, lib
 from .formats import ExpertWeights, QuantMatrix
 
-_QUANT = {"nvfp4": _lib.NVMOE_Q_NVFP4, "q2_k": _lib.NVMOE_Q_Q2_K, "iq2_xxs": _lib.NVMOE_Q_IQ2_XXS}
+_QUANT = {"nvfp4": _lib.NVMOE_Q_NVFP4, "q2_k": _lib.NVMOE_Q_Q2_K, "iq2_xxs": _lib.NVMOE_Q_IQ2_XXS,
+          "bf16": _lib.NVMOE_Q_BF16}
 
 
 def _stream(stream=None) -> int:

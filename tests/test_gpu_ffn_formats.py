@@ -56,3 +56,43 @@ def test_ffn_gguf_formats_match_oracle(cuda_device, quant, H, I, S, n_tok, k):
     yv = y.float().cpu().numpy()
     assert np.isfinite(yv).all()
     assert np.abs(yv - yr).max() <= 1e-2 * float(np.abs(yr).max())
+
+
+@pytest.mark.parametrize("n_tok,k,shared", [(1, 4, False), (32, 4, False), (8, 4, True)])
+def test_ffn_bf16_pool_matches_oracle(cuda_device, n_tok, k, shared):
+    """bf16 slot pools (the CPU-plumbing layer: 64 experts, top-4, H 1024, I 256, 16 slots)
+    through the decode FFN, which multiplies them in f16, against the fp32 oracle."""
+    H, I, S = 1024, 256, 16
+    pool = random_experts("bf16", S, H, I, seed=91).to(cuda_device)
+    sh = random_experts("bf16", 1, H, I, seed=92).to(cuda_device) if shared else None
+    rng = np.random.default_rng(93 + n_tok)
+    x = torch.from_numpy(rng.standard_normal((n_tok, H)).astype(np.float32)).to(
+        torch.bfloat16).to(cuda_device)
+    ids = torch.from_numpy(np.stack([rng.choice(S, size=k, replace=False)
+                                     for _ in range(n_tok)]).astype(np.int32)).to(cuda_device)
+    w = torch.from_numpy(rng.random((n_tok, k)).astype(np.float32)).to(cuda_device)
+    st = torch.full((1,), 77, dtype=torch.int32, device=cuda_device)
+    y = ops.moe_ffn(pool, x, ids, w, shared=sh, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+
+    def dense(wts):
+        def get(which, s):
+            m = wts.gate_up if which != "down" else wts.down
+            rows = slice(0, I) if which == "gate" else (slice(I, 2 * I) if which == "up" else slice(None))
+            b = m.data[s, rows].cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+            return R.bf16_to_f32(b)
+        return get
+    d = dense(pool)
+    shared_dense = None
+    if shared:
+        ds = dense(sh)
+        shared_dense = (ds("gate", 0), ds("up", 0), ds("down", 0))
+    yr = R.moe_ffn(x.cpu().view(torch.int16).numpy().view(np.uint16), ids.cpu().numpy(),
+                   w.cpu().numpy(), lambda s: d("gate", s), lambda s: d("up", s),
+                   lambda s: d("down", s), shared=shared_dense)
+    yv = y.float().cpu().numpy()
+    assert np.isfinite(yv).all()
+    scale = float(np.abs(yr).max())
+    assert np.abs(yv - yr).max() <= 1e-2 * scale
+    assert np.abs(yv - yr).mean() <= 2e-3 * scale
