@@ -158,3 +158,44 @@ def test_decode_layers_back_to_back_equal_serialised(cuda_device):
         assert torch.equal(out_a, out_b), f"step {r}"
         for ta, tb in zip(a.tables, b.tables):
             assert torch.equal(ta.slot_of_real, tb.slot_of_real)
+
+
+@pytest.mark.parametrize("n_tok", [1, 32])
+def test_decode_layer_cpu_plumbing_bf16(cuda_device, n_tok):
+    """The CPU-plumbing layer (64 experts, top-4, H 1024, I 256, bf16 weights ~N(0, 0.02), a
+    16-slot LRU pool, Zipf(1.1) routing) through nvmoe_decode_layer against the oracle chain."""
+    cfg = StackConfig(n_layers=1, n_experts=64, top_k=4, hidden=1024, inter=256, cache_size=16,
+                      quant="bf16", shared_expert=False)
+    stack = MoEStack(cfg, device=cuda_device, seed=11)
+    orc = OracleLayer(64, 16)
+    bias = layer_log_bias(1, 64, 1.1, seed=0)[0]
+    host = stack.host
+
+    def dense(which, e):
+        m = host.gate_up if which != "down" else host.down
+        rows = slice(0, 256) if which == "gate" else (slice(256, 512) if which == "up" else slice(None))
+        return R.bf16_to_f32(m.data[e, rows].contiguous().view(torch.int16).numpy().view(np.uint16))
+
+    rng = np.random.default_rng(n_tok)
+    checked = 0
+    for step in range(6):
+        lg = router_logits(n_tok, bias, rng)
+        x = torch.from_numpy(rng.standard_normal((n_tok, 1024)).astype(np.float32)).to(torch.bfloat16)
+        y = stack.layer_step(0, x.to(cuda_device), torch.from_numpy(lg).to(cuda_device))
+        plan = stack.plans(n_tok)[0]
+        torch.cuda.synchronize()
+        rids, rw = R.router_topk_softmax(lg, 4)
+        ref = orc.eval(rids.reshape(-1), is_decode=True)
+        if ref["status"] != 0:  # more distinct experts than the 16 slots at this batch
+            assert int(plan.status.item()) == ref["status"]
+            continue
+        assert int(plan.status.item()) == 0
+        np.testing.assert_array_equal(plan.slot_ids.cpu().numpy().reshape(-1), ref["slots"])
+        yr = R.moe_ffn(x.view(torch.int16).numpy().view(np.uint16), rids, rw,
+                       lambda e: dense("gate", e), lambda e: dense("up", e),
+                       lambda e: dense("down", e))
+        scale = float(np.abs(yr).max())
+        assert np.abs(y.float().cpu().numpy() - yr).max() <= 1e-2 * scale
+        checked += 1
+    if n_tok == 1:
+        assert checked == 6  # (at batch 32 the 16 slots overflow, as the reference's would)
