@@ -38,6 +38,7 @@ extern "C" {
 #define NVMOE_ERR_NO_TABLES -9      /* IQ2_XXS grid table not registered */
 #define NVMOE_ERR_TIMEOUT -10       /* a bounded wait inside a kernel gave up (status word) */
 #define NVMOE_ERR_SCRATCH_LIMIT -11 /* call needs more scratch than nvmoe_moe_ffn_noalloc has */
+#define NVMOE_ERR_GROUP_LIMIT -12   /* more token groups than a kernel's group tables hold */
 
 typedef void* nvmoe_stream_t; /* cudaStream_t */
 typedef void* nvmoe_event_t;  /* cudaEvent_t  */
@@ -163,6 +164,23 @@ typedef struct nvmoe_expert_pool {
     nvmoe_matrix_bank gate, up, down;
 } nvmoe_expert_pool;
 
+/* Kernel choice of one FFN call (nvmoe_ffn_args.kernel); the configuration the reference reads
+ * from NVMOE_* / FREETOKEN_* environment variables travels here, per call, instead.
+ *   NVMOE_KERNEL_DEFAULT: nvmoe_moe_ffn runs the mma.sync kernel; nvmoe_moe_ffn_prefill runs the
+ *     block-scaled FP4 kernel where the shapes allow it, else the kind::f16 kernel.
+ *   NVMOE_KERNEL_MMA: decode FFN on in-register dequantised weights feeding mma.sync.
+ *   NVMOE_KERNEL_FP4: block-scaled FP4 tensor-core MMAs (tcgen05 kind::mxf4nvf4) on the NVFP4
+ *     banks as stored (decode: NVFP4 pools with H and I multiples of 256, <= 256 tokens; it falls
+ *     back to NVMOE_KERNEL_MMA where those do not hold).
+ *   NVMOE_KERNEL_F16: prefill on tcgen05 kind::f16 MMAs with the weights dequantised into
+ *     tensor memory. */
+enum nvmoe_kernel {
+    NVMOE_KERNEL_DEFAULT = 0,
+    NVMOE_KERNEL_MMA = 1,
+    NVMOE_KERNEL_FP4 = 2,
+    NVMOE_KERNEL_F16 = 3,
+};
+
 /* Arguments of one FFN call.  y[t] = sum_j w[t,j] * down_s( silu(gate_s x[t]) * up_s x[t] ),
  * s = slot_ids[t, j]; plus, when `shared` is set, the always-on shared expert (slot 0 of that
  * pool) with weight 1, or sigmoid(x[t] . shared_gate) when shared_gate (bf16 [H]) is set
@@ -184,6 +202,7 @@ typedef struct nvmoe_ffn_args {
     void* workspace;      /* device scratch, >= nvmoe_moe_ffn_workspace_size  */
     size_t workspace_bytes;
     int32_t* status;      /* optional device int: NVMOE_ERR_BAD_SLOT on a bad slot id */
+    int32_t kernel;       /* enum nvmoe_kernel: which kernel runs the call (0 = the default) */
 } nvmoe_ffn_args;
 
 size_t nvmoe_moe_ffn_workspace_size(int n_tok, int top_k, int hidden, int inter, int n_slots);
@@ -192,9 +211,9 @@ int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
 /* Which kernel nvmoe_moe_ffn takes for these arguments (no launch): NVMOE_FFN_PATH_MMA
  * (in-register dequantisation feeding mma.sync; the default) or NVMOE_FFN_PATH_FP4 (block-scaled
  * FP4 MMAs on the tensor cores, weights fed unchanged from the slot banks, activations as 4
- * NVFP4 residual terms), which runs for NVFP4 pools with H and I multiples of 256 when the
- * environment variable NVMOE_FFN_KERNEL is "fp4".  Negative = the call's error status.  An
- * addition of this library (no counterpart in the reference). */
+ * NVFP4 residual terms), which runs when args->kernel is NVMOE_KERNEL_FP4 and the pool is NVFP4
+ * with H and I multiples of 256.  Negative = the call's error status.  An addition of this
+ * library (no counterpart in the reference). */
 enum { NVMOE_FFN_PATH_MMA = 0, NVMOE_FFN_PATH_FP4 = 1 };
 int nvmoe_moe_ffn_path(const nvmoe_ffn_args* args);
 
@@ -206,6 +225,8 @@ int nvmoe_moe_ffn_path(const nvmoe_ffn_args* args);
  * into the library, present on every GPU that loads it until the process exits.  Calls whose
  * nvmoe_moe_ffn_workspace_size exceeds 16 MiB return NVMOE_ERR_SCRATCH_LIMIT.  The first call on
  * a device looks up the array's address (once per device); make it before any stream capture.
+ * The address is cached for the process's life and does not survive cudaDeviceReset: do not
+ * call this entry point on a device after resetting it.
  * All calls on a device share the array (it keeps the last call's contents; nothing in it needs
  * to start at zero), so calls that overlap on the GPU race: serialise them.  Allocates nothing. */
 int nvmoe_moe_ffn_noalloc(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
@@ -213,9 +234,9 @@ int nvmoe_moe_ffn_noalloc(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
 /* R10 — the same FFN for large batches (prefill, ~1k tokens and up): entries sorted by slot into
  * tiles, each expert's gate/up and down as tcgen05 grouped GEMMs (NVFP4 pools).  Default kernel:
  * block-scaled FP4 MMAs (kind::mxf4nvf4) on the slot banks' codes and scales as stored, the
- * activations as 4 NVFP4 residual terms, tiles of 32 entries (H a multiple of 512, I of 256 up
- * to 1536); NVMOE_PREFILL_KERNEL=f16 (or other shapes) selects kind::f16 MMAs on weights
- * dequantised into tensor memory, tiles of 128.  Replaces the narrowed-union prefill's
+ * activations as 3 NVFP4 residual terms, tiles of 42 entries (3 x 42 = 126 MMA rows; H a
+ * multiple of 512, I of 256 up to 1536); args->kernel == NVMOE_KERNEL_F16 (or other shapes)
+ * selects kind::f16 MMAs on weights dequantised into tensor memory, tiles of 128.  Replaces the narrowed-union prefill's
  * _expert_gemm call (nvme_offload_cache.py:1957-2013) and mul_mat_id for n_tokens > 1
  * (moe_cache_probe.cpp:1668-1684).  Same arguments and result as nvmoe_moe_ffn; workspace >=
  * nvmoe_moe_ffn_prefill_workspace_size (the sorted activation images, h and the per-entry

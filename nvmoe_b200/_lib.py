@@ -23,6 +23,7 @@ NVMOE_ERR_BAD_SLOT = -8
 NVMOE_ERR_NO_TABLES = -9
 NVMOE_ERR_TIMEOUT = -10
 NVMOE_ERR_SCRATCH_LIMIT = -11
+NVMOE_ERR_GROUP_LIMIT = -12
 
 STATUS_NAMES = {
     0: "NVMOE_OK",
@@ -37,6 +38,7 @@ STATUS_NAMES = {
     -9: "NVMOE_ERR_NO_TABLES",
     -10: "NVMOE_ERR_TIMEOUT",
     -11: "NVMOE_ERR_SCRATCH_LIMIT",
+    -12: "NVMOE_ERR_GROUP_LIMIT",
 }
 
 NVMOE_Q_NVFP4 = 0
@@ -46,6 +48,11 @@ NVMOE_Q_BF16 = 3
 
 NVMOE_ROUTER_SOFTMAX = 0
 NVMOE_ROUTER_SIGMOID_BIAS = 1
+
+NVMOE_KERNEL_DEFAULT = 0
+NVMOE_KERNEL_MMA = 1
+NVMOE_KERNEL_FP4 = 2
+NVMOE_KERNEL_F16 = 3
 
 
 class NvmoeError(RuntimeError):
@@ -124,6 +131,7 @@ class FfnArgs(C.Structure):
         ("workspace", C.c_void_p),
         ("workspace_bytes", C.c_size_t),
         ("status", C.c_void_p),
+        ("kernel", C.c_int32),
     ]
 
 

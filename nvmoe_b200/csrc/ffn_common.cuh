@@ -146,6 +146,7 @@ struct FfnParams {
     int grp_tok;           // entries per token group: min(8, n_tok), at least 1
     const uint32_t* aux_table;  // the format's lookup table in device memory (IQ2_XXS grid)
     int ypart_smem;        // 1: the down phase keeps y_part in shared memory
+    int kernel;            // enum nvmoe_kernel of the call
     int use_fp4;           // 1: the block-scaled FP4 tensor-core kernel runs this call (NVFP4)
     int spare_sm;          // 1: the FFN grid leaves one SM free (for the next layer's front)
     FfnRefill rf;          // misses this call copies in (rf.n_banks = 0: none)

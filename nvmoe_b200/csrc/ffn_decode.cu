@@ -883,6 +883,9 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P) {
     // caller's slot ids repeat a slot within a token
     P.grp_tok = std::max(1, std::min(kGroupMaxTok, args->n_tok));
     P.aux_table = aux_table;
+    if (args->kernel < NVMOE_KERNEL_DEFAULT || args->kernel > NVMOE_KERNEL_F16)
+        return NVMOE_ERR_INVALID_ARG;
+    P.kernel = args->kernel;
     P.use_fp4 = ffn_fp4_eligible(P) ? 1 : 0;
     if (!P.use_fp4 && !mma_shape) return NVMOE_ERR_UNSUPPORTED;
     return NVMOE_OK;

@@ -101,9 +101,12 @@ struct __align__(64) Fp4Params {
     FfnParams P;
 };
 
+__device__ __forceinline__ void report_status(const FfnParams& P, int code) {
+    atomicExch(wsp<int>(P, P.L.hdr) + HDR_STATUS, code);
+    if (P.status) atomicExch(P.status, code);
+}
 __device__ __forceinline__ void report_timeout(const FfnParams& P) {
-    atomicExch(wsp<int>(P, P.L.hdr) + HDR_STATUS, NVMOE_ERR_TIMEOUT);
-    if (P.status) atomicExch(P.status, NVMOE_ERR_TIMEOUT);
+    report_status(P, NVMOE_ERR_TIMEOUT);
 }
 
 using namespace fp4;
@@ -258,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_fp4_kernel(const __grid_const
             const int t = i / H, col = i - t * H;
             P.y[(int64_t)t * P.y_stride + col] = 0;
         }
-        if (n_groups > kMaxGroups && c == 0 && tid == 0) report_timeout(P);
+        if (n_groups > kMaxGroups && c == 0 && tid == 0) report_status(P, NVMOE_ERR_GROUP_LIMIT);
     }
     const int NG = (n_groups > 0 && n_groups <= kMaxGroups) ? n_groups : 0;
     const int U1 = NG * JB, U2 = NG * RB;
@@ -743,7 +746,7 @@ bool fp4_pool_maps(const nvmoe_expert_pool& p, CUtensorMap* m) {
 
 // Whether a call runs on the FP4 tensor-core kernel (decided in ffn_setup, so the kernels
 // before it know whether to write the f16 token copy): NVFP4 pools whose shapes it covers, when
-// the environment variable NVMOE_FFN_KERNEL is "fp4".  By default the mma.sync kernel runs:
+// the call asks for it (nvmoe_ffn_args.kernel == NVMOE_KERNEL_FP4).  By default the mma.sync kernel runs:
 // measured at batch 8 on the Qwen3.8-shaped layer it is faster (the FP4 kernel's per-unit
 // epilogue handoffs between CTAs cost more than its dequantisation-free stream saves).
 bool ffn_fp4_eligible(const FfnParams& P) {
@@ -757,8 +760,7 @@ bool ffn_fp4_eligible(const FfnParams& P) {
         (uint64_t)P.n_tok * P.pool.hidden * (kFp4MaxCtas + 1) >= (1ull << 32))
         return false;
     if (P.x_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(P.x) & 15)) return false;
-    const char* env = std::getenv("NVMOE_FFN_KERNEL");
-    if (!env || std::strcmp(env, "fp4") != 0) return false;
+    if (P.kernel != NVMOE_KERNEL_FP4) return false;
     CUtensorMap m[6];
     if (!fp4_pool_maps(P.pool, m)) return false;
     if (P.has_shared && !fp4_pool_maps(P.shared, m)) return false;

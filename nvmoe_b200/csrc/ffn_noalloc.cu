@@ -15,7 +15,10 @@
 //     rejected with NVMOE_ERR_SCRATCH_LIMIT, before anything is launched;
 //   - the first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress (once per device, with that device current); make that first call
-//     before any stream capture;
+//     before any stream capture.  The address is kept for the life of the process: it does
+//     not survive cudaDeviceReset (or any other teardown of the device's primary context),
+//     after which the array may sit elsewhere; a process that resets a device must not call
+//     this entry point on it again;
 //   - every call on a device shares the one array, which keeps the previous call's contents
 //     (nothing in it has to start at zero: each call writes every scratch word before reading
 //     it); calls that overlap on the GPU (different streams, or different host threads without

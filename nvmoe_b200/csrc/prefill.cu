@@ -573,11 +573,10 @@ bool prefill_fp4_ok(const nvmoe_ffn_args* a);
 size_t prefill_fp4_workspace(int n_tok, int top_k, int H, int I, int n_slots);
 int prefill_fp4_run(const nvmoe_ffn_args* a, cudaStream_t st);
 
-// The block-scaled FP4 path (prefill_fp4.cu) runs when the shapes suit it, unless the
-// environment variable NVMOE_PREFILL_KERNEL is "f16" (this file's kind::f16 path).
+// The block-scaled FP4 path (prefill_fp4.cu) runs when the shapes suit it, unless the call
+// asks for this file's kind::f16 path (nvmoe_ffn_args.kernel == NVMOE_KERNEL_F16).
 bool prefill_use_fp4(const nvmoe_ffn_args* a) {
-    const char* env = std::getenv("NVMOE_PREFILL_KERNEL");
-    return !(env && std::strcmp(env, "f16") == 0) && prefill_fp4_ok(a);
+    return a->kernel != NVMOE_KERNEL_F16 && prefill_fp4_ok(a);
 }
 
 }  // namespace nvmoe
@@ -605,6 +604,8 @@ extern "C" int nvmoe_moe_ffn_prefill(const nvmoe_ffn_args* a, nvmoe_stream_t str
     if (a->n_tok < 0 || a->top_k <= 0 || a->x_row_stride % 8 != 0 ||
         (reinterpret_cast<uintptr_t>(a->x) & 15) || a->y_row_stride % 4 != 0 ||
         (reinterpret_cast<uintptr_t>(a->y) & 7))
+        return NVMOE_ERR_INVALID_ARG;
+    if (a->kernel < NVMOE_KERNEL_DEFAULT || a->kernel > NVMOE_KERNEL_F16)
         return NVMOE_ERR_INVALID_ARG;
     if (a->n_tok == 0) return NVMOE_OK;
     if (prefill_use_fp4(a)) return prefill_fp4_run(a, (cudaStream_t)stream);

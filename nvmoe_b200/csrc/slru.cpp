@@ -10,8 +10,10 @@
 //   - pop_lru_excluding skips protected keys (probation first, then protected) and falls back to
 //     pop_lru when every key is excluded;
 //   - the first capacity hint wins; without one there is no protected cap.
-// Implementation: one slab of nodes in two intrusive doubly-linked lists plus an open-addressing
-// index, so every operation is O(1) without per-operation heap allocation.
+// Implementation: one slab of nodes (reused through a free list) in two intrusive doubly-linked
+// lists, indexed by a std::unordered_map from key to node.  Operations are O(1) on average; an
+// insert of a new key may allocate a hash node, and pop_lru_excluding builds a hash set of the
+// excluded keys on each call.
 #include <cstdint>
 #include <cstdlib>
 #include <unordered_map>

@@ -28,9 +28,18 @@ import torch.distributed as dist
 LocalFfn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 
 
+def shard_size(n_expert: int, world: int) -> int:
+    """Experts per rank.  The shards are contiguous and equal, so world must divide n_expert
+    (and not exceed it); anything else would send pairs to a rank that does not exist."""
+    if world <= 0 or n_expert < world or n_expert % world != 0:
+        raise ValueError(f"expert parallelism needs n_expert ({n_expert}) to be a positive "
+                         f"multiple of the world size ({world})")
+    return n_expert // world
+
+
 def expert_owner(expert_ids: torch.Tensor, n_expert: int, world: int) -> torch.Tensor:
     """Rank that owns each expert (contiguous shards of n_expert / world experts)."""
-    per = n_expert // world
+    per = shard_size(n_expert, world)
     return torch.div(expert_ids, per, rounding_mode="floor")
 
 
@@ -46,7 +55,7 @@ def ep_layer(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, n_expert
     world = dist.get_world_size(group)
     B, k = ids.shape
     H = x.shape[1]
-    per = n_expert // world
+    per = shard_size(n_expert, world)
     dev = x.device
     # 2. dispatch, pairs grouped by destination rank (stable: pair p = t * k + j in order)
     flat_ids = ids.reshape(-1).to(torch.int64)

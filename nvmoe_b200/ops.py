@@ -18,6 +18,24 @@ _QUANT = {"nvfp4": _lib.NVMOE_Q_NVFP4, "q2_k": _lib.NVMOE_Q_Q2_K, "iq2_xxs": _li
           "bf16": _lib.NVMOE_Q_BF16}
 
 
+_KERNELS = {"default": _lib.NVMOE_KERNEL_DEFAULT, "mma": _lib.NVMOE_KERNEL_MMA,
+            "fp4": _lib.NVMOE_KERNEL_FP4, "f16": _lib.NVMOE_KERNEL_F16}
+
+
+def kernel_choice(kernel: str | None, env_var: str) -> int:
+    """nvmoe_ffn_args.kernel for a call: the named kernel ("default", "mma", "fp4", "f16"), or,
+    when None, the value of the environment variable env_var (NVMOE_FFN_KERNEL for the decode
+    FFN, NVMOE_PREFILL_KERNEL for prefill).  The library itself reads no environment: this
+    adapter is the one place the reference's env-style configuration is accepted."""
+    import os
+    name = kernel if kernel is not None else os.environ.get(env_var, "default")
+    try:
+        return _KERNELS[name.lower()]
+    except KeyError:
+        raise ValueError(f"unknown kernel {name!r} (from {env_var if kernel is None else 'argument'});"
+                         f" one of {sorted(_KERNELS)}") from None
+
+
 def _stream(stream=None) -> int:
     s = stream if stream is not None else torch.cuda.current_stream()
     return int(s.cuda_stream)
@@ -236,7 +254,8 @@ _default_ws: dict[int, FfnWorkspace] = {}
 
 
 def ffn_path(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor,
-             weights: torch.Tensor, shared: ExpertWeights | None = None) -> str:
+             weights: torch.Tensor, shared: ExpertWeights | None = None,
+             kernel: str | None = None) -> str:
     """Kernel that moe_ffn takes for these arguments: "fp4" (block-scaled FP4 tensor-core
     MMAs) or "mma" (mma.sync on in-register dequantised weights); see nvmoe_moe_ffn_path."""
     _require_cuda(x, slot_ids, weights)
@@ -249,7 +268,8 @@ def ffn_path(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor,
     args = _lib.FfnArgs(
         C.pointer(ps), C.pointer(ss) if ss is not None else None, None, x.data_ptr(),
         x.stride(0), slot_ids.data_ptr(), slot_ids.stride(0), weights.data_ptr(),
-        weights.stride(0), k, n, x.data_ptr(), x.stride(0), ws.data_ptr(), ws.numel(), None)
+        weights.stride(0), k, n, x.data_ptr(), x.stride(0), ws.data_ptr(), ws.numel(), None,
+        kernel_choice(kernel, "NVMOE_FFN_KERNEL"))
     rc = lib().nvmoe_moe_ffn_path(C.byref(args))
     check(min(rc, 0), "nvmoe_moe_ffn_path")
     return "fp4" if rc == 1 else "mma"
@@ -258,7 +278,7 @@ def ffn_path(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor,
 def moe_ffn(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor, weights: torch.Tensor,
             shared: ExpertWeights | None = None, shared_gate: torch.Tensor | None = None,
             out: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,
-            status: torch.Tensor | None = None) -> torch.Tensor:
+            status: torch.Tensor | None = None, kernel: str | None = None) -> torch.Tensor:
     """y = routed-expert FFN over the slot pool (bf16 [n, H]); see nvmoe_moe_ffn."""
     _require_cuda(x, slot_ids, weights)
     assert x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
@@ -280,7 +300,7 @@ def moe_ffn(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor, weight
         C.pointer(ps), C.pointer(ss) if ss is not None else None,
         _ptr(shared_gate), x.data_ptr(), x.stride(0), slot_ids.data_ptr(), slot_ids.stride(0),
         weights.data_ptr(), weights.stride(0), k, n, out.data_ptr(), out.stride(0),
-        ws.data_ptr(), ws.numel(), _ptr(status))
+        ws.data_ptr(), ws.numel(), _ptr(status), kernel_choice(kernel, "NVMOE_FFN_KERNEL"))
     check(lib().nvmoe_moe_ffn(C.byref(args), _stream()), "nvmoe_moe_ffn")
     return out
 
@@ -289,7 +309,7 @@ def moe_ffn_prefill(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor
                     weights: torch.Tensor, shared: ExpertWeights | None = None,
                     shared_gate: torch.Tensor | None = None, out: torch.Tensor | None = None,
                     workspace: FfnWorkspace | None = None,
-                    status: torch.Tensor | None = None) -> torch.Tensor:
+                    status: torch.Tensor | None = None, kernel: str | None = None) -> torch.Tensor:
     """The routed-expert FFN for large batches (token-sorted tcgen05 grouped GEMM); same result
     as moe_ffn.  See nvmoe_moe_ffn_prefill."""
     _require_cuda(x, slot_ids, weights)
@@ -311,7 +331,7 @@ def moe_ffn_prefill(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor
         C.pointer(ps), C.pointer(ss) if ss is not None else None,
         _ptr(shared_gate), x.data_ptr(), x.stride(0), slot_ids.data_ptr(), slot_ids.stride(0),
         weights.data_ptr(), weights.stride(0), k, n, out.data_ptr(), out.stride(0),
-        ws.data_ptr(), ws.numel(), _ptr(status))
+        ws.data_ptr(), ws.numel(), _ptr(status), kernel_choice(kernel, "NVMOE_PREFILL_KERNEL"))
     check(lib().nvmoe_moe_ffn_prefill(C.byref(args), _stream()), "nvmoe_moe_ffn_prefill")
     return out
 
@@ -364,7 +384,7 @@ class DecodeLayerPlan:
                  host_slot_of_id: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,
                  router: str = "softmax", router_bias: torch.Tensor | None = None,
                  norm_topk: bool = True, routed_scaling: float = 1.0, device="cuda",
-                 early_outputs: bool = False):
+                 early_outputs: bool = False, kernel: str | None = None):
         self.n_tok, self.top_k = n_tok, top_k
         self.pool_s = expert_pool_struct(pool)
         self.shared_s = expert_pool_struct(shared) if shared is not None else None
@@ -398,6 +418,7 @@ class DecodeLayerPlan:
         a.ffn.workspace = self.ws.data_ptr()
         a.ffn.workspace_bytes = self.ws.numel()
         a.ffn.status = self.status.data_ptr()
+        a.ffn.kernel = kernel_choice(kernel, "NVMOE_FFN_KERNEL")
         # the caller alternates workspace / miss-list sets between consecutive steps
         a.early_outputs = int(bool(early_outputs))
         self.args = a

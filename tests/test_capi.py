@@ -46,3 +46,38 @@ def test_host_side_argument_validation_without_gpu():
     assert lib.nvmoe_moe_ffn(None, None) == _lib.NVMOE_ERR_INVALID_ARG
     assert lib.nvmoe_moe_ffn_workspace_size(8, 10, 2048, 512, 128) > 0
     assert lib.nvmoe_moe_ffn_workspace_size(0, 10, 2048, 512, 128) == 0
+
+
+def test_struct_layouts_match_a_c_compiler(tmp_path):
+    """Every ctypes mirror has the size and field offsets gcc gives the header's structs."""
+    import shutil
+    import subprocess
+
+    import pytest
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    mirrors = {"nvmoe_slot_table": _lib.SlotTable, "nvmoe_miss_list": _lib.MissList,
+               "nvmoe_matrix_bank": _lib.MatrixBank, "nvmoe_expert_pool": _lib.ExpertPool,
+               "nvmoe_ffn_args": _lib.FfnArgs, "nvmoe_refill_bank": _lib.RefillBank,
+               "nvmoe_decode_args": _lib.DecodeArgs}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nvmoe_b200.h"',
+             'int main(void) {']
+    for cname, py in mirrors.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    got = {}
+    for ln in out.splitlines():
+        c, f, v = ln.split()
+        got[(c, f)] = int(v)
+    for cname, py in mirrors.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)

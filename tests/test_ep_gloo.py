@@ -80,3 +80,43 @@ def test_ep_layer_two_ranks_matches_single_process():
 def test_expert_owner_contiguous_shards():
     ids = torch.arange(E)
     assert expert_owner(ids, E, 4).tolist() == [0, 0, 1, 1, 2, 2, 3, 3]
+
+
+def test_uneven_shards_are_rejected():
+    """n_expert must be a positive multiple of the world size: a shard of E // P experts with a
+    remainder would route the tail experts to rank P, which does not exist."""
+    with pytest.raises(ValueError):
+        expert_owner(torch.arange(10), 10, 4)
+    with pytest.raises(ValueError):
+        expert_owner(torch.arange(3), 3, 4)
+
+
+def _reject_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x = torch.zeros((2, H))
+        ids = torch.zeros((2, K), dtype=torch.int32)
+        try:
+            ep_layer(x, ids, torch.ones((2, K)), 7, lambda a, b, c: a)
+            q.put((rank, "no error"))
+        except ValueError:
+            q.put((rank, "rejected"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_layer_rejects_uneven_shards_on_gloo_ranks():
+    """Both ranks refuse 7 experts over 2 ranks before any collective runs."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_reject_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: "rejected", 1: "rejected"}

@@ -20,7 +20,7 @@ def _args(pool_s, shared_s, x, ids, w, y):
     return _lib.FfnArgs(
         C.pointer(pool_s), C.pointer(shared_s) if shared_s is not None else None, None,
         x.data_ptr(), x.stride(0), ids.data_ptr(), ids.stride(0), w.data_ptr(), w.stride(0),
-        ids.shape[1], x.shape[0], y.data_ptr(), y.stride(0), None, 0, None)
+        ids.shape[1], x.shape[0], y.data_ptr(), y.stride(0), None, 0, None, 0)
 
 
 def _within_tolerance(y, ref):
