@@ -51,6 +51,8 @@ def parse():
                     help="also time one prefill layer of this many tokens (0: skip)")
     ap.add_argument("--only-prefill", action="store_true",
                     help="time the prefill layer alone on one GPU and print its object")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     return ap.parse_args()
 
 
@@ -150,13 +152,17 @@ def run_nvmoe(a, rank, world, local_rank):
     bias = layer_log_bias(L, E, 1.1, seed=0)
     stack.prewarm(np.argsort(-bias, axis=1, kind="stable"))
 
-    # fresh routing every step: one round of logits (and tokens) per warm-up / timed step
+    # fresh routing every step: one round of logits (and tokens) per warm-up / timed step, and
+    # E2E_WARM + e2e_steps more rounds that only the end-to-end leg uses
     R = a.warmup + a.steps
+    e2e_steps = 0 if a.no_e2e else max(10, a.steps)
+    E2E_WARM = 3
+    RT = R + (E2E_WARM + e2e_steps if e2e_steps else 0)
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     bias_t = torch.from_numpy(bias).to(dev)
-    logits = torch.randn((R, L, B, E), generator=g, device=dev) + bias_t[None, :, None, :]
-    xs = torch.randn((R, B, H), generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn((RT, L, B, E), generator=g, device=dev) + bias_t[None, :, None, :]
+    xs = torch.randn((RT, B, H), generator=g, device=dev).to(torch.bfloat16)
     out = torch.empty((L, B, H), dtype=torch.bfloat16, device=dev)
 
     # distinct experts per (round, layer) for the algorithmic byte count
@@ -186,6 +192,12 @@ def run_nvmoe(a, rank, world, local_rank):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    # every graph is replayed once before the timed region (a graph's first launch uploads
+    # it), then the cache goes back to its prewarmed state and the warm-up steps run
+    for gr in graphs:
+        gr.replay()
+    torch.cuda.synchronize()
+    stack.prewarm(np.argsort(-bias, axis=1, kind="stable"))
     for i in range(a.warmup):
         graphs[i].replay()
     barrier()
@@ -220,11 +232,15 @@ def run_nvmoe(a, rank, world, local_rank):
         ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
                     shared=stack.shared[l], out=yb[l], workspace=ws)
     torch.cuda.synchronize()
+    # events bracket the fused expert kernel alone (ffn_fused); the grouping launch before it
+    # (nvmoe_moe_ffn_prepare) sits outside them
     with torch.cuda.graph(ffn_graph, stream=cap_stream):
         for l in range(L):
+            ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
+                        shared=stack.shared[l], out=yb[l], workspace=ws, phase="prepare")
             evs[l][0].record()
             ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
-                        shared=stack.shared[l], out=yb[l], workspace=ws)
+                        shared=stack.shared[l], out=yb[l], workspace=ws, phase="execute")
             evs[l][1].record()
     Ulast = np.array([len(np.unique(plans[l].slot_ids.cpu().numpy())) for l in range(L)])
     ffn_ms, reps = 0.0, 5
@@ -236,36 +252,40 @@ def run_nvmoe(a, rank, world, local_rank):
     ffn_bytes = reps * float(((Ulast + 1) * stack.bytes_per_expert).sum() +
                              L * (2 * B * H * 2 + B * k * 8))
 
-    # e2e through the public API with host buffers: H2D tokens + logits, D2H outputs per step
-    xh = xs.cpu().pin_memory()
-    lh = logits.cpu().pin_memory()
-    yh = torch.empty((L, B, H), dtype=torch.bfloat16).pin_memory()
-    xin = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
-    lin = torch.empty((L, B, E), dtype=torch.float32, device=dev)
-    gr_e2e = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gr_e2e, stream=cap_stream):
-        stack.forward(xin, lin, out)
-    torch.cuda.synchronize()
-    e2e_steps = min(R, max(10, a.steps))
-    for i in range(3):
-        xin.copy_(xh[i], non_blocking=True); lin.copy_(lh[i], non_blocking=True)
-        gr_e2e.replay(); yh.copy_(out, non_blocking=True)
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(e2e_steps):
-        xin.copy_(xh[i], non_blocking=True)
-        lin.copy_(lh[i], non_blocking=True)
-        gr_e2e.replay()
-        yh.copy_(out, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    if world > 1:
-        tt = torch.tensor([e2e_ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+    # e2e through the public API with host buffers: H2D tokens + logits, D2H outputs per step,
+    # on routing rounds no earlier step has seen
+    e2e_ms = None
+    if e2e_steps:
+        xh = xs[R:].cpu().pin_memory()
+        lh = logits[R:].cpu().pin_memory()
+        yh = torch.empty((L, B, H), dtype=torch.bfloat16).pin_memory()
+        xin = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+        lin = torch.empty((L, B, E), dtype=torch.float32, device=dev)
+        gr_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr_e2e, stream=cap_stream):
+            stack.forward(xin, lin, out)
+        torch.cuda.synchronize()
+        for i in range(E2E_WARM):
+            xin.copy_(xh[i], non_blocking=True)
+            lin.copy_(lh[i], non_blocking=True)
+            gr_e2e.replay()
+            yh.copy_(out, non_blocking=True)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(E2E_WARM, E2E_WARM + e2e_steps):
+            xin.copy_(xh[i], non_blocking=True)
+            lin.copy_(lh[i], non_blocking=True)
+            gr_e2e.replay()
+            yh.copy_(out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        if world > 1:
+            tt = torch.tensor([e2e_ms], device=dev)
+            torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+            e2e_ms = float(tt.item())
 
     peaks = load_peaks()
     hbm_peak = peaks["hbm_gbs"] if peaks else 6650.0
@@ -277,17 +297,18 @@ def run_nvmoe(a, rank, world, local_rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4/f16",
         "data": "synthetic (seeded; random-init NVFP4 expert weights)",
         "config": config_dict(a, world),
-        "e2e": {"value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
-                "h2d_bytes_per_step": B * H * 2 + L * B * E * 4,
-                "d2h_bytes_per_step": L * B * H * 2},
+        "e2e": None if e2e_ms is None else {
+            "value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
+            "h2d_bytes_per_step": B * H * 2 + L * B * E * 4,
+            "d2h_bytes_per_step": L * B * H * 2},
         # per layer step: decode_front_kernel + ffn_fused (misses are copied in by the FFN)
         "gpu_launches": a.steps * L * 2,
-        "roofline": {"bound": "hbm", "kernel": "expert FFN (prep + ffn_fused, one layer)",
+        "roofline": {"bound": "hbm", "kernel": "ffn_fused (the fused expert kernel of one layer)",
                      "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else
                      "fallback 6650 GB/s",
-                     "traffic": _traffic_from_profiles(),
+                     "traffic": _traffic_from_profiles(B),
                      "bytes_per_launch": round(ffn_bytes / n_ffn),
                      "avg_launch_us": round(1e3 * ffn_ms / n_ffn, 3)},
         "breakdown": {"layer_step_us": round(1e3 * ms_step / L, 3),
@@ -354,12 +375,15 @@ def run_prefill(a, dev, peaks):
     return out
 
 
-def _traffic_from_profiles():
-    p = ROOT / "profiles" / "ffn_fused_nvfp4_decode_b8.md"
+def _traffic_from_profiles(batch):
+    """DRAM bytes per ffn_fused launch (dram__bytes_read.sum + dram__bytes_write.sum) from the
+    ncu capture of this bench's roofline launches, kept with its command in the profile summary
+    profiles/ffn_fused_nvfp4_decode_b<batch>.txt (None when no capture exists for this batch)."""
+    p = ROOT / "profiles" / f"ffn_fused_nvfp4_decode_b{batch}.txt"
     if not p.exists():
         return None
     for ln in p.read_text().splitlines():
-        if ln.startswith("traffic_bytes_per_launch:"):
+        if ln.startswith("dram_bytes_per_launch:"):
             try:
                 return float(ln.split(":", 1)[1].strip())
             except ValueError:
@@ -462,7 +486,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     line = run_nvmoe(a, rank, world, local_rank)
-    if rank == 0:
+    if rank == 0 and not a.no_cpu:
         v, cores, desc = cpu_oracle_sample(a.batch, a.cpu_baseline_seconds)
         line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": cores,
                                 "kind": "port", "sample": desc}

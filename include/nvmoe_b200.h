@@ -207,6 +207,13 @@ typedef struct nvmoe_ffn_args {
 
 size_t nvmoe_moe_ffn_workspace_size(int n_tok, int top_k, int hidden, int inter, int n_slots);
 int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
+/* nvmoe_moe_ffn in its two launches, for callers that schedule (or time) them apart:
+ * _prepare groups the routed entries by slot into the workspace (token rows, group records);
+ * _execute runs the fused expert kernel on that workspace.  Same args for both, in that order
+ * on one stream, with nothing in between that writes the workspace.  An addition of this library
+ * (the reference's _expert_gemm is one opaque call). */
+int nvmoe_moe_ffn_prepare(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
+int nvmoe_moe_ffn_execute(const nvmoe_ffn_args* args, nvmoe_stream_t stream);
 
 /* Which kernel nvmoe_moe_ffn takes for these arguments (no launch): NVMOE_FFN_PATH_MMA
  * (in-register dequantisation feeding mma.sync; the default) or NVMOE_FFN_PATH_FP4 (block-scaled

@@ -184,6 +184,8 @@ SIGNATURES = {
     "nvmoe_set_iq2xxs_grid": (C.c_int, [C.c_void_p]),
     "nvmoe_moe_ffn_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     "nvmoe_moe_ffn": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
+    "nvmoe_moe_ffn_prepare": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
+    "nvmoe_moe_ffn_execute": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
     "nvmoe_moe_ffn_path": (C.c_int, [C.POINTER(FfnArgs)]),
     "nvmoe_moe_ffn_noalloc": (C.c_int, [C.POINTER(FfnArgs), C.c_void_p]),
     "nvmoe_moe_ffn_prefill_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int,

@@ -929,6 +929,24 @@ extern "C" int nvmoe_moe_ffn_path(const nvmoe_ffn_args* args) {
     return P.use_fp4 ? NVMOE_FFN_PATH_FP4 : NVMOE_FFN_PATH_MMA;
 }
 
+extern "C" int nvmoe_moe_ffn_prepare(const nvmoe_ffn_args* args, nvmoe_stream_t stream) {
+    using namespace nvmoe;
+    FfnParams P;
+    const int rc = ffn_setup(args, P);
+    if (rc != NVMOE_OK) return rc;
+    if (args->n_tok == 0) return NVMOE_OK;
+    return ffn_launch_prep(P, (cudaStream_t)stream);
+}
+
+extern "C" int nvmoe_moe_ffn_execute(const nvmoe_ffn_args* args, nvmoe_stream_t stream) {
+    using namespace nvmoe;
+    FfnParams P;
+    const int rc = ffn_setup(args, P);
+    if (rc != NVMOE_OK) return rc;
+    if (args->n_tok == 0) return NVMOE_OK;
+    return ffn_launch_main(P, (cudaStream_t)stream);
+}
+
 extern "C" int nvmoe_moe_ffn(const nvmoe_ffn_args* args, nvmoe_stream_t stream) {
     using namespace nvmoe;
     FfnParams P;

@@ -35,6 +35,13 @@ def _pin(w: ExpertWeights) -> ExpertWeights:
     return ExpertWeights(w.quant, w.hidden, w.inter, pm(w.gate_up), pm(w.down))
 
 
+def safe_ubatch(cache_size: int, top_k: int) -> int:
+    """Largest micro-batch whose distinct routed experts always fit the slot pool, as the
+    llama.cpp engine clamps n_ubatch (scripts/moe_cache_probe.cpp:1668-1684):
+    min(6, max(1, (cache_size - 4) // top_k))."""
+    return min(6, max(1, (cache_size - 4) // top_k))
+
+
 @dataclass
 class StackConfig:
     n_layers: int = 48
@@ -47,6 +54,10 @@ class StackConfig:
     shared_expert: bool = True
     router: str = "softmax"
     pinned_k: int = 0
+    # tokens per layer call: a batch larger than this runs as consecutive micro-batches, each
+    # through every layer, like llama.cpp's n_ubatch (0: the whole batch in one call; the
+    # reference's clamp is safe_ubatch(cache_size, top_k))
+    ubatch: int = 0
 
 
 class MoEStack:
@@ -133,9 +144,17 @@ class MoEStack:
                               device=self.device)
         return self.plans(x.shape[0])[l](x, logits, out)
 
+    def ubatches(self, n_tok: int) -> list[tuple[int, int]]:
+        """[start, end) token ranges of the micro-batches a batch of n_tok runs as."""
+        u = self.cfg.ubatch if self.cfg.ubatch > 0 else n_tok
+        return [(a, min(a + u, n_tok)) for a in range(0, n_tok, u)]
+
     def forward(self, x: torch.Tensor, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """All layers on the same token batch: logits [L, n, E], out [L, n, H]."""
-        plans = self.plans(x.shape[0])
-        for l in range(self.cfg.n_layers):
-            plans[l](x, logits[l], out[l])
+        """All layers on the same token batch: logits [L, n, E], out [L, n, H].  With
+        cfg.ubatch set, each micro-batch runs through every layer before the next one starts
+        (the order llama.cpp decodes a batch split into ubatches)."""
+        for a, b in self.ubatches(x.shape[0]):
+            plans = self.plans(b - a)
+            for l in range(self.cfg.n_layers):
+                plans[l](x[a:b], logits[l, a:b], out[l, a:b])
         return out

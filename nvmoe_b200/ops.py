@@ -278,8 +278,11 @@ def ffn_path(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor,
 def moe_ffn(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor, weights: torch.Tensor,
             shared: ExpertWeights | None = None, shared_gate: torch.Tensor | None = None,
             out: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,
-            status: torch.Tensor | None = None, kernel: str | None = None) -> torch.Tensor:
-    """y = routed-expert FFN over the slot pool (bf16 [n, H]); see nvmoe_moe_ffn."""
+            status: torch.Tensor | None = None, kernel: str | None = None,
+            phase: str = "both") -> torch.Tensor:
+    """y = routed-expert FFN over the slot pool (bf16 [n, H]); see nvmoe_moe_ffn.  phase
+    "prepare" / "execute" launches one half (nvmoe_moe_ffn_prepare / _execute), "both" the
+    whole call."""
     _require_cuda(x, slot_ids, weights)
     assert x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
     assert slot_ids.dtype == torch.int32 and weights.dtype == torch.float32
@@ -301,7 +304,9 @@ def moe_ffn(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor, weight
         _ptr(shared_gate), x.data_ptr(), x.stride(0), slot_ids.data_ptr(), slot_ids.stride(0),
         weights.data_ptr(), weights.stride(0), k, n, out.data_ptr(), out.stride(0),
         ws.data_ptr(), ws.numel(), _ptr(status), kernel_choice(kernel, "NVMOE_FFN_KERNEL"))
-    check(lib().nvmoe_moe_ffn(C.byref(args), _stream()), "nvmoe_moe_ffn")
+    fn = {"both": "nvmoe_moe_ffn", "prepare": "nvmoe_moe_ffn_prepare",
+          "execute": "nvmoe_moe_ffn_execute"}[phase]
+    check(getattr(lib(), fn)(C.byref(args), _stream()), fn)
     return out
 
 

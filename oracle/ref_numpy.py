@@ -91,6 +91,24 @@ def dequant_nvfp4(codes: np.ndarray, scales: np.ndarray, global_scale=None) -> n
     return out
 
 
+def dequant_nvfp4_torch(codes, scales, global_scale=None):
+    """dequant_nvfp4 restated in torch CPU tensor ops (vectorised and multi-threaded), for the
+    parity tests at full layer sizes (512 experts x 1.5 M values).  Same values and the same
+    operation order, (e2m1 * e4m3) * global in fp32; a CPU test holds it to dequant_nvfp4 bit
+    for bit.  Returns a float32 torch tensor."""
+    import torch
+    c = torch.as_tensor(codes, dtype=torch.uint8)
+    tab = torch.from_numpy(_E2M1)
+    lo = tab[(c & 0xF).long()]
+    hi = tab[(c >> 4).long()]
+    vals = torch.stack([lo, hi], dim=-1).reshape(*c.shape[:-1], c.shape[-1] * 2)
+    sc = torch.as_tensor(scales, dtype=torch.uint8).contiguous().view(torch.float8_e4m3fn)
+    out = vals * sc.float().repeat_interleave(16, dim=-1)
+    if global_scale is not None:
+        out = out * torch.tensor(np.float32(global_scale))
+    return out
+
+
 def dequant_q2_k(blocks: np.ndarray) -> np.ndarray:
     """ggml block_q2_K (84 B / 256 values): y = (d*sc)*q - (dmin*m), fp32 with a rounding after
     every operation, value e -> qs[32*(e//128) + e%32] >> 2*((e%128)//32)."""

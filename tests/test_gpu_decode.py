@@ -163,9 +163,16 @@ def test_decode_layers_back_to_back_equal_serialised(cuda_device):
 @pytest.mark.parametrize("n_tok", [1, 32])
 def test_decode_layer_cpu_plumbing_bf16(cuda_device, n_tok):
     """The CPU-plumbing layer (64 experts, top-4, H 1024, I 256, bf16 weights ~N(0, 0.02), a
-    16-slot LRU pool, Zipf(1.1) routing) through nvmoe_decode_layer against the oracle chain."""
+    16-slot LRU pool, Zipf(1.1) routing) through the engine against the oracle chain.  The
+    engine clamps the micro-batch as the llama.cpp engine does (moe_cache_probe.cpp:1668-1684):
+    min(6, (16 - 4) // 4) = 3 tokens, so batch 32 runs as 11 micro-batches, each one remap call
+    whose distinct experts fit the 16 slots; every step is checked (outputs of every token, and
+    the slot tables after the step)."""
+    from nvmoe_b200.engine import safe_ubatch
+    ub = safe_ubatch(16, 4)
+    assert ub == 3
     cfg = StackConfig(n_layers=1, n_experts=64, top_k=4, hidden=1024, inter=256, cache_size=16,
-                      quant="bf16", shared_expert=False)
+                      quant="bf16", shared_expert=False, ubatch=ub)
     stack = MoEStack(cfg, device=cuda_device, seed=11)
     orc = OracleLayer(64, 16)
     bias = layer_log_bias(1, 64, 1.1, seed=0)[0]
@@ -177,25 +184,24 @@ def test_decode_layer_cpu_plumbing_bf16(cuda_device, n_tok):
         return R.bf16_to_f32(m.data[e, rows].contiguous().view(torch.int16).numpy().view(np.uint16))
 
     rng = np.random.default_rng(n_tok)
-    checked = 0
+    out = torch.empty((1, n_tok, 1024), dtype=torch.bfloat16, device=cuda_device)
     for step in range(6):
         lg = router_logits(n_tok, bias, rng)
         x = torch.from_numpy(rng.standard_normal((n_tok, 1024)).astype(np.float32)).to(torch.bfloat16)
-        y = stack.layer_step(0, x.to(cuda_device), torch.from_numpy(lg).to(cuda_device))
-        plan = stack.plans(n_tok)[0]
+        stack.forward(x.to(cuda_device), torch.from_numpy(lg).to(cuda_device)[None], out)
         torch.cuda.synchronize()
         rids, rw = R.router_topk_softmax(lg, 4)
-        ref = orc.eval(rids.reshape(-1), is_decode=True)
-        if ref["status"] != 0:  # more distinct experts than the 16 slots at this batch
-            assert int(plan.status.item()) == ref["status"]
-            continue
+        for a, b in stack.ubatches(n_tok):
+            ref = orc.eval(rids[a:b].reshape(-1), is_decode=True)
+            assert ref["status"] == 0  # the clamp keeps every micro-batch within the pool
+        plan = stack.plans(stack.ubatches(n_tok)[-1][1] - stack.ubatches(n_tok)[-1][0])[0]
         assert int(plan.status.item()) == 0
-        np.testing.assert_array_equal(plan.slot_ids.cpu().numpy().reshape(-1), ref["slots"])
+        sor, ris, lu, st = orc.tables()
+        np.testing.assert_array_equal(stack.tables[0].slot_of_real.cpu().numpy(), sor)
+        np.testing.assert_array_equal(stack.tables[0].real_in_slot.cpu().numpy(), ris)
+        np.testing.assert_array_equal(stack.tables[0].last_used.cpu().numpy().view(np.uint32), lu)
         yr = R.moe_ffn(x.view(torch.int16).numpy().view(np.uint16), rids, rw,
                        lambda e: dense("gate", e), lambda e: dense("up", e),
                        lambda e: dense("down", e))
         scale = float(np.abs(yr).max())
-        assert np.abs(y.float().cpu().numpy() - yr).max() <= 1e-2 * scale
-        checked += 1
-    if n_tok == 1:
-        assert checked == 6  # (at batch 32 the 16 slots overflow, as the reference's would)
+        assert np.abs(out[0].float().cpu().numpy() - yr).max() <= 1e-2 * scale

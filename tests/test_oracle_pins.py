@@ -114,3 +114,18 @@ def test_reference_cpp_slru_replays_reference_python_traces():
         pytest.skip("oracle/_ref not built (reference tree absent)")
     for tr in json.loads((GOLD / "slru_traces.json").read_text()):
         _replay(native.RefSlru(tr["ratio"]), tr["ops"])
+
+
+def test_torch_nvfp4_dequant_equals_numpy_restatement():
+    """The vectorised torch restatement used at full layer sizes gives the numpy restatement's
+    values bit for bit (all codes, all E4M3 scale bytes incl. subnormals, a non-trivial global)."""
+    rng = np.random.default_rng(123)
+    codes = rng.integers(0, 256, size=(37, 64), dtype=np.uint8)
+    scales = rng.integers(0, 256, size=(37, 8), dtype=np.uint8)
+    scales[0, :] = np.arange(8, dtype=np.uint8)  # subnormals and zero
+    a = R.dequant_nvfp4(codes, scales, np.float32(0.3125))
+    b = R.dequant_nvfp4_torch(codes, scales, np.float32(0.3125)).numpy()
+    assert a.shape == b.shape
+    nan = np.isnan(a)
+    np.testing.assert_array_equal(nan, np.isnan(b))  # scale bytes 0x7F / 0xFF (NaN payloads vary)
+    np.testing.assert_array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
