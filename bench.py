@@ -8,10 +8,12 @@ Workload (one "step" = one decode batch through a stack of MoE layers):
   128 slots per layer prewarmed with each layer's most frequent experts; 48 layers with
   distinct slot pools (10.9 GB of pools: inputs larger than L2 between steps); misses refill
   from a pinned host tier holding all 512 experts (shared by the layers' pools).
-  Per layer: router top-k -> slot remap (LRU, miss list) -> fused FFN (gate/up SwiGLU, down,
-  weighted combine, shared expert) that also copies the misses in from pinned host memory.
-  Every layer reads the same token batch; layers are independent (no norm / attention between
-  them), so a layer's routing and remap overlap the previous layer's FFN.
+  Layers depend on each other (the headline): per layer the residual add, RMSNorm and router
+  gate GEMV (bf16 gate [512, 2048], logit bias ln p of Zipf(1.1)) -> router top-k -> slot
+  remap (LRU, miss list) -> fused FFN (gate/up SwiGLU, down, weighted combine, shared expert)
+  that also copies the misses in from pinned host memory; attention is omitted.
+  Reported beside it ("independent_layers"): every layer routes precomputed N(0,1) + ln p
+  logits of the same tokens, so a layer's routing and remap overlap the previous layer's FFN.
 
 metric: layer tokens/s = batch * layers / step time (device CUDA events, max over ranks).
 N > 1: independent replicas (one stack per GPU, own batch): weak scaling, no collective on the
@@ -59,7 +61,8 @@ def parse():
 def config_dict(a, world):
     return {
         "workload": f"Qwen3.8-shaped NVFP4 MoE layer decode, batch {a.batch}, {a.layers}-layer "
-                    "stack, 512 experts top-10 + shared, H2048 I512, 128 slots/layer",
+                    "stack of dependent layers (residual + RMSNorm + router gate in front of "
+                    "each), 512 experts top-10 + shared, H2048 I512, 128 slots/layer",
         "model": "Qwen3.8-Flash-Next MoE layer (synthetic NVFP4)",
         "global_batch": a.batch * world,
         "seq_len": 1,
@@ -67,7 +70,8 @@ def config_dict(a, world):
         "experts": 512, "top_k": 10, "hidden": 2048, "inter": 512, "slots_per_layer": 128,
         "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
         "l2": "inputs larger than L2 (10.9 GB of distinct per-layer slot pools)",
-        "routing": "softmax top-10 of N(0,1) + ln Zipf(1.1), seed 0",
+        "routing": "softmax top-10 of the gate logits (RMS-normalised tokens x N(0, 1/H) gate "
+                   "rows, about N(0,1)) + ln Zipf(1.1), seed 0",
     }
 
 
@@ -150,10 +154,13 @@ def run_nvmoe(a, rank, world, local_rank):
     E, k, H, I, S = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.inter, cfg.cache_size
     stack = MoEStack(cfg, device=dev, seed=0)
     bias = layer_log_bias(L, E, 1.1, seed=0)
-    stack.prewarm(np.argsort(-bias, axis=1, kind="stable"))
+    ranking = np.argsort(-bias, axis=1, kind="stable")
+    stack.prewarm(ranking)
+    # dependent layers: the routing skew enters as the gate's logit bias ln p (Zipf 1.1)
+    stack.init_router(logit_bias=bias, seed=5)
 
-    # fresh routing every step: one round of logits (and tokens) per warm-up / timed step, and
-    # E2E_WARM + e2e_steps more rounds that only the end-to-end leg uses
+    # fresh tokens (and, for the independent stack, fresh logits) every step; the last
+    # E2E_WARM + e2e_steps rounds are only seen by the end-to-end leg
     R = a.warmup + a.steps
     e2e_steps = 0 if a.no_e2e else max(10, a.steps)
     E2E_WARM = 3
@@ -161,88 +168,99 @@ def run_nvmoe(a, rank, world, local_rank):
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     bias_t = torch.from_numpy(bias).to(dev)
-    logits = torch.randn((RT, L, B, E), generator=g, device=dev) + bias_t[None, :, None, :]
+    logits = torch.randn((R, L, B, E), generator=g, device=dev) + bias_t[None, :, None, :]
     xs = torch.randn((RT, B, H), generator=g, device=dev).to(torch.bfloat16)
     out = torch.empty((L, B, H), dtype=torch.bfloat16, device=dev)
-
-    # distinct experts per (round, layer) for the algorithmic byte count
-    U = np.zeros((R, L), np.int64)
-    for r in range(R):
-        ids, _ = ops.router_topk(logits[r].reshape(L * B, E), k)
-        ids = ids.view(L, B * k).cpu().numpy()
-        for l in range(L):
-            U[r, l] = len(np.unique(ids[l]))
-
-    # one captured graph per round: L x nvmoe_decode_layer (router + remap + FFN with refill)
-    plans = stack.plans(B)
+    hout = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
     cap_stream = torch.cuda.Stream(dev)
-    stack.forward(xs[0], logits[0], out)  # eager pass: attributes, allocations
-    torch.cuda.synchronize()
-    stack.prewarm(np.argsort(-bias, axis=1, kind="stable"))
-    graphs = []
-    for r in range(R):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=cap_stream):
-            stack.forward(xs[r], logits[r], out)
-        graphs.append(gr)
-    torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    # every graph is replayed once before the timed region (a graph's first launch uploads
-    # it), then the cache goes back to its prewarmed state and the warm-up steps run
-    for gr in graphs:
-        gr.replay()
-    torch.cuda.synchronize()
-    stack.prewarm(np.argsort(-bias, axis=1, kind="stable"))
-    for i in range(a.warmup):
-        graphs[i].replay()
-    barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
+    def distinct(plans):
+        return np.array([len(np.unique(p.slot_ids.cpu().numpy())) for p in plans])
+
+    def timed(step, plans, clocks: bool):
+        """Captures one graph per round, replays every graph once (the first launch of a
+        graph uploads it) recording the distinct experts each layer step routes, puts the
+        cache back in its prewarmed state, runs the warm-up rounds and times the rest."""
+        step(0)  # eager pass: kernel attributes, allocations
+        torch.cuda.synchronize()
+        stack.prewarm(ranking)
+        graphs = []
+        for r in range(R):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=cap_stream):
+                step(r)
+            graphs.append(gr)
+        torch.cuda.synchronize()
+        U = np.zeros((R, L), np.int64)
+        for r, gr in enumerate(graphs):
+            gr.replay()
+            U[r] = distinct(plans)  # the same routing the timed replay of round r sees
+        stack.prewarm(ranking)
+        for i in range(a.warmup):
+            graphs[i].replay()
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(local_rank) if clocks else None
+        if clk:
+            clk.__enter__()
         t0.record()
         for i in range(a.steps):
             graphs[a.warmup + i].replay()
         t1.record()
         torch.cuda.synchronize()
-    barrier()
-    elapsed = t0.elapsed_time(t1)
-    misses_last = int(stack.misses.counts[1].item())
-    if world > 1:
-        tt = torch.tensor([elapsed], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        elapsed = float(tt.item())
-    clocks = clk.summary()
-    ms_step = elapsed / a.steps
-    value = B * L * world / (ms_step / 1e3)
+        if clk:
+            clk.__exit__(None, None, None)
+        barrier()
+        el = t0.elapsed_time(t1)
+        if world > 1:
+            tt = torch.tensor([el], device=dev)
+            torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+            el = float(tt.item())
+        del graphs
+        return el / a.steps, U, (clk.summary() if clk else None)
 
-    # roofline kernel: the expert FFN (nvmoe_moe_ffn: prep + gate_up + down) of every layer
-    # on the slot ids of the final step, timed per launch with CUDA events
+    # headline: layers that depend on each other (residual + RMSNorm + router gate GEMV in
+    # front of every layer's routing): per layer nvmoe_router_gate + nvmoe_decode_layer
+    chain = stack.chain_buffers(B)
+    ms_chain, U_chain, clocks = timed(lambda r: stack.forward_chain(xs[r], hout), chain["plans"],
+                                      clocks=True)
+    misses_last = int(stack.misses.counts[1].item())
+    # beside it: independent layers (every layer routes precomputed logits of the same tokens,
+    # so a layer's routing overlaps the previous layer's FFN)
+    plans = stack.plans(B)
+    ms_ind, U_ind, _ = timed(lambda r: stack.forward(xs[r], logits[r], out), plans, clocks=False)
+    value = B * L * world / (ms_chain / 1e3)
+
+    # roofline kernel: ffn_fused of every layer on the slot ids of the final dependent step,
+    # timed per launch with CUDA events
     ffn_graph = torch.cuda.CUDAGraph()
     evs = [(torch.cuda.Event(enable_timing=True, external=True),
             torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
     ws = ops.FfnWorkspace(dev)
     yb = torch.empty((L, B, H), dtype=torch.bfloat16, device=dev)
-    xr = xs[R - 1]
+    cp = chain["plans"]
+    xr = chain["xn"]
     for l in range(L):  # eager once (attributes)
-        ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
+        ops.moe_ffn(stack.pools[l], xr[l], cp[l].slot_ids, cp[l].weights,
                     shared=stack.shared[l], out=yb[l], workspace=ws)
     torch.cuda.synchronize()
     # events bracket the fused expert kernel alone (ffn_fused); the grouping launch before it
     # (nvmoe_moe_ffn_prepare) sits outside them
     with torch.cuda.graph(ffn_graph, stream=cap_stream):
         for l in range(L):
-            ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
+            ops.moe_ffn(stack.pools[l], xr[l], cp[l].slot_ids, cp[l].weights,
                         shared=stack.shared[l], out=yb[l], workspace=ws, phase="prepare")
             evs[l][0].record()
-            ops.moe_ffn(stack.pools[l], xr, plans[l].slot_ids, plans[l].weights,
+            ops.moe_ffn(stack.pools[l], xr[l], cp[l].slot_ids, cp[l].weights,
                         shared=stack.shared[l], out=yb[l], workspace=ws, phase="execute")
             evs[l][1].record()
-    Ulast = np.array([len(np.unique(plans[l].slot_ids.cpu().numpy())) for l in range(L)])
+    Ulast = distinct(cp)
     ffn_ms, reps = 0.0, 5
     for _ in range(reps):
         ffn_graph.replay()
@@ -251,34 +269,31 @@ def run_nvmoe(a, rank, world, local_rank):
     n_ffn = reps * L
     ffn_bytes = reps * float(((Ulast + 1) * stack.bytes_per_expert).sum() +
                              L * (2 * B * H * 2 + B * k * 8))
+    del ffn_graph
 
-    # e2e through the public API with host buffers: H2D tokens + logits, D2H outputs per step,
-    # on routing rounds no earlier step has seen
+    # e2e through the public API (MoEStack.forward_chain) with host buffers: per step the H2D
+    # copy of the step's tokens and the D2H read of the stack's output, on fresh tokens
     e2e_ms = None
     if e2e_steps:
         xh = xs[R:].cpu().pin_memory()
-        lh = logits[R:].cpu().pin_memory()
-        yh = torch.empty((L, B, H), dtype=torch.bfloat16).pin_memory()
+        yh = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
         xin = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
-        lin = torch.empty((L, B, E), dtype=torch.float32, device=dev)
         gr_e2e = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr_e2e, stream=cap_stream):
-            stack.forward(xin, lin, out)
+            stack.forward_chain(xin, hout)
         torch.cuda.synchronize()
         for i in range(E2E_WARM):
             xin.copy_(xh[i], non_blocking=True)
-            lin.copy_(lh[i], non_blocking=True)
             gr_e2e.replay()
-            yh.copy_(out, non_blocking=True)
+            yh.copy_(hout, non_blocking=True)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
         for i in range(E2E_WARM, E2E_WARM + e2e_steps):
             xin.copy_(xh[i], non_blocking=True)
-            lin.copy_(lh[i], non_blocking=True)
             gr_e2e.replay()
-            yh.copy_(out, non_blocking=True)
+            yh.copy_(hout, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
@@ -286,23 +301,24 @@ def run_nvmoe(a, rank, world, local_rank):
             tt = torch.tensor([e2e_ms], device=dev)
             torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
             e2e_ms = float(tt.item())
+        del gr_e2e
 
     peaks = load_peaks()
     hbm_peak = peaks["hbm_gbs"] if peaks else 6650.0
     achieved = (ffn_bytes / n_ffn) / ((ffn_ms / n_ffn) / 1e3) / 1e9
-    step_bytes = float(((U[a.warmup:] + 1) * stack.bytes_per_expert).sum()) / a.steps
+    step_bytes = float(((U_chain[a.warmup:] + 1) * stack.bytes_per_expert).sum()) / a.steps
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 4),
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_chain, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4/f16",
-        "data": "synthetic (seeded; random-init NVFP4 expert weights)",
+        "data": "synthetic (seeded; random-init NVFP4 expert weights and bf16 router gates)",
         "config": config_dict(a, world),
         "e2e": None if e2e_ms is None else {
             "value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
-            "h2d_bytes_per_step": B * H * 2 + L * B * E * 4,
-            "d2h_bytes_per_step": L * B * H * 2},
-        # per layer step: decode_front_kernel + ffn_fused (misses are copied in by the FFN)
-        "gpu_launches": a.steps * L * 2,
+            "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
+        # per layer step: router gate + decode_front_kernel + ffn_fused (misses are copied in
+        # by the FFN), plus the final residual add
+        "gpu_launches": a.steps * (3 * L + 1),
         "roofline": {"bound": "hbm", "kernel": "ffn_fused (the fused expert kernel of one layer)",
                      "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
@@ -311,10 +327,17 @@ def run_nvmoe(a, rank, world, local_rank):
                      "traffic": _traffic_from_profiles(B),
                      "bytes_per_launch": round(ffn_bytes / n_ffn),
                      "avg_launch_us": round(1e3 * ffn_ms / n_ffn, 3)},
-        "breakdown": {"layer_step_us": round(1e3 * ms_step / L, 3),
-                      "layer_step_hbm_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
-                      "distinct_experts_per_layer": round(float(U.mean()), 2),
+        "breakdown": {"layer_step_us": round(1e3 * ms_chain / L, 3),
+                      "layer_step_hbm_gbs": round(step_bytes / (ms_chain / 1e3) / 1e9, 1),
+                      "distinct_experts_per_layer": round(float(U_chain.mean()), 2),
                       "misses_last_layer_step": misses_last},
+        "independent_layers": {
+            "value": round(B * L * world / (ms_ind / 1e3), 1), "unit": UNIT,
+            "ms_per_step": round(ms_ind, 4), "layer_step_us": round(1e3 * ms_ind / L, 3),
+            "distinct_experts_per_layer": round(float(U_ind.mean()), 2),
+            "gpu_launches": a.steps * 2 * L,
+            "what": "same stack and tokens, every layer routing precomputed N(0,1) + ln Zipf "
+                    "logits: no gate GEMV, and a layer's routing overlaps the previous FFN"},
         "clocks": clocks,
     }
     if a.prefill_tokens > 0:

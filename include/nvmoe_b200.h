@@ -83,6 +83,41 @@ int nvmoe_router_topk(const float* logits, int64_t logits_row_stride, int n_tok,
                       int32_t* out_ids, int64_t ids_row_stride, float* out_weights,
                       int64_t weights_row_stride, nvmoe_stream_t stream);
 
+/* ================================================================ in front of R1: router gate
+ * The steps in front of the router top-k in a decoder stack, in one launch: the residual add
+ * and RMSNorm of the decoder layer and the MoE block's router gate (Qwen4ExpMoE.forward's
+ * gate.forward(hidden), nvme-moe-bench/nvme_offload_cache.py:2114).  Per token t:
+ *   h[t]      = bf16(resid[t] + delta[t])                    (delta NULL: h = resid)
+ *   x[t]      = bf16(gamma * bf16(h * 1/sqrt(mean(h^2) + eps)))   (norm_weight NULL: x = h)
+ *   logits[t] = x[t] . gate_weight^T (+ logit_bias)          (fp32 accumulation)
+ * resid_out (h) and x_out (x) may be NULL; neither may overlap resid or delta.  gate_weight NULL:
+ * only h / x are produced.  H is 1024, 2048 or 4096; rows 16-byte aligned.  As the launch after
+ * a decode layer step it waits for that step (programmatic dependent launch) and loads its gate
+ * rows while the step finishes; pass nvmoe_decode_args.inputs_after_wait = 1 to the step after
+ * it. */
+typedef struct nvmoe_router_gate_args {
+    const uint16_t* resid; /* bf16 [n_tok, H]                                  */
+    int64_t resid_row_stride;
+    const uint16_t* delta; /* bf16 [n_tok, H] added to resid, may be NULL      */
+    int64_t delta_row_stride;
+    uint16_t* resid_out;   /* bf16 [n_tok, H] h, may be NULL                   */
+    int64_t resid_out_row_stride;
+    const uint16_t* norm_weight; /* bf16 [H] RMSNorm gamma, may be NULL          */
+    float eps;
+    uint16_t* x_out;       /* bf16 [n_tok, H] x, may be NULL                   */
+    int64_t x_out_row_stride;
+    const uint16_t* gate_weight; /* bf16 [n_expert, H] router gate, may be NULL  */
+    int64_t gate_row_stride;     /* elements                                     */
+    const float* logit_bias;     /* fp32 [n_expert] added to the logits, may be NULL */
+    float* logits;         /* fp32 [n_tok, n_expert]                           */
+    int64_t logits_row_stride;
+    int32_t n_tok;
+    int32_t hidden;
+    int32_t n_expert;
+} nvmoe_router_gate_args;
+
+int nvmoe_router_gate(const nvmoe_router_gate_args* args, nvmoe_stream_t stream);
+
 /* ================================================================ R2/R3/R6: slot remap
  * Device-resident slot tables of one slot pool (one layer in the llama.cpp engine:
  * layer_cache.slot_of_real / real_in_slot / slot_last_used / current_step,
@@ -340,6 +375,10 @@ typedef struct nvmoe_decode_args {
      * two sets), so the step's front kernel writes them while that step's FFN still runs.
      * 0: they are written after it (always correct). */
     int32_t early_outputs;
+    /* 1: the logits and token rows are written by the launch just before this call on the
+     * stream (nvmoe_router_gate, in a stack whose layers depend on each other), so the step
+     * reads them only after waiting for that launch; 0: they were complete before it began. */
+    int32_t inputs_after_wait;
 } nvmoe_decode_args;
 
 int nvmoe_decode_layer(const nvmoe_decode_args* args, nvmoe_stream_t stream);

@@ -165,6 +165,30 @@ class DecodeArgs(C.Structure):
         ("host_slot_of_id", C.c_void_p),
         ("ffn", FfnArgs),
         ("early_outputs", C.c_int32),
+        ("inputs_after_wait", C.c_int32),
+    ]
+
+
+class RouterGateArgs(C.Structure):
+    _fields_ = [
+        ("resid", C.c_void_p),
+        ("resid_row_stride", C.c_int64),
+        ("delta", C.c_void_p),
+        ("delta_row_stride", C.c_int64),
+        ("resid_out", C.c_void_p),
+        ("resid_out_row_stride", C.c_int64),
+        ("norm_weight", C.c_void_p),
+        ("eps", C.c_float),
+        ("x_out", C.c_void_p),
+        ("x_out_row_stride", C.c_int64),
+        ("gate_weight", C.c_void_p),
+        ("gate_row_stride", C.c_int64),
+        ("logit_bias", C.c_void_p),
+        ("logits", C.c_void_p),
+        ("logits_row_stride", C.c_int64),
+        ("n_tok", C.c_int32),
+        ("hidden", C.c_int32),
+        ("n_expert", C.c_int32),
     ]
 
 
@@ -208,6 +232,7 @@ SIGNATURES = {
     "nvmoe_refill_gather": (C.c_int, [C.POINTER(RefillBank), C.c_int, C.POINTER(MissList),
                                       C.c_void_p, C.c_int32, C.c_void_p]),
     "nvmoe_decode_layer": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
+    "nvmoe_router_gate": (C.c_int, [C.POINTER(RouterGateArgs), C.c_void_p]),
 }
 
 _lock = threading.Lock()

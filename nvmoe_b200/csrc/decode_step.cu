@@ -35,6 +35,7 @@ struct FrontParams {
     float* weights;
     FfnParams fp;
     int early;  // the workspace and miss list are not the previous step's: written before the wait
+    int inputs_after_wait;  // the logits / token rows come from the kernel before this one
 };
 
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
@@ -180,6 +181,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         s_err = NVMOE_OK;
         s_step = (int)(*F.rp.t.current_step + 1u);
     }
+    // in a stack whose layers depend on each other the logits are the router gate's output
+    if (F.inputs_after_wait) grid_dep_wait();
     for (int t = warp; t < n_tok; t += nw)
         router_topk_warp(F.logits + (int64_t)t * F.lstride, E, K, F.mode, F.bias, F.norm_topk,
                          F.scaling, sids + t * K, sw + t * K);
@@ -480,6 +483,7 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
     F.rp.is_decode = a->is_decode;
     F.rp.m = m;
     F.early = a->early_outputs ? 1 : 0;
+    F.inputs_after_wait = a->inputs_after_wait ? 1 : 0;
 
     if (n > kFrontMaxIds || t.cache_size > kFrontMaxSlots) return NVMOE_ERR_UNSUPPORTED;
     if (F.fp.pool.n_slots < t.cache_size) return NVMOE_ERR_INVALID_ARG;

@@ -1,0 +1,206 @@
+// In front of the router top-k in a decoder stack: residual add, RMSNorm and the router gate
+// GEMV of one MoE layer, in one launch (nvmoe_router_gate).
+//
+// Reference: Qwen4ExpMoE.forward runs gate.forward(hidden) on the normalised hidden state
+// (nvme-moe-bench/nvme_offload_cache.py:2114) to produce the router logits that the cache hook's
+// top-k and slot remap consume; the decoder layer in front of it adds the residual and applies
+// RMSNorm.  FreeToken (which holds those modules) is not in the reference tree; the arithmetic
+// here is the usual decoder-layer form:
+//   h      = bf16(resid + delta)                                  (fp32 add, one rounding)
+//   x      = bf16(gamma * bf16(h * (1 / sqrt(mean(h^2) + eps))))  (RMSNorm, fp32 statistics)
+//   logits = x . W_gate^T (+ logit_bias)                          (fp32 accumulation)
+//
+// Layout: CTA b owns gate rows [b*epc, (b+1)*epc) held in shared memory (loaded before the
+// dependency wait: the weights are constant, so their load overlaps the previous kernel's tail);
+// each warp normalises whole token rows in registers (no block barrier inside the token loop)
+// and dots them with the CTA's gate rows.  Every CTA normalises every token (cheap: the rows
+// come from L2); CTA 0 alone stores h and x.  HBM traffic is the gate matrix once.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace nvmoe {
+namespace {
+
+constexpr int kGateThreads = 256;
+constexpr int kGateWarps = kGateThreads / 32;
+
+struct GateParams {
+    nvmoe_router_gate_args a;
+    int epc;  // gate rows per CTA
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// NCH = H / 256: a lane holds 8 values of each 256-wide chunk (16 bytes of bf16).
+template <int NCH>
+__global__ void __launch_bounds__(kGateThreads) router_gate_kernel(GateParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const nvmoe_router_gate_args& a = p.a;
+    const int H = NCH * 256;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e0 = blockIdx.x * p.epc;
+    const int ne = a.gate_weight ? min(p.epc, a.n_expert - e0) : 0;
+    uint4* wrow = reinterpret_cast<uint4*>(smem);  // [ne][H / 8]
+    const int vpr = H / 8;
+    for (int i = threadIdx.x; i < ne * vpr; i += kGateThreads) {
+        const int r = i / vpr, c = i - r * vpr;
+        cp_async16(wrow + i, a.gate_weight + (int64_t)(e0 + r) * a.gate_row_stride + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    grid_dep_launch();
+    grid_dep_wait();  // the residual / delta rows come from the kernel before this one
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+
+    const bool writer = blockIdx.x == 0;
+    for (int t = warp; t < a.n_tok; t += kGateWarps) {
+        const uint16_t* rr = a.resid + (int64_t)t * a.resid_row_stride;
+        const uint16_t* dr = a.delta ? a.delta + (int64_t)t * a.delta_row_stride : nullptr;
+        uint32_t hv[NCH][4];
+        uint4 rv[NCH], dv[NCH];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            rv[c] = *reinterpret_cast<const uint4*>(rr + c * 256 + lane * 8);
+            dv[c] = dr ? *reinterpret_cast<const uint4*>(dr + c * 256 + lane * 8)
+                       : make_uint4(0, 0, 0, 0);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const uint32_t* r4 = reinterpret_cast<const uint32_t*>(&rv[c]);
+            const uint32_t* d4 = reinterpret_cast<const uint32_t*>(&dv[c]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (dr) {
+                    const float lo = __fadd_rn(bf16_lo(r4[q]), bf16_lo(d4[q]));
+                    const float hi = __fadd_rn(bf16_hi(r4[q]), bf16_hi(d4[q]));
+                    hv[c][q] = pack_bf16x2(lo, hi);
+                } else {
+                    hv[c][q] = r4[q];  // h = resid as given (keeps -0)
+                }
+                const float l2 = bf16_lo(hv[c][q]), h2 = bf16_hi(hv[c][q]);
+                ss = __fmaf_rn(l2, l2, ss);
+                ss = __fmaf_rn(h2, h2, ss);
+            }
+        }
+        if (writer && a.resid_out) {
+            uint16_t* o = a.resid_out + (int64_t)t * a.resid_out_row_stride;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+                *reinterpret_cast<uint4*>(o + c * 256 + lane * 8) =
+                    make_uint4(hv[c][0], hv[c][1], hv[c][2], hv[c][3]);
+        }
+        if (a.norm_weight) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), a.eps)));
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                const uint4 gv = *reinterpret_cast<const uint4*>(a.norm_weight + c * 256 + lane * 8);
+                const uint32_t* g4 = reinterpret_cast<const uint32_t*>(&gv);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t n = pack_bf16x2(__fmul_rn(bf16_lo(hv[c][q]), inv),
+                                                   __fmul_rn(bf16_hi(hv[c][q]), inv));
+                    hv[c][q] = pack_bf16x2(__fmul_rn(bf16_lo(g4[q]), bf16_lo(n)),
+                                           __fmul_rn(bf16_hi(g4[q]), bf16_hi(n)));
+                }
+            }
+        }
+        if (writer && a.x_out) {
+            uint16_t* o = a.x_out + (int64_t)t * a.x_out_row_stride;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+                *reinterpret_cast<uint4*>(o + c * 256 + lane * 8) =
+                    make_uint4(hv[c][0], hv[c][1], hv[c][2], hv[c][3]);
+        }
+        for (int r = 0; r < ne; ++r) {
+            float acc = 0.f;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                const uint4 wv = wrow[r * vpr + c * 32 + lane];
+                const uint32_t* w4 = reinterpret_cast<const uint32_t*>(&wv);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    acc = __fmaf_rn(bf16_lo(hv[c][q]), bf16_lo(w4[q]), acc);
+                    acc = __fmaf_rn(bf16_hi(hv[c][q]), bf16_hi(w4[q]), acc);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) {
+                const int e = e0 + r;
+                a.logits[(int64_t)t * a.logits_row_stride + e] =
+                    a.logit_bias ? __fadd_rn(acc, a.logit_bias[e]) : acc;
+            }
+        }
+    }
+}
+
+template <int NCH>
+int launch_gate(const GateParams& p, int grid, size_t smem, cudaStream_t st) {
+    if (smem > 48 * 1024)
+        NVMOE_CUDA_TRY(cudaFuncSetAttribute(router_gate_kernel<NCH>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const cudaError_t e =
+        launch_pdl(router_gate_kernel<NCH>, dim3(grid), dim3(kGateThreads), smem, st, true, p);
+    return cuda_status("router_gate launch", e);
+}
+
+bool overlaps(const void* a, int64_t a_bytes, const void* b, int64_t b_bytes) {
+    if (!a || !b) return false;
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + (uintptr_t)b_bytes && y < x + (uintptr_t)a_bytes;
+}
+
+bool rows_ok(const void* p, int64_t stride) {
+    return !p || ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && stride % 8 == 0);
+}
+
+}  // namespace
+}  // namespace nvmoe
+
+extern "C" int nvmoe_router_gate(const nvmoe_router_gate_args* a, nvmoe_stream_t stream) {
+    using namespace nvmoe;
+    if (!a || !a->resid || a->n_tok < 0) return NVMOE_ERR_INVALID_ARG;
+    const int H = a->hidden;
+    if (H != 1024 && H != 2048 && H != 4096) return NVMOE_ERR_UNSUPPORTED;
+    if (a->gate_weight && (!a->logits || a->n_expert <= 0)) return NVMOE_ERR_INVALID_ARG;
+    if (!rows_ok(a->resid, a->resid_row_stride) || !rows_ok(a->delta, a->delta_row_stride) ||
+        !rows_ok(a->resid_out, a->resid_out_row_stride) ||
+        !rows_ok(a->x_out, a->x_out_row_stride) || !rows_ok(a->gate_weight, a->gate_row_stride) ||
+        !rows_ok(a->norm_weight, 0))
+        return NVMOE_ERR_INVALID_ARG;
+    if (a->n_tok == 0) return NVMOE_OK;
+    // every CTA reads resid / delta while CTA 0 writes resid_out and x_out: no overlap allowed
+    const int64_t rb = ((int64_t)(a->n_tok - 1) * std::max<int64_t>(a->resid_row_stride, 0) + H) * 2;
+    const int64_t db = ((int64_t)(a->n_tok - 1) * std::max<int64_t>(a->delta_row_stride, 0) + H) * 2;
+    const int64_t ob = ((int64_t)(a->n_tok - 1) * std::max<int64_t>(a->resid_out_row_stride, 0) + H) * 2;
+    const int64_t xb = ((int64_t)(a->n_tok - 1) * std::max<int64_t>(a->x_out_row_stride, 0) + H) * 2;
+    for (const auto& w : {std::make_pair((const void*)a->resid_out, ob),
+                          std::make_pair((const void*)a->x_out, xb)})
+        if (overlaps(w.first, w.second, a->resid, rb) || overlaps(w.first, w.second, a->delta, db))
+            return NVMOE_ERR_INVALID_ARG;
+    GateParams p;
+    p.a = *a;
+    // gate rows per CTA: more rows per CTA at larger batches (every CTA normalises every token)
+    p.epc = a->n_tok <= 8 ? 4 : a->n_tok <= 32 ? 8 : 16;
+    const int grid = a->gate_weight ? (a->n_expert + p.epc - 1) / p.epc : 1;
+    const size_t smem = a->gate_weight ? (size_t)p.epc * H * 2 : 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (H / 256) {
+        case 4: return launch_gate<4>(p, grid, smem, st);
+        case 8: return launch_gate<8>(p, grid, smem, st);
+        default: return launch_gate<16>(p, grid, smem, st);
+    }
+}

@@ -10,12 +10,14 @@ materialised layout, nvme_offload_cache.py:1626-1682), so the miss list alone de
 """
 from __future__ import annotations
 
+import ctypes as C
+import math
 from dataclasses import dataclass
 
 import numpy as np
 import torch
 
-from . import ops
+from . import _lib, ops
 from .formats import ExpertWeights, QuantMatrix, random_experts
 
 
@@ -92,6 +94,9 @@ class MoEStack:
         self.banks = [ops.refill_banks(p, self.host) for p in self.pools]
         self.ws_sets = [ops.FfnWorkspace(d) for _ in range(2)]
         self._plans: dict[int, list] = {}
+        self._chain: dict[int, dict] = {}
+        self.gate_w = self.norm_w = self.logit_bias = None
+        self.eps = 1e-6
 
     @property
     def bytes_per_expert(self) -> int:
@@ -143,6 +148,86 @@ class MoEStack:
             out = torch.empty((x.shape[0], self.cfg.hidden), dtype=torch.bfloat16,
                               device=self.device)
         return self.plans(x.shape[0])[l](x, logits, out)
+
+    # ---------------------------------------------------------------- dependent layers
+    def init_router(self, logit_bias: np.ndarray | None = None, seed: int = 0,
+                    eps: float = 1e-6) -> None:
+        """Per-layer router gates for forward_chain: gate weights [L, E, H] bf16 ~ N(0, 1/H)
+        (unit-variance logits on RMS-normalised tokens), RMSNorm gammas [L, H] bf16
+        ~ 1 + N(0, 0.1), and an optional fp32 logit bias [L, E] (the synthetic routing skew,
+        ln p of a Zipf law)."""
+        c = self.cfg
+        g = torch.Generator().manual_seed(seed)
+        self.gate_w = (torch.randn((c.n_layers, c.n_experts, c.hidden), generator=g) /
+                       math.sqrt(c.hidden)).to(torch.bfloat16).to(self.device)
+        self.norm_w = (1.0 + 0.1 * torch.randn((c.n_layers, c.hidden), generator=g)).to(
+            torch.bfloat16).to(self.device)
+        self.logit_bias = (None if logit_bias is None else
+                           torch.from_numpy(np.ascontiguousarray(logit_bias, np.float32)).to(
+                               self.device))
+        self.eps = eps
+        self._chain.clear()
+
+    def chain_buffers(self, n_tok: int) -> dict:
+        """Device buffers and prebuilt C arguments of forward_chain for batches of n_tok: per
+        layer the residual h (h[l] enters layer l, l >= 1), the normalised tokens xn, the
+        logits and the MoE output y."""
+        if self.gate_w is None:
+            raise RuntimeError("forward_chain needs init_router() first")
+        if n_tok in self._chain:
+            return self._chain[n_tok]
+        c, d = self.cfg, self.device
+        L, H, E = c.n_layers, c.hidden, c.n_experts
+        b = {"h": torch.empty((L, n_tok, H), dtype=torch.bfloat16, device=d),
+             "xn": torch.empty((L, n_tok, H), dtype=torch.bfloat16, device=d),
+             "logits": torch.empty((L, n_tok, E), dtype=torch.float32, device=d),
+             "y": torch.empty((L, n_tok, H), dtype=torch.bfloat16, device=d)}
+        b["plans"] = [
+            ops.DecodeLayerPlan(self.pools[l], self.tables[l], self.misses_sets[l % 2], n_tok,
+                                c.top_k, shared=self.shared[l], refill=self.banks[l],
+                                host_slot_of_id=self.host_slot_of_id,
+                                workspace=self.ws_sets[l % 2], router=c.router,
+                                device=d, early_outputs=False, inputs_after_wait=True)
+            for l in range(L)]
+        gates = []
+        for l in range(L):
+            # layers 0 and 1 read the caller's x (patched per call)
+            resid = b["h"][l - 1] if l >= 2 else b["xn"][0]
+            gates.append(ops.router_gate_args(
+                resid, b["logits"][l], self.gate_w[l],
+                delta=b["y"][l - 1] if l >= 1 else None,
+                resid_out=b["h"][l] if l >= 1 else None, norm_weight=self.norm_w[l],
+                eps=self.eps, x_out=b["xn"][l],
+                logit_bias=None if self.logit_bias is None else self.logit_bias[l]))
+        b["gates"] = gates
+        self._chain[n_tok] = b
+        return b
+
+    def forward_chain(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """L MoE layers whose inputs depend on each other, on tokens x [n, H] bf16:
+            h_0 = x;  per layer l: h_l = h_{l-1} + y_{l-1} (l >= 1), xn_l = RMSNorm_l(h_l),
+            logits_l = xn_l . gate_l^T + bias_l, y_l = MoE_l(xn_l) (router top-k, slot remap,
+            refill, expert FFN, shared expert);  out = h_{L-1} + y_{L-1}.
+        Per layer two calls: nvmoe_router_gate, then nvmoe_decode_layer, which waits for it."""
+        n = x.shape[0]
+        b = self.chain_buffers(n)
+        L = self.cfg.n_layers
+        lib = _lib.lib()
+        s = ops._stream()
+        for l in range(L):
+            ga = b["gates"][l]
+            if l == 0:
+                ga.resid, ga.resid_row_stride = x.data_ptr(), x.stride(0)
+            elif l == 1:
+                ga.resid, ga.resid_row_stride = x.data_ptr(), x.stride(0)
+            else:
+                ga.resid = b["h"][l - 1].data_ptr()
+            _lib.check(lib.nvmoe_router_gate(C.byref(ga), s), "nvmoe_router_gate")
+            b["plans"][l](b["xn"][l], b["logits"][l], b["y"][l])
+        fin = ops.router_gate_args(x if L == 1 else b["h"][L - 1], None, None,
+                                   delta=b["y"][L - 1], resid_out=out)
+        _lib.check(lib.nvmoe_router_gate(C.byref(fin), s), "nvmoe_router_gate")
+        return out
 
     def ubatches(self, n_tok: int) -> list[tuple[int, int]]:
         """[start, end) token ranges of the micro-batches a batch of n_tok runs as."""

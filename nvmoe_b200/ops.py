@@ -71,6 +71,49 @@ def router_topk(logits: torch.Tensor, top_k: int, mode: str = "softmax",
     return ids, w
 
 
+# ------------------------------------------------------------------ router gate (in front of R1)
+def router_gate_args(resid: torch.Tensor, logits: torch.Tensor | None,
+                     gate_weight: torch.Tensor | None, delta: torch.Tensor | None = None,
+                     resid_out: torch.Tensor | None = None,
+                     norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                     x_out: torch.Tensor | None = None,
+                     logit_bias: torch.Tensor | None = None) -> _lib.RouterGateArgs:
+    """C arguments of nvmoe_router_gate over these tensors (bf16 rows, fp32 logits)."""
+    _require_cuda(resid, logits, gate_weight, delta, resid_out, norm_weight, x_out, logit_bias)
+    n, H = resid.shape
+    for t in (resid, delta, resid_out, x_out, gate_weight):
+        if t is not None:
+            assert t.dtype == torch.bfloat16 and t.stride(-1) == 1
+    E = 0 if gate_weight is None else gate_weight.shape[0]
+    return _lib.RouterGateArgs(
+        resid.data_ptr(), resid.stride(0), _ptr(delta), 0 if delta is None else delta.stride(0),
+        _ptr(resid_out), 0 if resid_out is None else resid_out.stride(0), _ptr(norm_weight),
+        float(eps), _ptr(x_out), 0 if x_out is None else x_out.stride(0), _ptr(gate_weight),
+        0 if gate_weight is None else gate_weight.stride(0), _ptr(logit_bias), _ptr(logits),
+        0 if logits is None else logits.stride(0), n, H, E)
+
+
+def router_gate(resid: torch.Tensor, gate_weight: torch.Tensor | None,
+                delta: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
+                eps: float = 1e-6, logit_bias: torch.Tensor | None = None,
+                resid_out: torch.Tensor | None = None, x_out: torch.Tensor | None = None,
+                logits: torch.Tensor | None = None):
+    """Residual add + RMSNorm + router gate GEMV (nvmoe_router_gate): returns (h, x, logits)
+    for bf16 token rows resid [n, H] (+ delta), gate_weight bf16 [E, H]."""
+    n, H = resid.shape
+    dev = resid.device
+    if resid_out is None:
+        resid_out = torch.empty((n, H), dtype=torch.bfloat16, device=dev)
+    if x_out is None:
+        x_out = torch.empty((n, H), dtype=torch.bfloat16, device=dev)
+    if logits is None and gate_weight is not None:
+        logits = torch.empty((n, gate_weight.shape[0]), dtype=torch.float32, device=dev)
+    a = router_gate_args(resid, logits, gate_weight, delta, resid_out, norm_weight, eps, x_out,
+                         logit_bias)
+    check(lib().nvmoe_router_gate(C.byref(a), _stream()), "nvmoe_router_gate")
+    return resid_out, x_out, logits
+
+
 # ------------------------------------------------------------------ R2/R3/R6 remap
 @dataclass
 class SlotTableGPU:
@@ -389,7 +432,8 @@ class DecodeLayerPlan:
                  host_slot_of_id: torch.Tensor | None = None, workspace: FfnWorkspace | None = None,
                  router: str = "softmax", router_bias: torch.Tensor | None = None,
                  norm_topk: bool = True, routed_scaling: float = 1.0, device="cuda",
-                 early_outputs: bool = False, kernel: str | None = None):
+                 early_outputs: bool = False, kernel: str | None = None,
+                 inputs_after_wait: bool = False):
         self.n_tok, self.top_k = n_tok, top_k
         self.pool_s = expert_pool_struct(pool)
         self.shared_s = expert_pool_struct(shared) if shared is not None else None
@@ -426,6 +470,7 @@ class DecodeLayerPlan:
         a.ffn.kernel = kernel_choice(kernel, "NVMOE_FFN_KERNEL")
         # the caller alternates workspace / miss-list sets between consecutive steps
         a.early_outputs = int(bool(early_outputs))
+        a.inputs_after_wait = int(bool(inputs_after_wait))
         self.args = a
 
     def __call__(self, x: torch.Tensor, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

@@ -202,3 +202,37 @@ def moe_ffn(x_bf16: np.ndarray, slot_ids: np.ndarray, weights: np.ndarray, gate_
             out = out * (np.float32(1) / (np.float32(1) + np.exp(-gv)))[:, None]
         y += out
     return y
+
+
+# ---------------------------------------------------------------- in front of R1: router gate
+def residual_add_bf16(a_bits: np.ndarray, b_bits: np.ndarray | None) -> np.ndarray:
+    """h = bf16(a + b) for bf16 rows (fp32 add, one round-to-nearest-even): the decoder layer's
+    residual add in front of the MoE block."""
+    a = bf16_to_f32(a_bits)
+    if b_bits is None:
+        return np.asarray(a_bits, np.uint16)
+    return f32_to_bf16((a + bf16_to_f32(b_bits)).astype(np.float32))
+
+
+def rmsnorm_bf16(h_bits: np.ndarray, gamma_bits: np.ndarray | None, eps: float) -> np.ndarray:
+    """x = bf16(gamma * bf16(h * (1 / sqrt(mean(h^2) + eps)))) per row, fp32 statistics (the
+    RMSNorm of the decoder layer whose output feeds Qwen4ExpMoE.forward's gate.forward,
+    nvme-moe-bench/nvme_offload_cache.py:2114); gamma None: x = h."""
+    if gamma_bits is None:
+        return np.asarray(h_bits, np.uint16)
+    h = bf16_to_f32(h_bits)
+    H = h.shape[-1]
+    var = (np.sum(h.astype(np.float64) ** 2, axis=-1) / H).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt((var + np.float32(eps)).astype(np.float32))).astype(np.float32)
+    n = f32_to_bf16((h * inv[..., None]).astype(np.float32))
+    return f32_to_bf16((bf16_to_f32(gamma_bits) * bf16_to_f32(n)).astype(np.float32))
+
+
+def router_gate_logits(x_bits: np.ndarray, w_bits: np.ndarray,
+                       bias: np.ndarray | None = None) -> np.ndarray:
+    """logits = x . W^T (+ bias): the MoE block's router gate (gate.forward,
+    nvme_offload_cache.py:2114), accumulated in float64 and returned as fp32."""
+    lg = bf16_to_f32(x_bits).astype(np.float64) @ bf16_to_f32(w_bits).astype(np.float64).T
+    if bias is not None:
+        lg = lg + np.asarray(bias, np.float64)
+    return lg.astype(np.float32)
