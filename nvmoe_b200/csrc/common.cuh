@@ -170,6 +170,38 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
     return res;
 }
 
+// The same scan over 64-bit values (several small counters packed in bit fields whose sums
+// stay inside their fields are scanned at once).  warp_sums: 33 shared entries.
+__device__ __forceinline__ unsigned long long block_exclusive_scan_u64(
+    unsigned long long v, unsigned long long* warp_sums, unsigned long long* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = (blockDim.x + 31) >> 5;
+    unsigned long long inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += n;
+    }
+    if (lane == 31) warp_sums[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const unsigned long long s = lane < nwarps ? warp_sums[lane] : 0ull;
+        unsigned long long si = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long n = __shfl_up_sync(0xffffffffu, si, o);
+            if (lane >= o) si += n;
+        }
+        warp_sums[lane] = si - s;
+        if (lane == 31) warp_sums[32] = si;
+    }
+    __syncthreads();
+    const unsigned long long res = warp_sums[warp] + inc - v;
+    *total = warp_sums[32];
+    __syncthreads();
+    return res;
+}
+
 #endif  // __CUDACC__
 
 }  // namespace nvmoe

@@ -94,24 +94,36 @@ __host__ __device__ inline FrontSmem front_smem(int E, int S, int n, int n_ent) 
     return L;
 }
 
-// Token rows -> f16 and the shared-expert gate, one warp per token (no block barrier).
+// Token rows -> f16 and the shared-expert gate, one warp per token (no block barrier).  The
+// row's loads are issued in batches of 8 x 16 bytes per lane before any of them is used.
 __device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, int lane) {
     const int H = P.pool.hidden;
     const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
     __half* x16 = wsp<__half>(P, P.L.x16) + (int64_t)t * H;
     float dot = 0.f, amax = 0.f;
-    for (int i = lane * 8; i < H; i += 256) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
-        const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
-        __align__(16) __half o[8];
+    constexpr int kBatch = 8;
+    for (int i0 = lane * 8; i0 < H; i0 += 256 * kBatch) {
+        uint4 v[kBatch];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float f = bf16_bits_to_f32(e[k]);
-            o[k] = __float2half_rn(f);
-            amax = fmaxf(amax, fabsf(f));
-            if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
+        for (int b = 0; b < kBatch; ++b) {
+            const int i = i0 + b * 256;
+            v[b] = i < H ? *reinterpret_cast<const uint4*>(xr + i) : make_uint4(0, 0, 0, 0);
         }
-        if (!P.use_fp4) *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int i = i0 + b * 256;
+            if (i >= H) break;
+            const uint16_t* e = reinterpret_cast<const uint16_t*>(&v[b]);
+            __align__(16) __half o[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float f = bf16_bits_to_f32(e[k]);
+                o[k] = __float2half_rn(f);
+                amax = fmaxf(amax, fabsf(f));
+                if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
+            }
+            if (!P.use_fp4) *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+        }
     }
     if (P.use_fp4) {  // the row's FP4 term exponent
 #pragma unroll
@@ -132,6 +144,7 @@ __device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, i
 __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontParams F) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int warp_sums[33];
+    __shared__ unsigned long long warp_sums64[33];
     __shared__ int s_err, s_step;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nthr = blockDim.x, nw = nthr >> 5;
@@ -305,31 +318,47 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     for (int p = tid; p < n; p += nthr) atomicAdd(&cnt[sids[p]], 1);
     __syncthreads();
     const int ngs = P.has_shared ? (n_tok + P.grp_tok - 1) / P.grp_tok : 0;
-    int n_act = 0, n_ent = 0, n_grp = 0, g_shared = 0;
-    for (int cls = 0; cls < 2; ++cls) {
-        if (cls == 1) {
-            g_shared = n_grp;
-            n_grp += ngs;
+    // Entry, group and active-slot offsets of every slot (hit slots first, then the shared
+    // expert's groups, then the slots refilled in this step), with two packed scans:
+    // f: entries / groups of hit slots in bits 0-15 / 16-31, of missed slots in 32-47 / 48-63;
+    // a: active hit / missed slots in bits 0-31 / 32-63 (every total is at most n <= 2048).
+    // Slots past the first nthr keep their within-class rank in act / gbase / aidx until the
+    // class totals are known.
+    unsigned long long run_f = 0, run_a = 0;
+    for (int base = 0; base < S; base += nthr) {
+        const int s = base + tid;
+        const int c = s < S ? cnt[s] : 0;
+        const bool miss = s < S && missof[s] >= 0;
+        const unsigned long long ng = (unsigned long long)((c + P.grp_tok - 1) / P.grp_tok);
+        const int sh = miss ? 32 : 0;
+        const unsigned long long f = ((unsigned long long)c | (ng << 16)) << sh;
+        const unsigned long long av = (c > 0 ? 1ull : 0ull) << sh;
+        unsigned long long tf, ta;
+        const unsigned long long xf = block_exclusive_scan_u64(f, warp_sums64, &tf) + run_f;
+        const unsigned long long xa = block_exclusive_scan_u64(av, warp_sums64, &ta) + run_a;
+        run_f += tf;
+        run_a += ta;
+        if (s < S) {
+            act[s] = c > 0 ? (int)((xf >> sh) & 0xffff) : -1;  // entry rank within the class
+            gbase[s] = (int)((xf >> (sh + 16)) & 0xffff);
+            aidx[s] = (int)((xa >> sh) & 0xffffffffu);
+            cnt[s] = c;
         }
-        for (int base = 0; base < S; base += nthr) {
-            const int s = base + tid;
-            const bool mine = s < S && ((missof[s] >= 0) == (cls == 1));
-            const int c = mine ? cnt[s] : 0;
-            const int ng = (c + P.grp_tok - 1) / P.grp_tok;
-            int tot_a, tot_e, tot_g;
-            const int ra = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_a);
-            const int re = block_exclusive_scan(c, warp_sums, &tot_e);
-            const int rg = block_exclusive_scan(ng, warp_sums, &tot_g);
-            if (mine) {
-                act[s] = c > 0 ? n_ent + re : -1;  // entry base of the slot
-                gbase[s] = n_grp + rg;              // first group of the slot
-                aidx[s] = n_act + ra;               // its place in the active-slot list
-                if (c > 0) cnt[s] = n_ent + re;     // scatter cursor
-            }
-            n_act += tot_a;
-            n_ent += tot_e;
-            n_grp += tot_g;
+    }
+    const int ent_hit = (int)(run_f & 0xffff), grp_hit = (int)((run_f >> 16) & 0xffff);
+    const int act_hit = (int)(run_a & 0xffffffffu);
+    const int g_shared = grp_hit;
+    int n_act = act_hit + (int)(run_a >> 32);
+    int n_ent = ent_hit + (int)((run_f >> 32) & 0xffff);
+    const int n_grp = grp_hit + ngs + (int)(run_f >> 48);
+    for (int s = tid; s < S; s += nthr) {
+        const bool miss = missof[s] >= 0;
+        if (act[s] >= 0) {
+            act[s] += miss ? ent_hit : 0;     // entry base of the slot
+            cnt[s] = act[s];                  // scatter cursor
         }
+        gbase[s] += miss ? grp_hit + ngs : 0;  // first group of the slot
+        aidx[s] += miss ? act_hit : 0;         // its place in the active-slot list
     }
     __syncthreads();
     for (int p = tid; p < n; p += nthr) {

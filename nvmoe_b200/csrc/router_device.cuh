@@ -67,6 +67,74 @@ __device__ __forceinline__ void tile_pick(uint32_t (&key)[PL], int k, int& my_e,
     }
 }
 
+// The same picks as tile_pick, by threshold: T = the k-th largest of the 32 lanes' tile maxima
+// is a lower bound of the k-th largest key of the row (those k maxima are k distinct keys), so
+// the k picks are among the keys >= T.  The candidates (usually k to 2k of them) are gathered in
+// shared memory as (key, ~e) pairs and sorted in one bitonic pass across the warp, which orders
+// equal keys by ascending e as the pick loop does.  Returns false (nothing written) when there
+// are more than 32 candidates or fewer than k keys; the caller then runs tile_pick.  Uniform
+// across the warp; key is not modified.
+__device__ __forceinline__ unsigned long long* topk_candidate_buffer() {
+    __shared__ unsigned long long buf[32][32];  // one 32-entry buffer per warp of the block
+    return buf[threadIdx.x >> 5];
+}
+
+template <int PL>
+__device__ __forceinline__ bool tile_pick_threshold(const uint32_t (&key)[PL], int k, int& my_e,
+                                                    uint32_t& my_key) {
+    const int lane = threadIdx.x & 31;
+    uint32_t v = 0;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) v = max(v, key[i]);
+    // bitonic sort of the lane maxima, descending across the warp
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+        const bool desc = (lane & size) == 0;
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, v, j);
+            v = (((lane & j) == 0) == desc) ? max(v, o) : min(v, o);
+        }
+    }
+    const uint32_t T = __shfl_sync(0xffffffffu, v, k - 1);
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) m |= (key[i] >= T ? 1u : 0u) << i;
+    if (T == 0u) m = 0;
+    const int c = __popc(m);
+    const int C = (int)__reduce_add_sync(0xffffffffu, (unsigned)c);
+    if (T == 0u || C > 32) return false;
+    int inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += n;
+    }
+    unsigned long long* buf = topk_candidate_buffer();
+    int pos = inc - c;
+#pragma unroll
+    for (int i = 0; i < PL; ++i)
+        if ((m >> i) & 1u)
+            buf[pos++] = ((unsigned long long)key[i] << 32) | (0xffffffffu - (uint32_t)(i * 32 + lane));
+    __syncwarp();
+    unsigned long long x = lane < C ? buf[lane] : 0ull;
+    __syncwarp();
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+        const bool desc = (lane & size) == 0;
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, x, j);
+            x = (((lane & j) == 0) == desc) ? (x > o ? x : o) : (x < o ? x : o);
+        }
+    }
+    if (lane < k) {
+        my_key = (uint32_t)(x >> 32);
+        my_e = (int)(0xffffffffu - (uint32_t)x);
+    }
+    return true;
+}
+
 // Selection keys of n experts (the row's first n) into a PL-per-lane tile, then the top k.
 template <int PL>
 __device__ __forceinline__ void row_select(const float* __restrict__ lr, int n, int k, int mode,
@@ -92,7 +160,7 @@ __device__ __forceinline__ void row_select(const float* __restrict__ lr, int n, 
         const float c = __uint_as_float(key[i]);
         key[i] = (i * 32 + lane >= n) ? 0u : ((c != c) ? kNanKey : ordered_key(c));
     }
-    tile_pick<PL>(key, k, my_id, my_key);
+    if (!tile_pick_threshold<PL>(key, k, my_id, my_key)) tile_pick<PL>(key, k, my_id, my_key);
 }
 
 // Top-k of one token row by one warp; writes ids / weights [top_k] (called by all 32 lanes).
@@ -130,12 +198,17 @@ __device__ __forceinline__ void router_topk_warp(const float* __restrict__ lr, i
         my_id = (pe >> 5) ? 512 + b : a;
     }
 
-    // the picked values: softmax the logit, sigmoid the plain score (re-read, L1-resident)
+    // the picked values: softmax the logit (its key maps back to it, except the NaN / -inf
+    // key, which is re-read), sigmoid the plain score (re-read)
     const bool mine = lane < top_k;
     float my_val = 0.f;
     if (mine) {
-        const float l = lr[my_id];
-        my_val = (mode == NVMOE_ROUTER_SOFTMAX) ? l : 1.0f / (1.0f + expf(-l));
+        if (mode == NVMOE_ROUTER_SOFTMAX && my_key != 0x007FFFFFu) {
+            my_val = __uint_as_float((my_key & 0x80000000u) ? (my_key & 0x7fffffffu) : ~my_key);
+        } else {
+            const float l = lr[my_id];
+            my_val = (mode == NVMOE_ROUTER_SOFTMAX) ? l : 1.0f / (1.0f + expf(-l));
+        }
     }
     const float first_val = __shfl_sync(0xffffffffu, my_val, 0);
 

@@ -10,11 +10,12 @@
 //   x      = bf16(gamma * bf16(h * (1 / sqrt(mean(h^2) + eps))))  (RMSNorm, fp32 statistics)
 //   logits = x . W_gate^T (+ logit_bias)                          (fp32 accumulation)
 //
-// Layout: CTA b owns gate rows [b*epc, (b+1)*epc) held in shared memory (loaded before the
-// dependency wait: the weights are constant, so their load overlaps the previous kernel's tail);
-// each warp normalises whole token rows in registers (no block barrier inside the token loop)
-// and dots them with the CTA's gate rows.  Every CTA normalises every token (cheap: the rows
-// come from L2); CTA 0 alone stores h and x.  HBM traffic is the gate matrix once.
+// Layout: a 2-D grid of CTAs, one per (block of kGateRows gate rows, block of kGateTok tokens).
+// Each warp holds one gate row in registers, loaded before the dependency wait (the weights are
+// constant, so their load overlaps the previous kernel's tail).  After the wait the warps
+// normalise the CTA's tokens into shared memory (CTAs of the first row block also store h and
+// x), then every warp dots its row with each token.  The gate matrix is read from HBM once;
+// the token rows are re-read from L2 by each row block.
 #include "common.cuh"
 
 #include <algorithm>
@@ -22,18 +23,9 @@
 namespace nvmoe {
 namespace {
 
-constexpr int kGateThreads = 256;
-constexpr int kGateWarps = kGateThreads / 32;
-
-struct GateParams {
-    nvmoe_router_gate_args a;
-    int epc;  // gate rows per CTA
-};
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
-}
+constexpr int kGateRows = 4;   // gate rows per CTA (one per warp)
+constexpr int kGateTok = 8;    // tokens per CTA
+constexpr int kGateThreads = 32 * kGateRows;
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
@@ -41,29 +33,30 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
-// NCH = H / 256: a lane holds 8 values of each 256-wide chunk (16 bytes of bf16).
+// NCH = H / 256: a lane holds 8 values (16 bytes of bf16) of each 256-wide chunk of a row.
 template <int NCH>
-__global__ void __launch_bounds__(kGateThreads) router_gate_kernel(GateParams p) {
+__global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_gate_args a) {
     extern __shared__ __align__(16) unsigned char smem[];
-    const nvmoe_router_gate_args& a = p.a;
-    const int H = NCH * 256;
+    uint4* xs = reinterpret_cast<uint4*>(smem);  // [kGateTok][H / 8] normalised tokens
+    constexpr int H = NCH * 256;
+    constexpr int VPR = H / 8;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int e0 = blockIdx.x * p.epc;
-    const int ne = a.gate_weight ? min(p.epc, a.n_expert - e0) : 0;
-    uint4* wrow = reinterpret_cast<uint4*>(smem);  // [ne][H / 8]
-    const int vpr = H / 8;
-    for (int i = threadIdx.x; i < ne * vpr; i += kGateThreads) {
-        const int r = i / vpr, c = i - r * vpr;
-        cp_async16(wrow + i, a.gate_weight + (int64_t)(e0 + r) * a.gate_row_stride + c * 8);
+    const int e = blockIdx.x * kGateRows + warp;
+    const bool has_row = a.gate_weight && e < a.n_expert;
+    const int t0 = blockIdx.y * kGateTok;
+    const int nt = min(kGateTok, a.n_tok - t0);
+    uint4 w[NCH];
+    if (has_row) {
+        const uint16_t* wr = a.gate_weight + (int64_t)e * a.gate_row_stride;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) w[c] = ldg_stream16(wr + c * 256 + lane * 8);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
     grid_dep_launch();
     grid_dep_wait();  // the residual / delta rows come from the kernel before this one
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
 
     const bool writer = blockIdx.x == 0;
-    for (int t = warp; t < a.n_tok; t += kGateWarps) {
+    for (int i = warp; i < nt; i += kGateRows) {
+        const int t = t0 + i;
         const uint16_t* rr = a.resid + (int64_t)t * a.resid_row_stride;
         const uint16_t* dr = a.delta ? a.delta + (int64_t)t * a.delta_row_stride : nullptr;
         uint32_t hv[NCH][4];
@@ -103,7 +96,8 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(GateParams p)
         if (a.norm_weight) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), a.eps)));
+            const float inv =
+                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), a.eps)));
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
                 const uint4 gv = *reinterpret_cast<const uint4*>(a.norm_weight + c * 256 + lane * 8);
@@ -124,36 +118,42 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(GateParams p)
                 *reinterpret_cast<uint4*>(o + c * 256 + lane * 8) =
                     make_uint4(hv[c][0], hv[c][1], hv[c][2], hv[c][3]);
         }
-        for (int r = 0; r < ne; ++r) {
-            float acc = 0.f;
 #pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-                const uint4 wv = wrow[r * vpr + c * 32 + lane];
-                const uint32_t* w4 = reinterpret_cast<const uint32_t*>(&wv);
+        for (int c = 0; c < NCH; ++c)
+            xs[i * VPR + c * 32 + lane] = make_uint4(hv[c][0], hv[c][1], hv[c][2], hv[c][3]);
+    }
+    if (!a.gate_weight) return;
+    __syncthreads();
+    if (!has_row) return;
+    for (int i = 0; i < nt; ++i) {
+        float acc = 0.f;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    acc = __fmaf_rn(bf16_lo(hv[c][q]), bf16_lo(w4[q]), acc);
-                    acc = __fmaf_rn(bf16_hi(hv[c][q]), bf16_hi(w4[q]), acc);
-                }
-            }
+        for (int c = 0; c < NCH; ++c) {
+            const uint4 xv = xs[i * VPR + c * 32 + lane];
+            const uint32_t* x4 = reinterpret_cast<const uint32_t*>(&xv);
+            const uint32_t* w4 = reinterpret_cast<const uint32_t*>(&w[c]);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (lane == 0) {
-                const int e = e0 + r;
-                a.logits[(int64_t)t * a.logits_row_stride + e] =
-                    a.logit_bias ? __fadd_rn(acc, a.logit_bias[e]) : acc;
+            for (int q = 0; q < 4; ++q) {
+                acc = __fmaf_rn(bf16_lo(x4[q]), bf16_lo(w4[q]), acc);
+                acc = __fmaf_rn(bf16_hi(x4[q]), bf16_hi(w4[q]), acc);
             }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0)
+            a.logits[(int64_t)(t0 + i) * a.logits_row_stride + e] =
+                a.logit_bias ? __fadd_rn(acc, a.logit_bias[e]) : acc;
     }
 }
 
 template <int NCH>
-int launch_gate(const GateParams& p, int grid, size_t smem, cudaStream_t st) {
+int launch_gate(const nvmoe_router_gate_args& a, dim3 grid, cudaStream_t st) {
+    const size_t smem = (size_t)kGateTok * NCH * 256 * 2;
     if (smem > 48 * 1024)
         NVMOE_CUDA_TRY(cudaFuncSetAttribute(router_gate_kernel<NCH>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const cudaError_t e =
-        launch_pdl(router_gate_kernel<NCH>, dim3(grid), dim3(kGateThreads), smem, st, true, p);
+        launch_pdl(router_gate_kernel<NCH>, grid, dim3(kGateThreads), smem, st, true, a);
     return cuda_status("router_gate launch", e);
 }
 
@@ -191,16 +191,13 @@ extern "C" int nvmoe_router_gate(const nvmoe_router_gate_args* a, nvmoe_stream_t
                           std::make_pair((const void*)a->x_out, xb)})
         if (overlaps(w.first, w.second, a->resid, rb) || overlaps(w.first, w.second, a->delta, db))
             return NVMOE_ERR_INVALID_ARG;
-    GateParams p;
-    p.a = *a;
-    // gate rows per CTA: more rows per CTA at larger batches (every CTA normalises every token)
-    p.epc = a->n_tok <= 8 ? 4 : a->n_tok <= 32 ? 8 : 16;
-    const int grid = a->gate_weight ? (a->n_expert + p.epc - 1) / p.epc : 1;
-    const size_t smem = a->gate_weight ? (size_t)p.epc * H * 2 : 0;
+    const dim3 grid(a->gate_weight ? (a->n_expert + kGateRows - 1) / kGateRows : 1,
+                    (a->n_tok + kGateTok - 1) / kGateTok);
+    if (grid.y > 65535) return NVMOE_ERR_UNSUPPORTED;
     cudaStream_t st = (cudaStream_t)stream;
     switch (H / 256) {
-        case 4: return launch_gate<4>(p, grid, smem, st);
-        case 8: return launch_gate<8>(p, grid, smem, st);
-        default: return launch_gate<16>(p, grid, smem, st);
+        case 4: return launch_gate<4>(*a, grid, st);
+        case 8: return launch_gate<8>(*a, grid, st);
+        default: return launch_gate<16>(*a, grid, st);
     }
 }
