@@ -509,10 +509,11 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     line = run_nvmoe(a, rank, world, local_rank)
-    if rank == 0 and not a.no_cpu:
-        v, cores, desc = cpu_oracle_sample(a.batch, a.cpu_baseline_seconds)
-        line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": cores,
-                                "kind": "port", "sample": desc}
+    if rank == 0:
+        if not a.no_cpu:
+            v, cores, desc = cpu_oracle_sample(a.batch, a.cpu_baseline_seconds)
+            line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": cores,
+                                    "kind": "port", "sample": desc}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

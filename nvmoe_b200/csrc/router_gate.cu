@@ -10,12 +10,13 @@
 //   x      = bf16(gamma * bf16(h * (1 / sqrt(mean(h^2) + eps))))  (RMSNorm, fp32 statistics)
 //   logits = x . W_gate^T (+ logit_bias)                          (fp32 accumulation)
 //
-// Layout: a 2-D grid of CTAs, one per (block of kGateRows gate rows, block of kGateTok tokens).
-// Each warp holds one gate row in registers, loaded before the dependency wait (the weights are
-// constant, so their load overlaps the previous kernel's tail).  After the wait the warps
-// normalise the CTA's tokens into shared memory (CTAs of the first row block also store h and
-// x), then every warp dots its row with each token.  The gate matrix is read from HBM once;
-// the token rows are re-read from L2 by each row block.
+// Layout: a 2-D grid of CTAs, one per (block of kGateRows gate rows, block of kGateTok tokens),
+// 8 warps each.  Warps w and w + 4 hold gate row w of the block in registers, loaded before the
+// dependency wait (the weights are constant, so their load overlaps the previous kernel's
+// tail).  After the wait each warp normalises one token of the block into shared memory (CTAs
+// of the first row block also store h and x); then warp w dots its row with the block's tokens
+// of parity w / 4, two tokens at a time.  The gate matrix is read from HBM once; the token rows
+// are re-read from L2 by each row block.
 #include "common.cuh"
 
 #include <algorithm>
@@ -23,9 +24,10 @@
 namespace nvmoe {
 namespace {
 
-constexpr int kGateRows = 4;   // gate rows per CTA (one per warp)
-constexpr int kGateTok = 8;    // tokens per CTA
-constexpr int kGateThreads = 32 * kGateRows;
+constexpr int kGateRows = 4;   // gate rows per CTA (each held by two warps)
+constexpr int kGateTok = 8;    // tokens per CTA (one per warp in the normalisation)
+constexpr int kGateWarps = 8;
+constexpr int kGateThreads = 32 * kGateWarps;
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
@@ -41,7 +43,7 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_
     constexpr int H = NCH * 256;
     constexpr int VPR = H / 8;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int e = blockIdx.x * kGateRows + warp;
+    const int e = blockIdx.x * kGateRows + (warp & (kGateRows - 1));
     const bool has_row = a.gate_weight && e < a.n_expert;
     const int t0 = blockIdx.y * kGateTok;
     const int nt = min(kGateTok, a.n_tok - t0);
@@ -55,7 +57,7 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_
     grid_dep_wait();  // the residual / delta rows come from the kernel before this one
 
     const bool writer = blockIdx.x == 0;
-    for (int i = warp; i < nt; i += kGateRows) {
+    for (int i = warp; i < nt; i += kGateWarps) {
         const int t = t0 + i;
         const uint16_t* rr = a.resid + (int64_t)t * a.resid_row_stride;
         const uint16_t* dr = a.delta ? a.delta + (int64_t)t * a.delta_row_stride : nullptr;
@@ -67,9 +69,10 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_
             dv[c] = dr ? *reinterpret_cast<const uint4*>(dr + c * 256 + lane * 8)
                        : make_uint4(0, 0, 0, 0);
         }
-        float ss = 0.f;
+        float ssp[4] = {0.f, 0.f, 0.f, 0.f};  // four chains, summed in a fixed order below
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
+            float& ss = ssp[c & 3];
             const uint32_t* r4 = reinterpret_cast<const uint32_t*>(&rv[c]);
             const uint32_t* d4 = reinterpret_cast<const uint32_t*>(&dv[c]);
 #pragma unroll
@@ -86,6 +89,7 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_
                 ss = __fmaf_rn(h2, h2, ss);
             }
         }
+        float ss = (ssp[0] + ssp[1]) + (ssp[2] + ssp[3]);
         if (writer && a.resid_out) {
             uint16_t* o = a.resid_out + (int64_t)t * a.resid_out_row_stride;
 #pragma unroll
@@ -125,24 +129,39 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_
     if (!a.gate_weight) return;
     __syncthreads();
     if (!has_row) return;
-    for (int i = 0; i < nt; ++i) {
-        float acc = 0.f;
+    // tokens of this warp's parity, two at a time (four independent accumulation chains)
+    for (int i = warp >> 2; i < nt; i += 4) {
+        const int i2 = i + 2 < nt ? i + 2 : i;
+        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
-            const uint4 xv = xs[i * VPR + c * 32 + lane];
-            const uint32_t* x4 = reinterpret_cast<const uint32_t*>(&xv);
+            const uint4 xv0 = xs[i * VPR + c * 32 + lane];
+            const uint4 xv1 = xs[i2 * VPR + c * 32 + lane];
+            const uint32_t* x0 = reinterpret_cast<const uint32_t*>(&xv0);
+            const uint32_t* x1 = reinterpret_cast<const uint32_t*>(&xv1);
             const uint32_t* w4 = reinterpret_cast<const uint32_t*>(&w[c]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                acc = __fmaf_rn(bf16_lo(x4[q]), bf16_lo(w4[q]), acc);
-                acc = __fmaf_rn(bf16_hi(x4[q]), bf16_hi(w4[q]), acc);
+                acc[0][q & 1] = __fmaf_rn(bf16_lo(x0[q]), bf16_lo(w4[q]), acc[0][q & 1]);
+                acc[0][q & 1] = __fmaf_rn(bf16_hi(x0[q]), bf16_hi(w4[q]), acc[0][q & 1]);
+                acc[1][q & 1] = __fmaf_rn(bf16_lo(x1[q]), bf16_lo(w4[q]), acc[1][q & 1]);
+                acc[1][q & 1] = __fmaf_rn(bf16_hi(x1[q]), bf16_hi(w4[q]), acc[1][q & 1]);
             }
         }
+        float r0 = acc[0][0] + acc[0][1], r1 = acc[1][0] + acc[1][1];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0)
+        for (int o = 16; o > 0; o >>= 1) {
+            r0 += __shfl_xor_sync(0xffffffffu, r0, o);
+            r1 += __shfl_xor_sync(0xffffffffu, r1, o);
+        }
+        if (lane == 0) {
+            const float b = a.logit_bias ? a.logit_bias[e] : 0.f;
             a.logits[(int64_t)(t0 + i) * a.logits_row_stride + e] =
-                a.logit_bias ? __fadd_rn(acc, a.logit_bias[e]) : acc;
+                a.logit_bias ? __fadd_rn(r0, b) : r0;
+            if (i2 != i)
+                a.logits[(int64_t)(t0 + i2) * a.logits_row_stride + e] =
+                    a.logit_bias ? __fadd_rn(r1, b) : r1;
+        }
     }
 }
 
