@@ -217,7 +217,8 @@ enum nvmoe_kernel {
 };
 
 /* Arguments of one FFN call.  y[t] = sum_j w[t,j] * down_s( silu(gate_s x[t]) * up_s x[t] ),
- * s = slot_ids[t, j]; plus, when `shared` is set, the always-on shared expert (slot 0 of that
+ * s = slot_ids[t, j] (a negative slot id is an empty entry: it contributes nothing; ids >= n_slots
+ * are reported as NVMOE_ERR_BAD_SLOT); plus, when `shared` is set, the always-on shared expert (slot 0 of that
  * pool) with weight 1, or sigmoid(x[t] . shared_gate) when shared_gate (bf16 [H]) is set
  * (nvme_offload_cache.py:2115-2123).  fp32 accumulation, bf16 in / out. */
 typedef struct nvmoe_ffn_args {
@@ -379,9 +380,60 @@ typedef struct nvmoe_decode_args {
      * stream (nvmoe_router_gate, in a stack whose layers depend on each other), so the step
      * reads them only after waiting for that launch; 0: they were complete before it began. */
     int32_t inputs_after_wait;
+    /* Pre-routed steps (logits == NULL): the expert ids [n_tok, top_k] (a negative id is an
+     * empty entry, skipped by the remap and the FFN) and their combine weights, e.g. the pairs an
+     * expert-parallel rank receives; read after waiting for the launches before this call. */
+    const int32_t* routed_ids;
+    const float* routed_weights;
+    int64_t routed_row_stride; /* elements between rows of routed_ids / routed_weights (0: top_k) */
 } nvmoe_decode_args;
 
 int nvmoe_decode_layer(const nvmoe_decode_args* args, nvmoe_stream_t stream);
+
+/* ================================================================ expert parallelism
+ * P ranks (one per GPU); rank r owns the routed experts [r*E/P, (r+1)*E/P) under local ids
+ * e - r*E/P, and its own copy of the shared expert under local id E/P.  No counterpart in the
+ * reference (single GPU); the step is its expert GEMM split across GPUs.  One layer step:
+ *   1. nvmoe_ep_dispatch packs this rank's tokens into P send segments of n_tok rows each: a
+ *      token goes once to every rank that owns one of its experts (and to this rank for the
+ *      shared expert), in token order.  A row holds the token (bf16 [H]), then its local expert
+ *      ids on that rank (int32 [k+1]: entry j for routed pick j, -1 where pick j is elsewhere;
+ *      entry k the shared expert, on this rank only) and their weights (fp32 [k+1]: the router
+ *      weight, 1 or sigmoid(x . shared_gate) for the shared expert), padded to
+ *      nvmoe_ep_row_bytes.  Rows past a segment's count have every id -1.  slot_of[t][d] is the
+ *      row of token t in segment d (-1: not sent).
+ *   2. the caller exchanges the segments (an all-to-all of P equal parts, e.g. NCCL);
+ *   3. the owner runs the P*n_tok received rows as one pre-routed step with top_k = k + 1
+ *      (nvmoe_decode_layer with routed_ids, or nvmoe_moe_ffn_prefill on its resident pool),
+ *      one output row per received row (the weighted sum of that row's local experts);
+ *   4. the outputs go back the same way;
+ *   5. nvmoe_ep_combine: y[t] = sum over d = 0..P-1 of back[d][slot_of[t][d]], fp32, bf16 out.
+ * Every size is fixed by n_tok, so no count crosses to the host and the step can be captured
+ * in a CUDA graph. */
+size_t nvmoe_ep_row_bytes(int hidden, int top_k);
+
+typedef struct nvmoe_ep_dispatch_args {
+    const uint16_t* x;          /* bf16 [n_tok, H] home tokens                          */
+    int64_t x_row_stride;       /* elements                                             */
+    const int32_t* ids;         /* [n_tok, top_k] global expert ids (contiguous)        */
+    const float* weights;       /* [n_tok, top_k] router weights (contiguous)           */
+    const uint16_t* shared_gate;/* bf16 [H], may be NULL (shared expert weight 1)       */
+    int32_t with_shared;        /* 1: route every token to this rank's shared expert    */
+    int32_t n_tok, top_k, hidden, n_expert, world, rank;
+    unsigned char* send;        /* [world][n_tok][nvmoe_ep_row_bytes] device bytes      */
+    int32_t* slot_of;           /* [n_tok][world]                                       */
+    int32_t* status;            /* optional device int: NVMOE_ERR_BAD_EXPERT_ID          */
+} nvmoe_ep_dispatch_args;
+int nvmoe_ep_dispatch(const nvmoe_ep_dispatch_args* args, nvmoe_stream_t stream);
+
+typedef struct nvmoe_ep_combine_args {
+    const uint16_t* back;       /* bf16 [world][n_tok][H] outputs returned by the owners */
+    const int32_t* slot_of;     /* [n_tok][world] from nvmoe_ep_dispatch                 */
+    int32_t n_tok, hidden, world;
+    uint16_t* y;                /* bf16 [n_tok, H]                                      */
+    int64_t y_row_stride;
+} nvmoe_ep_combine_args;
+int nvmoe_ep_combine(const nvmoe_ep_combine_args* args, nvmoe_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

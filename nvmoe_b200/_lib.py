@@ -166,6 +166,41 @@ class DecodeArgs(C.Structure):
         ("ffn", FfnArgs),
         ("early_outputs", C.c_int32),
         ("inputs_after_wait", C.c_int32),
+        ("routed_ids", C.c_void_p),
+        ("routed_weights", C.c_void_p),
+        ("routed_row_stride", C.c_int64),
+    ]
+
+
+class EpDispatchArgs(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p),
+        ("x_row_stride", C.c_int64),
+        ("ids", C.c_void_p),
+        ("weights", C.c_void_p),
+        ("shared_gate", C.c_void_p),
+        ("with_shared", C.c_int32),
+        ("n_tok", C.c_int32),
+        ("top_k", C.c_int32),
+        ("hidden", C.c_int32),
+        ("n_expert", C.c_int32),
+        ("world", C.c_int32),
+        ("rank", C.c_int32),
+        ("send", C.c_void_p),
+        ("slot_of", C.c_void_p),
+        ("status", C.c_void_p),
+    ]
+
+
+class EpCombineArgs(C.Structure):
+    _fields_ = [
+        ("back", C.c_void_p),
+        ("slot_of", C.c_void_p),
+        ("n_tok", C.c_int32),
+        ("hidden", C.c_int32),
+        ("world", C.c_int32),
+        ("y", C.c_void_p),
+        ("y_row_stride", C.c_int64),
     ]
 
 
@@ -233,6 +268,9 @@ SIGNATURES = {
                                       C.c_void_p, C.c_int32, C.c_void_p]),
     "nvmoe_decode_layer": (C.c_int, [C.POINTER(DecodeArgs), C.c_void_p]),
     "nvmoe_router_gate": (C.c_int, [C.POINTER(RouterGateArgs), C.c_void_p]),
+    "nvmoe_ep_row_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "nvmoe_ep_dispatch": (C.c_int, [C.POINTER(EpDispatchArgs), C.c_void_p]),
+    "nvmoe_ep_combine": (C.c_int, [C.POINTER(EpCombineArgs), C.c_void_p]),
 }
 
 _lock = threading.Lock()

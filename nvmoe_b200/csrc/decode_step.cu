@@ -21,7 +21,7 @@ namespace nvmoe {
 namespace {
 
 constexpr int kFrontThreads = 512;  // at most 16 warps; 128 registers per thread for the top-k tile
-constexpr int kFrontMaxIds = 2048;  // routed (token, k) entries per call on this path
+constexpr int kFrontMaxIds = 8192;  // routed (token, k) entries per call on this path
 constexpr int kFrontMaxSlots = 1024;
 
 struct FrontParams {
@@ -36,6 +36,9 @@ struct FrontParams {
     FfnParams fp;
     int early;  // the workspace and miss list are not the previous step's: written before the wait
     int inputs_after_wait;  // the logits / token rows come from the kernel before this one
+    const int32_t* rids;    // logits == NULL: routed expert ids [n_tok, K] (< 0: empty entry)
+    const float* rw;        //                 and their combine weights [n_tok, K]
+    int64_t rstride;        //                 elements between their rows
 };
 
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
@@ -194,20 +197,29 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         s_err = NVMOE_OK;
         s_step = (int)(*F.rp.t.current_step + 1u);
     }
-    // in a stack whose layers depend on each other the logits are the router gate's output
-    if (F.inputs_after_wait) grid_dep_wait();
-    for (int t = warp; t < n_tok; t += nw)
-        router_topk_warp(F.logits + (int64_t)t * F.lstride, E, K, F.mode, F.bias, F.norm_topk,
-                         F.scaling, sids + t * K, sw + t * K);
+    // in a stack whose layers depend on each other the logits are the router gate's output;
+    // pre-routed ids / weights (no logits) always come from the launches before this one
+    if (F.inputs_after_wait || !F.logits) grid_dep_wait();
+    if (F.logits) {
+        for (int t = warp; t < n_tok; t += nw)
+            router_topk_warp(F.logits + (int64_t)t * F.lstride, E, K, F.mode, F.bias,
+                             F.norm_topk, F.scaling, sids + t * K, sw + t * K);
+    } else {
+        for (int p = tid; p < n; p += nthr) {
+            const int64_t o = (int64_t)(p / K) * F.rstride + p % K;
+            sids[p] = __ldcg(F.rids + o);
+            sw[p] = __ldcg(F.rw + o);
+        }
+    }
     cp_async_wait_all();
     __syncthreads();
 
     // ---- B. remap in shared memory; this layer's tables and the miss list are written here
     for (int p = tid; p < n; p += nthr) {
-        const int id = sids[p];
-        if (id < 0 || id >= E)
+        const int id = sids[p];  // a negative id is an empty entry (pre-routed calls)
+        if (id >= E)
             s_err = NVMOE_ERR_BAD_EXPERT_ID;
-        else
+        else if (id >= 0)
             atomicMin(&first[id], p);
     }
     __syncthreads();
@@ -215,7 +227,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     int nuniq = 0, nmiss = 0;
     const uint32_t step = (uint32_t)s_step;
     if (status == NVMOE_OK) {
-        nuniq = ordered_compact(n, warp_sums, [&](int p) { return first[sids[p]] == p; },
+        nuniq = ordered_compact(n, warp_sums,
+                                [&](int p) { return sids[p] >= 0 && first[sids[p]] == p; },
                                 [&](int p, int r) { uniq[r] = sids[p]; });
         __syncthreads();
         if (nuniq > S) status = NVMOE_ERR_CACHE_OVERFLOW;
@@ -278,7 +291,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
             F.rp.t.slot_last_used[s] = step;
         }
         for (int p = tid; p < n; p += nthr) {
-            const int sl = uslot[first[sids[p]]];
+            const int sl = sids[p] >= 0 ? uslot[first[sids[p]]] : -1;
             sids[p] = sl;
             F.rp.out[p] = sl;
             F.weights[p] = sw[p];
@@ -315,13 +328,14 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     for (int s = tid; s < S; s += nthr) missof[s] = -1;
     __syncthreads();
     for (int j = tid; j < nmiss; j += nthr) missof[uslot[miss_r[j]]] = j;
-    for (int p = tid; p < n; p += nthr) atomicAdd(&cnt[sids[p]], 1);
+    for (int p = tid; p < n; p += nthr)
+        if (sids[p] >= 0) atomicAdd(&cnt[sids[p]], 1);
     __syncthreads();
     const int ngs = P.has_shared ? (n_tok + P.grp_tok - 1) / P.grp_tok : 0;
     // Entry, group and active-slot offsets of every slot (hit slots first, then the shared
     // expert's groups, then the slots refilled in this step), with two packed scans:
     // f: entries / groups of hit slots in bits 0-15 / 16-31, of missed slots in 32-47 / 48-63;
-    // a: active hit / missed slots in bits 0-31 / 32-63 (every total is at most n <= 2048).
+    // a: active hit / missed slots in bits 0-31 / 32-63 (every total is at most n <= 8192).
     // Slots past the first nthr keep their within-class rank in act / gbase / aidx until the
     // class totals are known.
     unsigned long long run_f = 0, run_a = 0;
@@ -362,6 +376,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
     }
     __syncthreads();
     for (int p = tid; p < n; p += nthr) {
+        if (sids[p] < 0) {
+            pe[p] = -1;
+            continue;
+        }
         const int e = atomicAdd(&cnt[sids[p]], 1);
         ent_tok_s[e] = p / K;
         ent_w_s[e] = sw[p];
@@ -389,7 +407,13 @@ __global__ void __launch_bounds__(kFrontThreads, 1) decode_front_kernel(FrontPar
         write_counts();
     }
     reset_phase_counters(P);
-    for (int t = warp; t < n_tok; t += nw) front_convert_token(P, t, lane);
+    for (int t = warp; t < n_tok; t += nw) {
+        // a pre-routed token with no entry (and no shared expert) is not read by the FFN
+        bool used = F.logits != nullptr || P.has_shared;
+        for (int j = lane; j < K && !used; j += 32) used = sids[t * K + j] >= 0;
+        if (!__any_sync(0xffffffffu, used)) continue;
+        front_convert_token(P, t, lane);
+    }
     int* desc = wsp<int>(P, P.L.grp_desc);
     int* ent_of = wsp<int>(P, P.L.ent_of);
     for (int s = tid; s < S; s += nthr) {  // the routed groups' records
@@ -465,7 +489,7 @@ int ffn_setup(const nvmoe_ffn_args* args, FfnParams& P);
 
 extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t stream) {
     using namespace nvmoe;
-    if (!a || !a->logits || !a->slot_ids || !a->weights) return NVMOE_ERR_INVALID_ARG;
+    if (!a || !a->slot_ids || !a->weights) return NVMOE_ERR_INVALID_ARG;
     const nvmoe_slot_table& t = a->table;
     if (!t.slot_of_real || !t.real_in_slot || !t.slot_last_used || !t.current_step)
         return NVMOE_ERR_INVALID_ARG;
@@ -476,6 +500,7 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
         return NVMOE_ERR_INVALID_ARG;
     if (a->router_mode != NVMOE_ROUTER_SOFTMAX && a->router_mode != NVMOE_ROUTER_SIGMOID_BIAS)
         return NVMOE_ERR_INVALID_ARG;
+    if (!a->logits && (!a->routed_ids || !a->routed_weights)) return NVMOE_ERR_INVALID_ARG;
     const nvmoe_miss_list& m = a->misses;
     if (!m.unique_ids || !m.unique_slot || !m.unique_hit || !m.miss_ids || !m.miss_slots ||
         !m.evicted_ids || !m.counts)
@@ -513,6 +538,9 @@ extern "C" int nvmoe_decode_layer(const nvmoe_decode_args* a, nvmoe_stream_t str
     F.rp.m = m;
     F.early = a->early_outputs ? 1 : 0;
     F.inputs_after_wait = a->inputs_after_wait ? 1 : 0;
+    F.rids = a->routed_ids;
+    F.rw = a->routed_weights;
+    F.rstride = a->routed_row_stride > 0 ? a->routed_row_stride : a->top_k;
 
     if (n > kFrontMaxIds || t.cache_size > kFrontMaxSlots) return NVMOE_ERR_UNSUPPORTED;
     if (F.fp.pool.n_slots < t.cache_size) return NVMOE_ERR_INVALID_ARG;

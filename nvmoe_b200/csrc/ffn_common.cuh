@@ -290,8 +290,8 @@ __device__ inline void ffn_group_block(const FfnParams& P, int* smem_i) {
         const int s = P.ids[(int64_t)t * P.ids_stride + j];
         if (s >= 0 && s < S)
             atomicAdd(&cnt[s], 1);
-        else
-            s_bad = 1;
+        else if (s >= S)
+            s_bad = 1;  // (a negative id is an empty entry)
     }
     __syncthreads();
     int* active_slot = wsp<int>(P, P.L.active_slot);

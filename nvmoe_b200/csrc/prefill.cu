@@ -104,7 +104,7 @@ __global__ void pf_count(PfParams P) {
         const int s = P.ids[(int64_t)t * P.ids_stride + j];
         if (s >= 0 && s < S)
             atomicAdd(&cnt[s], 1);
-        else
+        else if (s >= S)  // (a negative id is an empty entry)
             atomicExch(pws<int>(P, P.L.hdr) + PH_STATUS, NVMOE_ERR_BAD_SLOT);
     }
 }

@@ -210,7 +210,7 @@ __global__ void pf4_count(const __grid_constant__ Pf4Params P) {
         const bool ok = s >= 0 && s < S;
         const unsigned same = __match_any_sync(__activemask(), ok ? s : -1);
         if (ok && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&cnt[s], __popc(same));
-        if (!ok) atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_BAD_SLOT);
+        if (s >= S) atomicExch(qws<int>(P, P.L.hdr) + QH_STATUS, NVMOE_ERR_BAD_SLOT);
     }
 }
 

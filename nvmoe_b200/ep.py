@@ -110,3 +110,167 @@ def nvmoe_local_ffn(pool, table, misses=None, refill_banks=None, host_slot_of_id
         return ops.moe_ffn(pool, xp.contiguous(), slots, w.view(-1, 1).contiguous(),
                            workspace=workspace)
     return run
+
+
+# ---------------------------------------------------------------- the CUDA expert-parallel stack
+class EPMoEStack:
+    """Rank `rank` of `world` in an expert-parallel stack of dependent MoE layers (the decode
+    stack of MoEStack.forward_chain with its routed experts sharded by contiguous ranges).
+
+    The rank keeps, per layer, a slot pool and slot tables over its per = E / world routed
+    experts plus its copy of the shared expert (local id per), a pinned host tier of those
+    per + 1 experts, and the replicated router gates.  One layer step for n_tok home tokens:
+        nvmoe_router_gate -> nvmoe_router_topk -> nvmoe_ep_dispatch
+        -> exchange (all-to-all of world equal segments)
+        -> nvmoe_decode_layer, pre-routed, over the world * n_tok received rows (top_k + 1
+           entries each: remap, refill from the host tier, expert FFN)
+        -> exchange back -> nvmoe_ep_combine
+    Every buffer size is fixed by n_tok, so a step has no host synchronisation and can be
+    captured in a CUDA graph (with the exchanges, when they are NCCL collectives).
+
+    global_host: the model's routed experts (E, on the CPU); shared: its shared expert (1 slot,
+    CPU); ranking: [L, E] global expert popularity (most popular first) for the prewarm."""
+
+    def __init__(self, cfg, n_tok: int, rank: int, world: int, global_host, shared,
+                 device="cuda", seed: int = 0, logit_bias=None, router_seed: int = 5,
+                 eps: float = 1e-6):
+        import dataclasses
+
+        import numpy as np
+
+        from . import ops
+        from .engine import MoEStack, _pin
+        from .formats import concat_experts, select_experts
+
+        self.cfg, self.n_tok, self.rank, self.world = cfg, n_tok, rank, world
+        self.per = per = shard_size(cfg.n_experts, world)
+        self.device = d = torch.device(device)
+        local = concat_experts(select_experts(global_host, range(rank * per, (rank + 1) * per)),
+                               shared)
+        lcfg = dataclasses.replace(cfg, n_experts=per + 1, cache_size=min(cfg.cache_size, per + 1),
+                                   shared_expert=False)
+        self.local = MoEStack(lcfg, device=d, seed=seed, host_tier=_pin(local))
+        # replicated router gates (the same seed on every rank)
+        self.local.cfg = dataclasses.replace(lcfg, n_experts=cfg.n_experts)
+        self.local.init_router(logit_bias=logit_bias, seed=router_seed, eps=eps)
+        self.local.cfg = lcfg
+        L, H, E, k = cfg.n_layers, cfg.hidden, cfg.n_experts, cfg.top_k
+        self.K1 = k + 1
+        self.row = ops.ep_row_bytes(H, k)
+        z = lambda *shape, dt: torch.empty(shape, dtype=dt, device=d)  # noqa: E731
+        self.h = z(L, n_tok, H, dt=torch.bfloat16)
+        self.xn = z(L, n_tok, H, dt=torch.bfloat16)
+        self.logits = z(L, n_tok, E, dt=torch.float32)
+        self.y = z(L, n_tok, H, dt=torch.bfloat16)
+        self.ids = z(n_tok, k, dt=torch.int32)
+        self.w = z(n_tok, k, dt=torch.float32)
+        self.send = torch.zeros((world, n_tok, self.row), dtype=torch.uint8, device=d)
+        self.recv = torch.zeros((world, n_tok, self.row), dtype=torch.uint8, device=d)
+        self.slot_of = z(n_tok, world, dt=torch.int32)
+        self.ypair = z(world, n_tok, H, dt=torch.bfloat16)
+        self.back = z(world, n_tok, H, dt=torch.bfloat16)
+        self.status = torch.zeros(1, dtype=torch.int32, device=d)
+        rv = self.recv.view(world * n_tok, self.row)
+        self.recv_x = rv[:, :2 * H].view(torch.bfloat16)
+        self.recv_ids = rv[:, 2 * H:2 * H + 4 * self.K1].view(torch.int32)
+        self.recv_w = rv[:, 2 * H + 4 * self.K1:2 * H + 8 * self.K1].view(torch.float32)
+        st = self.local
+        self.plans = [
+            ops.DecodeLayerPlan(st.pools[l], st.tables[l], st.misses_sets[l % 2], world * n_tok,
+                                self.K1, refill=st.banks[l], host_slot_of_id=st.host_slot_of_id,
+                                workspace=st.ws_sets[l % 2], device=d)
+            for l in range(L)]
+        self.gates = []
+        for l in range(L):
+            self.gates.append(ops.router_gate_args(
+                self.h[l - 1] if l >= 2 else self.xn[0], self.logits[l], st.gate_w[l],
+                delta=self.y[l - 1] if l >= 1 else None,
+                resid_out=self.h[l] if l >= 1 else None, norm_weight=st.norm_w[l], eps=eps,
+                x_out=self.xn[l],
+                logit_bias=None if st.logit_bias is None else st.logit_bias[l]))
+        self._np = np
+
+    # ------------------------------------------------------------ cache state
+    def local_ranking(self, ranking):
+        """Per-layer prewarm order of this rank's pool: the shared expert, then its routed
+        experts in global popularity order."""
+        np = self._np
+        per, r = self.per, self.rank
+        out = []
+        for row in np.asarray(ranking):
+            mine = [int(e) - r * per for e in row if r * per <= int(e) < (r + 1) * per]
+            out.append([per] + mine)
+        return np.asarray(out, np.int64)
+
+    def prewarm(self, ranking) -> None:
+        self.local.prewarm(self.local_ranking(ranking))
+
+    # ------------------------------------------------------------ one layer, in phases
+    def phase_dispatch(self, l: int, x: torch.Tensor) -> None:
+        """Router gate (residual add, RMSNorm, gate GEMV), top-k and the dispatch pack of layer
+        l; x is the stack's input tokens (read by layers 0 and 1)."""
+        from . import _lib, ops
+        import ctypes as C
+        ga = self.gates[l]
+        if l <= 1:
+            ga.resid, ga.resid_row_stride = x.data_ptr(), x.stride(0)
+        _lib.check(_lib.lib().nvmoe_router_gate(C.byref(ga), ops._stream()), "nvmoe_router_gate")
+        ops.router_topk(self.logits[l], self.cfg.top_k, out_ids=self.ids, out_weights=self.w)
+        ops.ep_dispatch(self.xn[l], self.ids, self.w, self.cfg.n_experts, self.world, self.rank,
+                        self.send, self.slot_of, with_shared=True, status=self.status)
+
+    def phase_local(self, l: int) -> None:
+        """The owner's step over the received rows: remap, refill, expert FFN."""
+        self.plans[l].routed(self.recv_x, self.recv_ids, self.recv_w,
+                             self.ypair.view(self.world * self.n_tok, -1))
+
+    def phase_combine(self, l: int) -> None:
+        from . import ops
+        ops.ep_combine(self.back, self.slot_of, self.y[l])
+
+    def finish(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """out = h_{L-1} + y_{L-1} (the residual after the last layer)."""
+        from . import _lib, ops
+        import ctypes as C
+        L = self.cfg.n_layers
+        fin = ops.router_gate_args(x if L == 1 else self.h[L - 1], None, None,
+                                   delta=self.y[L - 1], resid_out=out)
+        _lib.check(_lib.lib().nvmoe_router_gate(C.byref(fin), ops._stream()), "nvmoe_router_gate")
+        return out
+
+    # ------------------------------------------------------------ the whole stack over NCCL
+    def forward(self, x: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+        """All layers for this rank's tokens x [n_tok, H]; out [n_tok, H] = the residual after
+        the last layer.  Every rank calls it in step (two all-to-alls per layer)."""
+        send = self.send.view(-1)
+        recv = self.recv.view(-1)
+        yp = self.ypair.view(-1)
+        back = self.back.view(-1)
+        for l in range(self.cfg.n_layers):
+            self.phase_dispatch(l, x)
+            dist.all_to_all_single(recv, send, group=group)
+            self.phase_local(l)
+            dist.all_to_all_single(back, yp, group=group)
+            self.phase_combine(l)
+        return self.finish(x, out)
+
+
+def ep_forward_emulated(stacks: list, xs: list, outs: list) -> list:
+    """The same layer steps for every rank of an expert-parallel group held in one process (one
+    GPU), the all-to-all done by segment copies: rank r receives segment r of every rank's send
+    buffer, in rank order.  Tests the kernels and the data layout without a second GPU."""
+    W = len(stacks)
+    for l in range(stacks[0].cfg.n_layers):
+        for r in range(W):
+            stacks[r].phase_dispatch(l, xs[r])
+        for r in range(W):
+            for s in range(W):
+                stacks[r].recv[s].copy_(stacks[s].send[r])
+        for r in range(W):
+            stacks[r].phase_local(l)
+        for r in range(W):
+            for s in range(W):
+                stacks[r].back[s].copy_(stacks[s].ypair[r])
+        for r in range(W):
+            stacks[r].phase_combine(l)
+    return [stacks[r].finish(xs[r], outs[r]) for r in range(W)]

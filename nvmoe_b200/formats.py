@@ -159,6 +159,27 @@ def random_experts(quant: str, n_slots: int, hidden: int, inter: int, seed: int 
     return ExpertWeights(quant, hidden, inter, gu, dn)
 
 
+def select_experts(w: ExpertWeights, idx) -> ExpertWeights:
+    """The experts idx (a sequence of slot indices) of w, copied in that order."""
+    idx = torch.as_tensor(list(idx), dtype=torch.long, device=w.gate_up.data.device)
+
+    def sel(m: QuantMatrix) -> QuantMatrix:
+        return QuantMatrix(m.quant, m.rows, m.cols, m.data.index_select(0, idx).contiguous(),
+                           None if m.scale is None else m.scale.index_select(0, idx).contiguous(),
+                           None if m.glob is None else m.glob.index_select(0, idx).contiguous())
+    return ExpertWeights(w.quant, w.hidden, w.inter, sel(w.gate_up), sel(w.down))
+
+
+def concat_experts(a: ExpertWeights, b: ExpertWeights) -> ExpertWeights:
+    """a's experts followed by b's (same format and shape)."""
+    def cat(x: QuantMatrix, y: QuantMatrix) -> QuantMatrix:
+        return QuantMatrix(x.quant, x.rows, x.cols, torch.cat([x.data, y.data]),
+                           None if x.scale is None else torch.cat([x.scale, y.scale]),
+                           None if x.glob is None else torch.cat([x.glob, y.glob]))
+    return ExpertWeights(a.quant, a.hidden, a.inter, cat(a.gate_up, b.gate_up),
+                         cat(a.down, b.down))
+
+
 # ------------------------------------------------------------------ codecs
 def ftw_to_gguf_nvfp4(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
     """FTW NVFP4 rows -> GGUF block_nvfp4 rows (scripts/convert_ftw_to_gguf.py:46-70):

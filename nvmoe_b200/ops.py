@@ -54,13 +54,18 @@ def _require_cuda(*ts: torch.Tensor) -> None:
 # ------------------------------------------------------------------ R1 router
 def router_topk(logits: torch.Tensor, top_k: int, mode: str = "softmax",
                 bias: torch.Tensor | None = None, norm_topk: bool = True,
-                routed_scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
-    """ids int32 [n, k] and combine weights fp32 [n, k] from fp32 logits [n, E]."""
+                routed_scaling: float = 1.0, out_ids: torch.Tensor | None = None,
+                out_weights: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """ids int32 [n, k] and combine weights fp32 [n, k] from fp32 logits [n, E] (written into
+    out_ids / out_weights when given: contiguous [n, k])."""
     _require_cuda(logits, bias)
     assert logits.dtype == torch.float32 and logits.dim() == 2 and logits.stride(1) == 1
     n, E = logits.shape
-    ids = torch.empty((n, top_k), dtype=torch.int32, device=logits.device)
-    w = torch.empty((n, top_k), dtype=torch.float32, device=logits.device)
+    ids = out_ids if out_ids is not None else torch.empty((n, top_k), dtype=torch.int32,
+                                                          device=logits.device)
+    w = out_weights if out_weights is not None else torch.empty((n, top_k), dtype=torch.float32,
+                                                                device=logits.device)
+    assert ids.is_contiguous() and w.is_contiguous()
     m = _lib.NVMOE_ROUTER_SOFTMAX if mode == "softmax" else _lib.NVMOE_ROUTER_SIGMOID_BIAS
     if bias is not None:
         bias = bias.float().contiguous()
@@ -473,15 +478,68 @@ class DecodeLayerPlan:
         a.inputs_after_wait = int(bool(inputs_after_wait))
         self.args = a
 
-    def __call__(self, x: torch.Tensor, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        assert x.shape[0] == self.n_tok and logits.shape[0] == self.n_tok
-        assert x.dtype == torch.bfloat16 and logits.dtype == torch.float32
+    def routed(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+               out: torch.Tensor) -> torch.Tensor:
+        """A pre-routed step (no router): expert ids [n_tok, top_k] (negative: empty entry)
+        and their weights, rows ids.stride(0) elements apart (the same for both)."""
+        assert x.shape[0] == self.n_tok and ids.shape == (self.n_tok, self.top_k)
+        assert ids.dtype == torch.int32 and weights.dtype == torch.float32
+        assert ids.stride(0) == weights.stride(0) and ids.stride(1) == 1
         a = self.args
-        a.logits = logits.data_ptr()
-        a.logits_row_stride = logits.stride(0)
+        a.logits = None
+        a.routed_ids = ids.data_ptr()
+        a.routed_weights = weights.data_ptr()
+        a.routed_row_stride = ids.stride(0)
         a.ffn.x = x.data_ptr()
         a.ffn.x_row_stride = x.stride(0)
         a.ffn.y = out.data_ptr()
         a.ffn.y_row_stride = out.stride(0)
         check(lib().nvmoe_decode_layer(C.byref(a), _stream()), "nvmoe_decode_layer")
         return out
+
+    def __call__(self, x: torch.Tensor, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        assert x.shape[0] == self.n_tok and logits.shape[0] == self.n_tok
+        assert x.dtype == torch.bfloat16 and logits.dtype == torch.float32
+        a = self.args
+        a.logits = logits.data_ptr()
+        a.logits_row_stride = logits.stride(0)
+        a.routed_ids = a.routed_weights = None
+        a.ffn.x = x.data_ptr()
+        a.ffn.x_row_stride = x.stride(0)
+        a.ffn.y = out.data_ptr()
+        a.ffn.y_row_stride = out.stride(0)
+        check(lib().nvmoe_decode_layer(C.byref(a), _stream()), "nvmoe_decode_layer")
+        return out
+
+
+# ------------------------------------------------------------------ expert parallelism
+def ep_row_bytes(hidden: int, top_k: int) -> int:
+    return int(lib().nvmoe_ep_row_bytes(hidden, top_k))
+
+
+def ep_dispatch(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, n_expert: int,
+                world: int, rank: int, send: torch.Tensor, slot_of: torch.Tensor,
+                with_shared: bool = True, shared_gate: torch.Tensor | None = None,
+                status: torch.Tensor | None = None) -> None:
+    """nvmoe_ep_dispatch: this rank's tokens x [n, H] bf16 routed to ids / weights [n, k] into
+    send [world, n, ep_row_bytes] u8 and slot_of [n, world] int32."""
+    _require_cuda(x, ids, weights, send, slot_of)
+    n, H = x.shape
+    k = ids.shape[1]
+    assert send.dtype == torch.uint8 and send.numel() >= world * n * ep_row_bytes(H, k)
+    assert ids.is_contiguous() and weights.is_contiguous() and slot_of.is_contiguous()
+    a = _lib.EpDispatchArgs(x.data_ptr(), x.stride(0), ids.data_ptr(), weights.data_ptr(),
+                            _ptr(shared_gate), int(with_shared), n, k, H, n_expert, world, rank,
+                            send.data_ptr(), slot_of.data_ptr(), _ptr(status))
+    check(lib().nvmoe_ep_dispatch(C.byref(a), _stream()), "nvmoe_ep_dispatch")
+
+
+def ep_combine(back: torch.Tensor, slot_of: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """nvmoe_ep_combine: out [n, H] = sum over ranks d of back[d, slot_of[t, d]]."""
+    _require_cuda(back, slot_of, out)
+    world, n, H = back.shape
+    assert back.is_contiguous() and slot_of.is_contiguous()
+    a = _lib.EpCombineArgs(back.data_ptr(), slot_of.data_ptr(), n, H, world, out.data_ptr(),
+                           out.stride(0))
+    check(lib().nvmoe_ep_combine(C.byref(a), _stream()), "nvmoe_ep_combine")
+    return out

@@ -61,7 +61,9 @@ def test_struct_layouts_match_a_c_compiler(tmp_path):
                "nvmoe_matrix_bank": _lib.MatrixBank, "nvmoe_expert_pool": _lib.ExpertPool,
                "nvmoe_ffn_args": _lib.FfnArgs, "nvmoe_refill_bank": _lib.RefillBank,
                "nvmoe_decode_args": _lib.DecodeArgs,
-               "nvmoe_router_gate_args": _lib.RouterGateArgs}
+               "nvmoe_router_gate_args": _lib.RouterGateArgs,
+               "nvmoe_ep_dispatch_args": _lib.EpDispatchArgs,
+               "nvmoe_ep_combine_args": _lib.EpCombineArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nvmoe_b200.h"',
              'int main(void) {']
     for cname, py in mirrors.items():
