@@ -16,8 +16,11 @@ Workload (one "step" = one decode batch through a stack of MoE layers):
   logits of the same tokens, so a layer's routing and remap overlap the previous layer's FFN.
 
 metric: layer tokens/s = batch * layers / step time (device CUDA events, max over ranks).
-N > 1: independent replicas (one stack per GPU, own batch): weak scaling, no collective on the
-data path.  --impl reference times the CPU oracle port of the same step on the host cores.
+N > 1: expert parallelism (weak scaling): every rank holds 512 / N experts of each layer in its
+128-slot pools and a batch of its own; each layer dispatches the tokens to the experts' owners
+and combines the outputs by NCCL all-to-all (graph-captured with the kernels).  The prefill
+object at N > 1 is the 4096-token layer under expert parallelism (strong scaling).
+--impl reference times the CPU oracle port of the same step on the host cores.
 """
 from __future__ import annotations
 
@@ -345,6 +348,193 @@ def run_nvmoe(a, rank, world, local_rank):
     return line
 
 
+def run_ep(a, rank, world, local_rank):
+    """Expert-parallel decode (the N-GPU line): every rank holds E / world experts of each layer
+    (128-slot pools, its own host tier) and B tokens of its own; the same dependent-layer stack
+    as the 1-GPU line, with the tokens dispatched to the experts' owners by NCCL all-to-all."""
+    import numpy as np
+    import torch
+
+    from nvmoe_b200.engine import StackConfig
+    from nvmoe_b200.ep import EPMoEStack
+    from nvmoe_b200.formats import random_experts
+    from nvmoe_b200.synth import layer_log_bias
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, B = a.layers, a.batch
+    cfg = StackConfig(n_layers=L)
+    E, k, H = cfg.n_experts, cfg.top_k, cfg.hidden
+    host = random_experts("nvfp4", E, H, cfg.inter, seed=0)
+    shared = random_experts("nvfp4", 1, H, cfg.inter, seed=2)
+    bias = layer_log_bias(L, E, 1.1, seed=0)
+    ranking = np.argsort(-bias, axis=1, kind="stable")
+    st = EPMoEStack(cfg, B, rank, world, host, shared, device=dev, seed=1 + rank, logit_bias=bias)
+    st.prewarm(ranking)
+    R = a.warmup + a.steps
+    e2e_steps = 0 if a.no_e2e else max(10, a.steps)
+    E2E_WARM = 3
+    RT = R + (E2E_WARM + e2e_steps if e2e_steps else 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    xs = torch.randn((RT, B, H), generator=g, device=dev).to(torch.bfloat16)
+    hout = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    cap = torch.cuda.Stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    st.forward(xs[0], hout)  # eager pass: kernel attributes, allocations
+    torch.cuda.synchronize()
+    st.prewarm(ranking)
+    graphs = []
+    for r in range(R):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cap):
+            st.forward(xs[r], hout)
+        graphs.append(gr)
+    torch.cuda.synchronize()
+    U = np.zeros((R, L), np.int64)  # distinct local experts each layer step ran
+    for r, gr in enumerate(graphs):
+        gr.replay()
+        torch.cuda.synchronize()
+        for l, p in enumerate(st.plans):
+            s = p.slot_ids.cpu().numpy()
+            U[r, l] = len(np.unique(s[s >= 0]))
+    st.prewarm(ranking)
+    for i in range(a.warmup):
+        graphs[i].replay()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        t0.record()
+        for i in range(a.steps):
+            graphs[a.warmup + i].replay()
+        t1.record()
+        torch.cuda.synchronize()
+    barrier()
+    el = t0.elapsed_time(t1)
+    tt = torch.tensor([el], device=dev)
+    torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+    ms = float(tt.item()) / a.steps
+    graphs = None
+    torch.cuda.synchronize()
+
+    e2e_ms = None
+    if e2e_steps:
+        xh = xs[R:].cpu().pin_memory()
+        yh = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
+        xin = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+        gr_e2e = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr_e2e, stream=cap):
+            st.forward(xin, hout)
+        torch.cuda.synchronize()
+        for i in range(E2E_WARM):
+            xin.copy_(xh[i], non_blocking=True)
+            gr_e2e.replay()
+            yh.copy_(hout, non_blocking=True)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(E2E_WARM, E2E_WARM + e2e_steps):
+            xin.copy_(xh[i], non_blocking=True)
+            gr_e2e.replay()
+            yh.copy_(hout, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        tt = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+        gr_e2e = None
+        torch.cuda.synchronize()
+
+    peaks = load_peaks()
+    hbm_peak = peaks["hbm_gbs"] if peaks else 6650.0
+    step_bytes = float(((U[a.warmup:] + 0) * st.local.bytes_per_expert).sum()) / a.steps
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(B * L * world / (ms / 1e3), 1), "unit": UNIT,
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4/f16",
+        "data": "synthetic (seeded; random-init NVFP4 expert weights and bf16 router gates)",
+        "config": dict(config_dict(a, world),
+                       parallelism=f"expert parallel x{world} ({E // world} experts per GPU, "
+                                   "NCCL all-to-all dispatch / combine)"),
+        "e2e": None if e2e_ms is None else {
+            "value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
+            "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
+        # per layer: router gate, top-k, two dispatch kernels, decode front, ffn_fused, combine
+        # (NCCL's all-to-all kernels not counted), plus the final residual add
+        "gpu_launches": a.steps * (7 * L + 1),
+        "roofline": {"bound": "hbm", "kernel": "expert-parallel layer step (one rank's expert "
+                                               "bytes per layer step / layer step time)",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4),
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else
+                     "fallback 6650 GB/s", "traffic": None},
+        "breakdown": {"layer_step_us": round(1e3 * ms / L, 3),
+                      "distinct_local_experts_per_layer": round(float(U.mean()), 2),
+                      "tokens_per_rank": B},
+        "clocks": clk.summary(),
+    }
+    return line
+
+
+def run_ep_prefill(a, rank, world, local_rank, peaks):
+    """The prefill layer under expert parallelism: a.prefill_tokens tokens in all (strong
+    scaling), a.prefill_tokens / world per rank, E / world experts resident per rank."""
+    import numpy as np
+    import torch
+
+    from nvmoe_b200 import ops
+    from nvmoe_b200.ep import EPPrefill
+    from nvmoe_b200.formats import random_experts
+    from nvmoe_b200.synth import layer_log_bias, router_logits
+
+    dev = torch.device("cuda", local_rank)
+    E, k, H, I = 512, 10, 2048, 512
+    T = a.prefill_tokens
+    Tr = T // world
+    host = random_experts("nvfp4", E, H, I, seed=11)
+    shared = random_experts("nvfp4", 1, H, I, seed=12)
+    rng = np.random.default_rng(7)
+    lg = torch.from_numpy(router_logits(T, layer_log_bias(1, E, 1.1, seed=0)[0], rng))
+    lg = lg[rank * Tr:(rank + 1) * Tr].contiguous().to(dev)
+    ids, w = ops.router_topk(lg, k)
+    x = torch.randn((T, H), generator=torch.Generator().manual_seed(13))[rank * Tr:(rank + 1) * Tr]
+    x = x.to(torch.bfloat16).to(dev)
+    out = torch.empty((Tr, H), dtype=torch.bfloat16, device=dev)
+    ep = EPPrefill(E, k, Tr, rank, world, host, shared, device=dev)
+    del host
+    for _ in range(3):
+        ep.forward(x, ids, w, out)
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 10
+    e0.record()
+    for _ in range(n):
+        ep.forward(x, ids, w, out)
+    e1.record()
+    torch.cuda.synchronize()
+    tt = torch.tensor([e0.elapsed_time(e1) / n], device=dev)
+    torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+    ms = float(tt.item())
+    flop = 6.0 * T * (k + 1) * H * I
+    tf = flop / (ms / 1e3) / 1e12
+    return {"tokens": T, "tokens_per_rank": Tr, "ms_per_layer": round(ms, 4),
+            "tokens_per_s": round(T / (ms / 1e3), 1), "algorithmic_tflops": round(tf, 1),
+            "mma_tflops_fp4": round(tf * FP4_TERMS, 1),
+            "frac_of_fp4_nominal_dense": round(tf * FP4_TERMS / FP4_NOMINAL_TFLOPS, 4),
+            "parallelism": f"expert parallel x{world}, strong scaling (NCCL all-to-all)",
+            "kernel": "nvmoe_ep_dispatch -> all-to-all -> tcgen05 kind::mxf4nvf4 grouped GEMM "
+                      "(pre-routed) -> all-to-all -> nvmoe_ep_combine"}
+
+
 def run_prefill(a, dev, peaks):
     """One Qwen3.8-shaped NVFP4 MoE layer over a.prefill_tokens bf16 tokens (the prefill
     config: 512 experts all resident, top-10 Zipf routing, shared expert) through
@@ -508,7 +698,12 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
-    line = run_nvmoe(a, rank, world, local_rank)
+    if world > 1:
+        line = run_ep(a, rank, world, local_rank)
+        if a.prefill_tokens > 0:
+            line["prefill"] = run_ep_prefill(a, rank, world, local_rank, load_peaks())
+    else:
+        line = run_nvmoe(a, rank, world, local_rank)
     if rank == 0:
         if not a.no_cpu:
             v, cores, desc = cpu_oracle_sample(a.batch, a.cpu_baseline_seconds)

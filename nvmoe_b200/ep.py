@@ -274,3 +274,52 @@ def ep_forward_emulated(stacks: list, xs: list, outs: list) -> list:
         for r in range(W):
             stacks[r].phase_combine(l)
     return [stacks[r].finish(xs[r], outs[r]) for r in range(W)]
+
+
+class EPPrefill:
+    """Expert-parallel prefill of one MoE layer: rank `rank` of `world` holds its per = E / world
+    routed experts and the shared expert resident in one pool (slot = local id), receives the
+    tokens routed to them and runs them through nvmoe_moe_ffn_prefill (token-sorted tcgen05
+    grouped GEMM), pre-routed with top_k + 1 entries per row (negative ids empty).  Tokens enter
+    and leave by nvmoe_ep_dispatch / nvmoe_ep_combine around two all-to-alls, as in the decode
+    stack.  With world == 1 the exchanges are the identity (the segments are the buffers)."""
+
+    def __init__(self, n_expert: int, top_k: int, n_tok: int, rank: int, world: int, global_host,
+                 shared, device="cuda"):
+        from . import ops
+        from .formats import concat_experts, select_experts
+        self.E, self.k, self.n_tok, self.rank, self.world = n_expert, top_k, n_tok, rank, world
+        self.per = per = shard_size(n_expert, world)
+        d = self.device = torch.device(device)
+        self.pool = concat_experts(select_experts(global_host, range(rank * per, (rank + 1) * per)),
+                                   shared).to(d)
+        H = self.H = global_host.hidden
+        self.K1 = top_k + 1
+        self.row = ops.ep_row_bytes(H, top_k)
+        self.send = torch.zeros((world, n_tok, self.row), dtype=torch.uint8, device=d)
+        self.recv = self.send if world == 1 else torch.zeros_like(self.send)
+        self.slot_of = torch.empty((n_tok, world), dtype=torch.int32, device=d)
+        self.ypair = torch.empty((world, n_tok, H), dtype=torch.bfloat16, device=d)
+        self.back = self.ypair if world == 1 else torch.empty_like(self.ypair)
+        self.status = torch.zeros(1, dtype=torch.int32, device=d)
+        rv = self.recv.view(world * n_tok, self.row)
+        self.recv_x = rv[:, :2 * H].view(torch.bfloat16)
+        self.recv_ids = rv[:, 2 * H:2 * H + 4 * self.K1].view(torch.int32)
+        self.recv_w = rv[:, 2 * H + 4 * self.K1:2 * H + 8 * self.K1].view(torch.float32)
+        self.ws = ops.FfnWorkspace(d)
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                out: torch.Tensor, group=None) -> torch.Tensor:
+        """This rank's n_tok tokens x [n_tok, H] with routed global ids / weights [n_tok, k]
+        -> out [n_tok, H] (routed experts + shared expert).  Every rank calls it in step."""
+        from . import ops
+        ops.ep_dispatch(x, ids, weights, self.E, self.world, self.rank, self.send, self.slot_of,
+                        with_shared=True, status=self.status)
+        if self.world > 1:
+            dist.all_to_all_single(self.recv.view(-1), self.send.view(-1), group=group)
+        ops.moe_ffn_prefill(self.pool, self.recv_x, self.recv_ids, self.recv_w,
+                            out=self.ypair.view(self.world * self.n_tok, self.H), workspace=self.ws,
+                            status=self.status)
+        if self.world > 1:
+            dist.all_to_all_single(self.back.view(-1), self.ypair.view(-1), group=group)
+        return ops.ep_combine(self.back, self.slot_of, out)

@@ -368,6 +368,7 @@ def moe_ffn_prefill(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor
     _require_cuda(x, slot_ids, weights)
     assert x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
     assert slot_ids.dtype == torch.int32 and weights.dtype == torch.float32
+    assert slot_ids.stride(1) == 1 and weights.stride(1) == 1
     n, H = x.shape
     k = slot_ids.shape[1]
     if out is None:

@@ -95,3 +95,28 @@ def test_prefill_reports_bad_slot(cuda_device):
     ops.moe_ffn_prefill(pool, x, ids, w, status=st)
     torch.cuda.synchronize()
     assert int(st.item()) == -8  # NVMOE_ERR_BAD_SLOT
+
+
+def test_prefill_skips_empty_entries(cuda_device):
+    """A negative slot id is an empty entry (the rows an expert-parallel rank receives carry
+    the experts it does not own as -1): the result equals the oracle over the remaining entries,
+    and a token without entries gets y = 0."""
+    from tests.helpers import DenseExperts, bf16_bits, within
+    S, n_tok, k = 24, 96, 5
+    pool = random_experts("nvfp4", S, H, I, seed=81)
+    rng = np.random.default_rng(82)
+    x, ids, w = _inputs(rng, n_tok, k, S, 0.7, cuda_device)
+    ids_h = ids.cpu().numpy()
+    ids_h[rng.random(ids_h.shape) < 0.6] = -1
+    ids_h[7, :] = -1
+    ids = torch.from_numpy(ids_h).to(cuda_device)
+    st = torch.full((1,), 77, dtype=torch.int32, device=cuda_device)
+    y = ops.moe_ffn_prefill(pool.to(cuda_device), x, ids, w, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    wh = w.cpu().numpy().copy()
+    wh[ids_h < 0] = 0.0
+    safe = np.where(ids_h < 0, 0, ids_h)
+    yr = R.moe_ffn(bf16_bits(x), safe, wh, *DenseExperts(pool).callables())
+    assert within(y, yr) <= 1e-2
+    assert not y[7].float().abs().any()
