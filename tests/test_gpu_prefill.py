@@ -114,9 +114,15 @@ def test_prefill_skips_empty_entries(cuda_device):
     y = ops.moe_ffn_prefill(pool.to(cuda_device), x, ids, w, status=st)
     torch.cuda.synchronize()
     assert int(st.item()) == 0
+    # the oracle sees each empty entry as a zero-weight pick of an all-zero expert S (a slot of
+    # its own, so a token's real picks are never merged with its empty ones)
     wh = w.cpu().numpy().copy()
     wh[ids_h < 0] = 0.0
-    safe = np.where(ids_h < 0, 0, ids_h)
-    yr = R.moe_ffn(bf16_bits(x), safe, wh, *DenseExperts(pool).callables())
+    dense = DenseExperts(pool)
+    zero = {"gate": np.zeros((I, H), np.float32), "up": np.zeros((I, H), np.float32),
+            "down": np.zeros((H, I), np.float32)}
+    pick = lambda which: (lambda s: zero[which] if s == S else dense.get(which, s))  # noqa: E731
+    yr = R.moe_ffn(bf16_bits(x), np.where(ids_h < 0, S, ids_h), wh, pick("gate"), pick("up"),
+                   pick("down"))
     assert within(y, yr) <= 1e-2
     assert not y[7].float().abs().any()
