@@ -58,6 +58,7 @@ def parse():
                     help="time the prefill layer alone on one GPU and print its object")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-config3", action="store_true", help="skip the Q2_K stack object")
     return ap.parse_args()
 
 
@@ -345,6 +346,8 @@ def run_nvmoe(a, rank, world, local_rank):
     }
     if a.prefill_tokens > 0:
         line["prefill"] = run_prefill(a, dev, peaks)
+    if not a.no_config3:
+        line["config3_q2k_stack"] = run_config3(a, dev)
     return line
 
 
@@ -533,6 +536,92 @@ def run_ep_prefill(a, rank, world, local_rank, peaks):
             "parallelism": f"expert parallel x{world}, strong scaling (NCCL all-to-all)",
             "kernel": "nvmoe_ep_dispatch -> all-to-all -> tcgen05 kind::mxf4nvf4 grouped GEMM "
                       "(pre-routed) -> all-to-all -> nvmoe_ep_combine"}
+
+
+def pcie_h2d_gbs(dev, nbytes=256 << 20):
+    """Pinned host -> device copy bandwidth of this box (one 256 MiB cudaMemcpyAsync, best of 5)."""
+    import torch
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dst.copy_(src, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    return best
+
+
+def run_config3(a, dev, batches=(1, 8, 16), steps=20, warmup=3):
+    """The Q2_K 48-layer stack: Qwen3.8 shape, Q2_K weights, dependent layers (RMSNorm + router
+    gate in front of each), slot pools of 128 of the 512 experts (25 %), misses refilled from the
+    pinned host tier by the FFN (SM copies over PCIe).  Per batch: layer-tokens/s, the refill
+    bytes per step and the time those bytes need at this box's pinned H2D bandwidth."""
+    import numpy as np
+    import torch
+
+    from nvmoe_b200.engine import MoEStack, StackConfig
+    from nvmoe_b200.synth import layer_log_bias
+
+    L = a.layers
+    cfg = StackConfig(n_layers=L, quant="q2_k")
+    stack = MoEStack(cfg, device=dev, seed=30)
+    bias = layer_log_bias(L, cfg.n_experts, 1.1, seed=0)
+    ranking = np.argsort(-bias, axis=1, kind="stable")
+    stack.init_router(logit_bias=bias, seed=31)
+    bw = pcie_h2d_gbs(dev)
+    per_expert = stack.bytes_per_expert
+    res = []
+    cap = torch.cuda.Stream(dev)
+    for B in batches:
+        R = warmup + steps
+        g = torch.Generator(device=dev)
+        g.manual_seed(3000 + B)
+        xs = torch.randn((R, B, cfg.hidden), generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty((B, cfg.hidden), dtype=torch.bfloat16, device=dev)
+        stack.forward_chain(xs[0], out)
+        torch.cuda.synchronize()
+        stack.prewarm(ranking)
+        graphs = []
+        for r in range(R):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=cap):
+                stack.forward_chain(xs[r], out)
+            graphs.append(gr)
+        plans = stack.chain_buffers(B)["plans"]
+        # misses per step: each miss installs a new expert in one slot of its layer (one remap
+        # per layer step), so they are the slots whose occupant changed over the step
+        miss = np.zeros(R, np.int64)
+        for r, gr in enumerate(graphs):
+            before = torch.stack([t.real_in_slot for t in stack.tables]).clone()
+            gr.replay()
+            after = torch.stack([t.real_in_slot for t in stack.tables])
+            miss[r] = int((before != after).sum().item())
+        stack.prewarm(ranking)
+        for i in range(warmup):
+            graphs[i].replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(warmup, R):
+            graphs[i].replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        refill = float(miss[warmup:].mean()) * per_expert
+        res.append({"batch": B, "layer_tokens_per_s": round(B * L / (ms / 1e3), 1),
+                    "ms_per_step": round(ms, 4), "layer_step_us": round(1e3 * ms / L, 3),
+                    "misses_per_step": round(float(miss[warmup:].mean()), 2),
+                    "refill_bytes_per_step": round(refill),
+                    "refill_pcie_us_per_step": round(refill / (bw * 1e9) * 1e6, 1)})
+        del graphs
+    del stack
+    torch.cuda.empty_cache()
+    return {"workload": f"Q2_K {L}-layer stack of dependent layers (RMSNorm + router gate), "
+                        "512 experts top-10 + shared, H2048 I512, 128 slots/layer (25 %)",
+            "pinned_h2d_gbs": round(bw, 1), "bytes_per_expert": per_expert, "batches": res}
 
 
 def run_prefill(a, dev, peaks):

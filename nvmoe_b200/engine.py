@@ -56,6 +56,9 @@ class StackConfig:
     shared_expert: bool = True
     router: str = "softmax"
     pinned_k: int = 0
+    # GLM-style routing (router "sigmoid"): top-k of sigmoid(logit) + a per-layer selection
+    # bias (set_router_bias), weights renormalised and scaled by routed_scaling
+    routed_scaling: float = 1.0
     # tokens per layer call: a batch larger than this runs as consecutive micro-batches, each
     # through every layer, like llama.cpp's n_ubatch (0: the whole batch in one call; the
     # reference's clamp is safe_ubatch(cache_size, top_k))
@@ -97,6 +100,14 @@ class MoEStack:
         self._chain: dict[int, dict] = {}
         self.gate_w = self.norm_w = self.logit_bias = None
         self.eps = 1e-6
+        self.router_bias = None  # [L, E] fp32 selection bias of the sigmoid router
+
+    def set_router_bias(self, bias: np.ndarray) -> None:
+        """Per-layer selection bias [L, E] of the sigmoid router (GLM's e_score_correction_bias,
+        nvme-moe-bench/nvme_offload_cache.py:3044-3089)."""
+        self.router_bias = torch.from_numpy(np.ascontiguousarray(bias, np.float32)).to(self.device)
+        self._plans.clear()
+        self._chain.clear()
 
     @property
     def bytes_per_expert(self) -> int:
@@ -124,6 +135,9 @@ class MoEStack:
             t.step.zero_()
         torch.cuda.synchronize(self.device)
 
+    def _bias(self, l: int):
+        return None if self.router_bias is None else self.router_bias[l]
+
     def plans(self, n_tok: int) -> list:
         """Per-layer nvmoe_decode_layer argument plans for batches of n_tok tokens."""
         c = self.cfg
@@ -135,6 +149,7 @@ class MoEStack:
                                     c.top_k, shared=self.shared[l], refill=self.banks[l],
                                     host_slot_of_id=self.host_slot_of_id,
                                     workspace=self.ws_sets[l % 2], router=c.router,
+                                    router_bias=self._bias(l), routed_scaling=c.routed_scaling,
                                     device=self.device,
                                     early_outputs=not (l == 0 and c.n_layers % 2 == 1))
                 for l in range(c.n_layers)]
@@ -187,6 +202,7 @@ class MoEStack:
                                 c.top_k, shared=self.shared[l], refill=self.banks[l],
                                 host_slot_of_id=self.host_slot_of_id,
                                 workspace=self.ws_sets[l % 2], router=c.router,
+                                router_bias=self._bias(l), routed_scaling=c.routed_scaling,
                                 device=d, early_outputs=False, inputs_after_wait=True)
             for l in range(L)]
         gates = []
