@@ -309,6 +309,29 @@ int nvmoe_slru_pop_lru_excluding(nvmoe_slru* lru, const int64_t* protect, int n_
                                  int64_t* key_out);
 void nvmoe_slru_discard(nvmoe_slru* lru, int64_t key);
 
+/* The bounded pinned host tier of one layer (scripts/moe_cache_probe.cpp:636-752 host part):
+ * host_slots pinned expert slots in front of the backing store (the reference's NVMe tier),
+ * placed by the segmented LRU above with capacity hint host_slots.  One call per layer step,
+ * after the GPU remap (nvmoe_remap's miss list read back by the host): GPU hits that are in the
+ * host tier are touched; then each GPU miss, in order, is either a host hit (touched; copy it
+ * from host_slot_out[m], load_out[m] = 0) or a host miss: a free host slot if any, else the least
+ * recent key not among this step's ids (probation first; any key when all are in use), whose
+ * expert leaves the host tier; the miss is inserted as new and the caller must fill
+ * host_slot_out[m] from the backing store first (load_out[m] = 1).  Host code, no GPU.
+ * Returns NVMOE_ERR_CACHE_OVERFLOW when a host miss finds no slot, NVMOE_ERR_BAD_EXPERT_ID for
+ * ids outside [0, n_expert). */
+typedef struct nvmoe_host_tier nvmoe_host_tier;
+nvmoe_host_tier* nvmoe_host_tier_create(int32_t n_expert, int32_t host_slots,
+                                        double protected_ratio);
+void nvmoe_host_tier_destroy(nvmoe_host_tier* tier);
+int nvmoe_host_tier_resolve(nvmoe_host_tier* tier, const int32_t* unique_ids,
+                            const uint8_t* unique_hit, int n_unique, const int32_t* miss_ids,
+                            int n_miss, int32_t* host_slot_out, uint8_t* load_out);
+/* Copies the tier's maps: host slot of each expert [n_expert] (-1: not resident) and expert of
+ * each host slot [host_slots] (-1: free).  Either pointer may be NULL. */
+int nvmoe_host_tier_tables(const nvmoe_host_tier* tier, int32_t* host_slot_of_id,
+                           int32_t* id_in_host_slot);
+
 /* ================================================================ R5: pinned-host refill
  * One bank of an expert row in both tiers: slot s of the device pool starts at
  * dst + s*dst_slot_stride, host slot h of the pinned tier at src + h*src_slot_stride; each

@@ -261,6 +261,11 @@ SIGNATURES = {
     "nvmoe_slru_pop_lru_excluding": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64), C.c_int,
                                                C.POINTER(C.c_int64)]),
     "nvmoe_slru_discard": (None, [C.c_void_p, C.c_int64]),
+    "nvmoe_host_tier_create": (C.c_void_p, [C.c_int32, C.c_int32, C.c_double]),
+    "nvmoe_host_tier_destroy": (None, [C.c_void_p]),
+    "nvmoe_host_tier_resolve": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                          C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "nvmoe_host_tier_tables": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "nvmoe_refill_async": (C.c_int, [C.POINTER(RefillBank), C.c_int, C.c_void_p, C.c_void_p,
                                      C.c_int, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                      C.c_void_p]),

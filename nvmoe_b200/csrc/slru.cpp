@@ -14,6 +14,7 @@
 // lists, indexed by a std::unordered_map from key to node.  Operations are O(1) on average; an
 // insert of a new key may allocate a hash node, and pop_lru_excluding builds a hash set of the
 // excluded keys on each call.
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 #include <unordered_map>
@@ -192,6 +193,90 @@ int nvmoe_slru_pop_lru_excluding(nvmoe_slru* lru, const int64_t* protect, int n,
 }
 void nvmoe_slru_discard(nvmoe_slru* lru, int64_t k) {
     if (lru) lru->impl.discard(k);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- the bounded pinned host tier
+// One layer's host tier of the llama.cpp engine (scripts/moe_cache_probe.cpp:636-752): a pool
+// of host_slots pinned expert slots in front of the backing store, placed by the segmented LRU
+// above.  nvmoe_host_tier_resolve is the host part of one eval_cb step, after the GPU remap.
+struct nvmoe_host_tier {
+    explicit nvmoe_host_tier(int32_t e, int32_t hs, double r)
+        : n_expert(e), host_slots(hs), slot_of((size_t)e, -1), id_in((size_t)hs, -1), lru(r) {
+        lru.set_capacity_hint(hs);
+    }
+    int32_t n_expert, host_slots, next_free = 0;
+    std::vector<int32_t> slot_of;  // host slot of expert e, -1: not in the host tier
+    std::vector<int32_t> id_in;    // expert in host slot h, -1: free
+    nvmoe::SegmentedLru lru;
+    std::unordered_set<int64_t> active;  // the step's distinct ids (reused)
+};
+
+extern "C" {
+
+nvmoe_host_tier* nvmoe_host_tier_create(int32_t n_expert, int32_t host_slots,
+                                        double protected_ratio) {
+    if (n_expert <= 0 || host_slots <= 0 || !(protected_ratio >= 0.0) ||
+        !std::isfinite(protected_ratio))
+        return nullptr;
+    return new nvmoe_host_tier(n_expert, host_slots, protected_ratio);
+}
+
+void nvmoe_host_tier_destroy(nvmoe_host_tier* t) { delete t; }
+
+int nvmoe_host_tier_resolve(nvmoe_host_tier* t, const int32_t* unique_ids,
+                            const uint8_t* unique_hit, int n_unique, const int32_t* miss_ids,
+                            int n_miss, int32_t* host_slot_out, uint8_t* load_out) {
+    if (!t || n_unique < 0 || n_miss < 0 || (n_unique > 0 && (!unique_ids || !unique_hit)) ||
+        (n_miss > 0 && (!miss_ids || !host_slot_out || !load_out)))
+        return NVMOE_ERR_INVALID_ARG;
+    for (int i = 0; i < n_unique; ++i)
+        if (unique_ids[i] < 0 || unique_ids[i] >= t->n_expert) return NVMOE_ERR_BAD_EXPERT_ID;
+    for (int m = 0; m < n_miss; ++m)
+        if (miss_ids[m] < 0 || miss_ids[m] >= t->n_expert) return NVMOE_ERR_BAD_EXPERT_ID;
+    t->active.clear();
+    for (int i = 0; i < n_unique; ++i) t->active.insert(unique_ids[i]);
+    // GPU hits that are also in the host tier refresh it (moe_cache_probe.cpp:659-674)
+    for (int i = 0; i < n_unique; ++i)
+        if (unique_hit[i] && t->slot_of[(size_t)unique_ids[i]] != -1) t->lru.touch(unique_ids[i]);
+    for (int m = 0; m < n_miss; ++m) {
+        const int32_t r = miss_ids[m];
+        const int32_t hs = t->slot_of[(size_t)r];
+        if (hs != -1) {  // host hit: copy from its slot
+            t->lru.touch(r);
+            host_slot_out[m] = hs;
+            load_out[m] = 0;
+            continue;
+        }
+        int32_t ns;
+        if (t->next_free < t->host_slots) {
+            ns = t->next_free++;
+        } else {  // the least recent key not used by this step (probation first)
+            int64_t victim = -1;
+            if (!t->lru.pop_lru_excluding(t->active, &victim) && !t->lru.pop_lru(&victim))
+                return NVMOE_ERR_CACHE_OVERFLOW;
+            ns = t->slot_of[(size_t)victim];
+            t->slot_of[(size_t)victim] = -1;
+            t->id_in[(size_t)ns] = -1;
+        }
+        t->id_in[(size_t)ns] = r;
+        t->slot_of[(size_t)r] = ns;
+        t->lru.insert_new(r);
+        host_slot_out[m] = ns;
+        load_out[m] = 1;  // the caller fills host slot ns from the backing store
+    }
+    return NVMOE_OK;
+}
+
+int nvmoe_host_tier_tables(const nvmoe_host_tier* t, int32_t* host_slot_of_id,
+                           int32_t* id_in_host_slot) {
+    if (!t) return NVMOE_ERR_INVALID_ARG;
+    if (host_slot_of_id)
+        std::copy(t->slot_of.begin(), t->slot_of.end(), host_slot_of_id);
+    if (id_in_host_slot)
+        std::copy(t->id_in.begin(), t->id_in.end(), id_in_host_slot);
+    return NVMOE_OK;
 }
 
 }  // extern "C"

@@ -119,6 +119,13 @@ def router_gate(resid: torch.Tensor, gate_weight: torch.Tensor | None,
     return resid_out, x_out, logits
 
 
+def residual_add(resid: torch.Tensor, delta: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out = bf16(resid + delta) (nvmoe_router_gate without norm or gate)."""
+    a = router_gate_args(resid, None, None, delta=delta, resid_out=out)
+    check(lib().nvmoe_router_gate(C.byref(a), _stream()), "nvmoe_router_gate")
+    return out
+
+
 # ------------------------------------------------------------------ R2/R3/R6 remap
 @dataclass
 class SlotTableGPU:
