@@ -348,6 +348,7 @@ def run_nvmoe(a, rank, world, local_rank):
         line["prefill"] = run_prefill(a, dev, peaks)
     if not a.no_config3:
         line["config3_q2k_stack"] = run_config3(a, dev)
+        line["config3_q2k_stack"]["bounded_host_tier"] = run_config3_bounded(dev)
     return line
 
 
@@ -622,6 +623,52 @@ def run_config3(a, dev, batches=(1, 8, 16), steps=20, warmup=3):
     return {"workload": f"Q2_K {L}-layer stack of dependent layers (RMSNorm + router gate), "
                         "512 experts top-10 + shared, H2048 I512, 128 slots/layer (25 %)",
             "pinned_h2d_gbs": round(bw, 1), "bytes_per_expert": per_expert, "batches": res}
+
+
+def run_config3_bounded(dev, layers=8, host_frac=0.5, batch=8, steps=10, warmup=3):
+    """The Q2_K stack with a bounded host tier: pinned host tiers of host_frac of the experts per
+    layer in front of a backing store (pageable host memory standing in for the NVMe tier), the
+    host tier placed by the native SLRU from each layer step's miss list read back by the host,
+    misses copied by cudaMemcpyAsync on a side stream (copy engine).  Eager, one host read per
+    layer step, as the reference's eval_cb; fewer layers than the stack above (its pinned tiers
+    are per layer)."""
+    import torch
+
+    from nvmoe_b200.engine import StackConfig
+    from nvmoe_b200.synth import layer_log_bias
+    from nvmoe_b200.tier import BoundedTierStack
+
+    cfg = StackConfig(n_layers=layers, quant="q2_k")
+    hs = int(cfg.n_experts * host_frac)
+    st = BoundedTierStack(cfg, hs, device=dev, seed=40)
+    st.init_router(logit_bias=layer_log_bias(layers, cfg.n_experts, 1.1, seed=0), seed=41)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4000)
+    xs = torch.randn((warmup + steps, batch, cfg.hidden), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty((batch, cfg.hidden), dtype=torch.bfloat16, device=dev)
+    for i in range(warmup):
+        st.forward(xs[i], out)
+    torch.cuda.synchronize()
+    s0 = dict(st.stats)
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(warmup, warmup + steps):
+        st.forward(xs[i], out)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1) / steps
+    d = {k: st.stats[k] - s0[k] for k in st.stats}
+    return {"workload": f"Q2_K {layers}-layer dependent stack, 128 GPU slots and {hs} pinned host "
+                        f"slots per layer of 512 experts, batch {batch}",
+            "layer_tokens_per_s": round(batch * layers / (ms / 1e3), 1),
+            "ms_per_step": round(ms, 3), "host_wall_ms_per_step": round(1e3 * wall / steps, 3),
+            "gpu_misses_per_step": round(d["gpu_misses"] / steps, 2),
+            "host_hits_per_step": round(d["host_hits"] / steps, 2),
+            "backing_loads_per_step": round(d["host_loads"] / steps, 2),
+            "refill_bytes_per_step": round(d["refill_bytes"] / steps),
+            "refill": "cudaMemcpyAsync per bank on a side stream, event-joined (copy engine)"}
 
 
 def run_prefill(a, dev, peaks):
