@@ -30,3 +30,19 @@ def test_pool_from_views_ftw_order():
     assert p.down.scale.data_ptr() == w.down.scale.data_ptr()
     assert p.gate_up.glob.shape == (4,) and p.down.glob.shape == (4,)
     assert p.gate_up.rows == 256 and p.down.rows == 256 and p.n_slots == 4
+
+
+def test_pool_from_views_gguf_and_bf16():
+    for q in ("q2_k", "iq2_xxs", "bf16"):
+        w = random_experts(q, 3, 512, 256, seed=3)
+        p = pool_from_views(w.banks(), q, 512, 256)
+        assert p.gate_up.data.data_ptr() == w.gate_up.data.data_ptr()
+        assert p.down.data.data_ptr() == w.down.data.data_ptr()
+        assert p.gate_up.data.shape == w.gate_up.data.shape
+        assert p.down.data.shape == w.down.data.shape
+
+
+def test_hook_flow_names():
+    from nvmoe_b200.cache import decode_routed, prefill_routed
+    assert callable(decode_routed) and callable(prefill_routed)
+    assert hasattr(SlotCache, "materialize_layer")

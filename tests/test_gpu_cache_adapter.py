@@ -90,3 +90,89 @@ def test_slot_cache_bank_views_are_the_pool(cuda_device):
         assert torch.equal(v[4][s].cpu(), host.down.scale[E + e])     # scales byte-exact
     cache.reset()
     assert int((cache.slot_for_id >= 0).sum()) == 0
+
+
+def test_slot_cache_prefill_flow_matches_oracle(cuda_device):
+    """prefill_routed as the narrowed-prefill patch runs it (nvme_offload_cache.py:1957-2013):
+    the prompt's routed union ensured in one call, one slot_for_id gather, the grouped GEMM with
+    is_prefill=True; after decode steps have filled part of the pool."""
+    from nvmoe_b200.cache import decode_routed, prefill_routed
+    from tests.helpers import DenseExperts, bf16_bits, within
+    host = _pin(random_experts("nvfp4", L * E, H, I, seed=23))
+    cache = SlotCache(host, L, E, S, device=cuda_device)
+    orc = OracleLayer(L * E, S)
+    bias = layer_log_bias(L, E, 1.1, seed=5)
+    rng = np.random.default_rng(7)
+    dense = DenseExperts(host)
+    for step in range(3):  # decode steps first
+        for l in range(L):
+            rids, rw = R.router_topk_softmax(router_logits(2, bias[l], rng), K)
+            ids = torch.from_numpy(rids.astype(np.int32)).to(cuda_device)
+            x = torch.randn((2, H), device=cuda_device).to(torch.bfloat16)
+            decode_routed(cache, l, x, torch.from_numpy(rw).to(cuda_device), ids)
+            orc.eval((rids + l * E).reshape(-1), is_decode=True)
+    T = 300
+    for l in range(L):
+        rids, rw = R.router_topk_softmax(router_logits(T, bias[l], rng), K)
+        ids = torch.from_numpy(rids.astype(np.int32)).to(cuda_device)
+        x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(torch.bfloat16)
+        y = prefill_routed(cache, l, x.to(cuda_device), torch.from_numpy(rw).to(cuda_device), ids)
+        torch.cuda.synchronize()
+        cache.check()
+        union = np.unique(rids).astype(np.int32)  # torch.unique: ascending
+        ref = orc.eval(union + l * E, is_decode=True)
+        assert ref["status"] == 0
+        sor, ris, _, _ = orc.tables()
+        np.testing.assert_array_equal(cache.slot_for_id.cpu().numpy().reshape(-1), sor)
+        np.testing.assert_array_equal(ids.cpu().numpy(), rids)  # topk_ids left as they were
+        yr = R.moe_ffn(bf16_bits(x), rids + l * E, rw, *dense.callables())
+        assert within(y, yr) <= 1e-2
+
+
+def test_materialize_layer_places_experts_at_identity_slots(cuda_device):
+    """materialize_layer (nvme_offload_cache.py:1626-1682) then the non-narrowed GEMM over
+    bank_views(num_experts) with the raw expert ids."""
+    from tests.helpers import DenseExperts, bf16_bits, within
+    host = _pin(random_experts("nvfp4", L * E, H, I, seed=24))
+    cache = SlotCache(host, L, E, S, device=cuda_device)
+    ids0 = torch.tensor([[3, 60, 7, 1]], dtype=torch.int32, device=cuda_device)
+    cache.ensure_experts(0, ids0)
+    cache.copy_missing()
+    cache.materialize_layer(1)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(cache.slot_for_id[1].cpu().numpy(), np.arange(E))
+    np.testing.assert_array_equal(cache.id_of_slot[:E].cpu().numpy(), E + np.arange(E))
+    assert int((cache.slot_for_id[0] >= 0).sum()) == 0  # layer 0's experts were in slots < E
+    rng = np.random.default_rng(8)
+    rids, rw = R.router_topk_softmax(rng.standard_normal((64, E)).astype(np.float32), K)
+    x = torch.from_numpy(rng.standard_normal((64, H)).astype(np.float32)).to(torch.bfloat16)
+    y = expert_gemm(cache, x.to(cuda_device), torch.from_numpy(rw).to(cuda_device),
+                    torch.from_numpy(rids.astype(np.int32)).to(cuda_device),
+                    views=cache.bank_views(E), n=None, alphas=None, is_prefill=True)
+    yr = R.moe_ffn(bf16_bits(x), rids + E, rw, *DenseExperts(host).callables())
+    assert within(y, yr) <= 1e-2
+
+
+def test_slot_cache_q2k_views(cuda_device):
+    """A Q2_K pool through the hook: bank_views() gives (gate_up, down) super-block rows and
+    expert_gemm runs the Q2_K decode kernel on them."""
+    from nvmoe_b200.cache import decode_routed
+    from tests.helpers import bf16_bits, within
+    host = _pin(random_experts("q2_k", L * E, H, I, seed=25))
+    cache = SlotCache(host, L, E, S, device=cuda_device)
+    assert len(cache.bank_views()) == 2
+    rng = np.random.default_rng(9)
+    rids, rw = R.router_topk_softmax(rng.standard_normal((3, E)).astype(np.float32), K)
+    ids = torch.from_numpy(rids.astype(np.int32)).to(cuda_device)
+    x = torch.from_numpy(rng.standard_normal((3, H)).astype(np.float32)).to(torch.bfloat16)
+    y = decode_routed(cache, 1, x.to(cuda_device), torch.from_numpy(rw).to(cuda_device), ids)
+    torch.cuda.synchronize()
+
+    def dq(which, g):
+        m = host.gate_up if which != "down" else host.down
+        rows = slice(0, I) if which == "gate" else (slice(I, 2 * I) if which == "up" else slice(None))
+        b = m.data[g, rows].numpy()
+        return R.dequant_q2_k(b).reshape(b.shape[0], -1)
+    yr = R.moe_ffn(bf16_bits(x), rids + E, rw, lambda g: dq("gate", g), lambda g: dq("up", g),
+                   lambda g: dq("down", g))
+    assert within(y, yr) <= 1e-2
