@@ -418,6 +418,10 @@ def refill_async(banks: list[_lib.RefillBank], gpu_slots, host_slots, n_gpu_slot
     g = np.ascontiguousarray(gpu_slots, np.int32)
     h = np.ascontiguousarray(host_slots, np.int32)
     arr = (_lib.RefillBank * len(banks))(*banks)
+    if done is not None and not done.cuda_event:
+        # torch creates the CUDA event on its first record: without one the copy stream and the
+        # compute stream would not be joined
+        done.record(compute_stream if compute_stream is not None else copy_stream)
     check(lib().nvmoe_refill_async(arr, len(banks), g.ctypes.data, h.ctypes.data, g.size,
                                    n_gpu_slots, n_host_slots, int(copy_stream.cuda_stream),
                                    None if compute_stream is None else int(compute_stream.cuda_stream),
