@@ -203,3 +203,65 @@ class RefSlru:
         return int(self.L.ref_slru_pop_lru_excluding(self.h, p, p.size))
 
     def discard(self, k): self.L.ref_slru_discard(self.h, k)
+
+
+REF_EVALCB_SO = HERE / "_ref" / "libref_evalcb.so"
+
+
+class RefEvalCb:
+    """The reference's own eval_cb remap + host-tier block (scripts/moe_cache_probe.cpp:627-753,
+    955-970) compiled into oracle/_ref/libref_evalcb.so by oracle/Makefile.  Same step interface
+    as OracleLayer.eval; the reference always has a host tier (host_cache_size >= 1: give it
+    n_expert slots to leave the GPU tier alone).  The reference aborts when a step has more
+    distinct ids than slots: callers keep within the pool."""
+
+    _lib = None
+
+    def __init__(self, n_expert: int, cache_size: int, pinned_k: int = 0,
+                 host_cache_size: int = 0, protected_ratio: float = 0.8):
+        if host_cache_size < 1:
+            raise ValueError("the reference's eval_cb always has a host tier (host_cache_size >= 1)")
+        if RefEvalCb._lib is None:
+            if not REF_EVALCB_SO.exists():
+                raise FileNotFoundError(str(REF_EVALCB_SO))
+            L = C.CDLL(str(REF_EVALCB_SO))
+            L.ref_evalcb_create.restype = _P
+            L.ref_evalcb_create.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_double]
+            L.ref_evalcb_destroy.argtypes = [_P]
+            L.ref_evalcb_step.restype = C.c_int
+            L.ref_evalcb_step.argtypes = [_P, _I32P, C.c_int, C.c_int, C.c_int, _I32P, _I32P,
+                                          _I32P, _I32P, _I32P, _I32P, _I32P, _I32P]
+            L.ref_evalcb_tables.argtypes = [_P, _I32P, _I32P, _U32P, _U32P]
+            RefEvalCb._lib = L
+        self.L = RefEvalCb._lib
+        self.n_expert, self.cache_size = n_expert, cache_size
+        self.h = self.L.ref_evalcb_create(n_expert, cache_size, pinned_k, host_cache_size,
+                                          protected_ratio)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.ref_evalcb_destroy(self.h)
+            self.h = None
+
+    def eval(self, ids: np.ndarray, n_used: int, is_decode: bool) -> dict:
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1)
+        n = ids.size
+        cap = max(n, 1)
+        out = np.empty(cap, np.int32)
+        hg, hh, nh = np.empty(cap, np.int32), np.empty(cap, np.int32), np.zeros(1, np.int32)
+        li, lg, lh, nl = (np.empty(cap, np.int32), np.empty(cap, np.int32),
+                          np.empty(cap, np.int32), np.zeros(1, np.int32))
+        self.L.ref_evalcb_step(self.h, ids, n // n_used, n_used, int(is_decode), out, hg, hh, nh,
+                               li, lg, lh, nl)
+        return {"slots": out[:n].copy(),
+                "h2d": list(zip(hg[:int(nh[0])].tolist(), hh[:int(nh[0])].tolist())),
+                "loads": list(zip(li[:int(nl[0])].tolist(), lg[:int(nl[0])].tolist(),
+                                  lh[:int(nl[0])].tolist()))}
+
+    def tables(self):
+        a = np.empty(self.n_expert, np.int32)
+        b = np.empty(self.cache_size, np.int32)
+        c = np.empty(self.cache_size, np.uint32)
+        d = np.empty(1, np.uint32)
+        self.L.ref_evalcb_tables(self.h, a, b, c, d)
+        return a, b, c, int(d[0])
