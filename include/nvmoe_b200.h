@@ -346,11 +346,12 @@ typedef struct nvmoe_refill_bank {
 } nvmoe_refill_bank;
 
 /* Issues one cudaMemcpyAsync per (bank, run of consecutive slot pairs) on copy_stream (host
- * arrays gpu_slots / host_slots of length n).  When compute_stream and done are given, `done`
- * is first recorded on compute_stream and waited on by copy_stream (an evicted slot may still
- * be read by FFN work queued there), then recorded on copy_stream after the copies and waited
- * on by compute_stream.  Bounds-checked against n_gpu_slots / n_host_slots; host memory must
- * be pinned for the copies to be asynchronous.  compute_stream / done may be NULL. */
+ * arrays gpu_slots / host_slots of length n).  When done is given, `done` is first recorded on
+ * compute_stream and waited on by copy_stream (an evicted slot may still be read by FFN work
+ * queued there), then recorded on copy_stream after the copies and waited on by
+ * compute_stream; a NULL compute_stream is the default stream.  done NULL: no join.
+ * Bounds-checked against n_gpu_slots / n_host_slots; host memory must be pinned for the copies
+ * to be asynchronous. */
 int nvmoe_refill_async(const nvmoe_refill_bank* banks, int n_banks, const int32_t* gpu_slots,
                        const int32_t* host_slots, int n, int32_t n_gpu_slots,
                        int32_t n_host_slots, nvmoe_stream_t copy_stream,

@@ -92,7 +92,8 @@ extern "C" int nvmoe_refill_async(const nvmoe_refill_bank* banks, int n_banks,
     cudaEvent_t ev = (cudaEvent_t)done;
     if (n == 0) return NVMOE_OK;
     // the evicted slots may still be read by FFN work queued earlier on the compute stream
-    if (ks && ev && ks != cs) {
+    // (a null compute stream is the default stream, a stream like any other here)
+    if (ev && ks != cs) {
         NVMOE_CUDA_TRY(cudaEventRecord(ev, ks));
         NVMOE_CUDA_TRY(cudaStreamWaitEvent(cs, ev, 0));
     }
@@ -117,7 +118,7 @@ extern "C" int nvmoe_refill_async(const nvmoe_refill_bank* banks, int n_banks,
     }
     if (ev) {
         NVMOE_CUDA_TRY(cudaEventRecord(ev, cs));
-        if (ks && ks != cs) NVMOE_CUDA_TRY(cudaStreamWaitEvent(ks, ev, 0));
+        if (ks != cs) NVMOE_CUDA_TRY(cudaStreamWaitEvent(ks, ev, 0));
     }
     return NVMOE_OK;
 }

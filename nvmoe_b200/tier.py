@@ -32,9 +32,9 @@ class HostTier:
             raise ValueError("nvmoe_host_tier_create rejected its arguments")
 
     def __del__(self):
-        if getattr(self, "h", None):
-            lib().nvmoe_host_tier_destroy(self.h)
-            self.h = None
+        h, self.h = getattr(self, "h", None), None
+        if h and _lib._lib is not None:  # (the library may be gone at interpreter exit)
+            _lib._lib.nvmoe_host_tier_destroy(h)
 
     def resolve(self, unique_ids, unique_hit, miss_ids):
         """(host slot of each miss, 1 where that slot must first be loaded)."""

@@ -11,7 +11,8 @@
 //     compute stream by an event (nvmoe_refill_async; moe_cache_probe.cpp:755-784,988-993);
 //   - the "mul_mat_id" node then runs the expert FFN on the slot-sized pool (nvmoe_moe_ffn),
 //     reading the rewritten ids through the same strided view;
-//   - two MoE layers are chained: layer 1's tokens are layer 0's output.
+//   - two MoE layers are chained: layer l + 1's tokens are RMSNorm(x_l + y_l) of layer l's input
+//     and output (nvmoe_router_gate with no gate matrix), as a decoder stack feeds them.
 // Test infrastructure (tests/test_gpu_evalcb_driver.py builds and runs it); not part of the
 // library.  Usage: mock_eval_cb <dir> E k H I S n_tok n_as_full L
 #include <cuda_runtime.h>
@@ -205,6 +206,12 @@ int main(int argc, char** argv) {
     uint16_t* x = dev_alloc<uint16_t>((size_t)n_tok * H);
     CK(cudaMemcpy(x, xh.data(), xh.size(), cudaMemcpyHostToDevice));
     uint16_t* y = dev_alloc<uint16_t>((size_t)NL * n_tok * H);
+    uint16_t* xin = dev_alloc<uint16_t>((size_t)NL * n_tok * H);  // each layer's input tokens
+    uint16_t* hres = dev_alloc<uint16_t>((size_t)n_tok * H);
+    CK(cudaMemcpy(xin, x, (size_t)n_tok * H * 2, cudaMemcpyDeviceToDevice));
+    std::vector<uint16_t> ones((size_t)H, 0x3F80);  // RMSNorm gamma = 1 (bf16)
+    uint16_t* gamma = dev_alloc<uint16_t>((size_t)H);
+    CK(cudaMemcpy(gamma, ones.data(), (size_t)H * 2, cudaMemcpyHostToDevice));
     // argsort output [n_as_full, n_tok] per layer; selected_experts is its first k columns
     int32_t* argsort = dev_alloc<int32_t>((size_t)NL * n_tok * n_as_full, -1);
     float* wts = dev_alloc<float>((size_t)NL * n_tok * k);
@@ -239,7 +246,24 @@ int main(int argc, char** argv) {
         nvmoe_ffn_args a;
         std::memset(&a, 0, sizeof(a));
         a.pool = &st.layers[(size_t)l].pool;
-        a.x = l == 0 ? x : y + (size_t)(l - 1) * n_tok * H;  // the chain: layer l-1's output
+        if (l > 0) {  // the chain: RMSNorm(x_{l-1} + y_{l-1})
+            nvmoe_router_gate_args g;
+            std::memset(&g, 0, sizeof(g));
+            g.resid = xin + (size_t)(l - 1) * n_tok * H;
+            g.resid_row_stride = H;
+            g.delta = y + (size_t)(l - 1) * n_tok * H;
+            g.delta_row_stride = H;
+            g.resid_out = hres;
+            g.resid_out_row_stride = H;
+            g.norm_weight = gamma;
+            g.eps = 1e-6f;
+            g.x_out = xin + (size_t)l * n_tok * H;
+            g.x_out_row_stride = H;
+            g.n_tok = n_tok;
+            g.hidden = H;
+            NV(nvmoe_router_gate(&g, st.compute));
+        }
+        a.x = xin + (size_t)l * n_tok * H;
         a.x_row_stride = H;
         a.slot_ids = static_cast<const int32_t*>(sel.data);
         a.ids_row_stride = n_as_full;
@@ -269,6 +293,9 @@ int main(int argc, char** argv) {
     for (size_t r = 0; r < (size_t)NL * n_tok; ++r)
         for (int c = k; c < n_as_full; ++c) untouched &= all[r * n_as_full + c] == -1;
     write_file(dir + "/y.bin", yh.data(), yh.size() * 2);
+    std::vector<uint16_t> xh2((size_t)NL * n_tok * H);
+    CK(cudaMemcpy(xh2.data(), xin, xh2.size() * 2, cudaMemcpyDeviceToHost));
+    write_file(dir + "/xin.bin", xh2.data(), xh2.size() * 2);
     write_file(dir + "/slots.bin", slots.data(), slots.size() * 4);
     char msg[128];
     const int m = std::snprintf(msg, sizeof msg, "OK ffn_status=%d refills=%lld untouched=%d", fs,

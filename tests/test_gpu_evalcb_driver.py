@@ -1,10 +1,11 @@
 """The llama.cpp eval-callback binding compiled against include/nvmoe_b200.h and run from C++:
 tests/evalcb/mock_eval_cb.cpp plays ggml_backend_sched with the callback the reference registers
 (moe_cache_probe.cpp:439-997) over two chained MoE layers, the selected-experts view
-non-contiguous (nb[1] = n_as_full * 4, test_sched_chain_shrink.cpp:75-105,211-215).  Checked:
-the ids rewritten in place equal the oracle's eval_cb slots, the columns outside the view are
-untouched, outputs are NaN-free (the reference test's criterion, :314-322) and within the FFN
-tolerance of the fp32 oracle, layer 1 on layer 0's GPU output."""
+non-contiguous (nb[1] = n_as_full * 4, test_sched_chain_shrink.cpp:75-105,211-215), layer 1's
+tokens RMSNorm(x + y) of layer 0's.  Checked: the ids rewritten in place equal the oracle's
+eval_cb slots, the columns outside the view are untouched, outputs are NaN-free (the reference
+test's criterion, :314-322) and within the FFN tolerance of the fp32 oracle on each layer's GPU
+input, which is itself checked against the oracle's RMSNorm (within 1 bf16 ulp)."""
 import os
 import shutil
 import subprocess
@@ -54,10 +55,16 @@ def test_mock_eval_cb_two_chained_layers(cuda_device, tmp_path):
     status = (tmp_path / "status.txt").read_text()
     assert status.startswith("OK ffn_status=0") and "untouched=1" in status, status
     y = np.fromfile(tmp_path / "y.bin", np.uint16).reshape(NL, n_tok, H)
+    xin = np.fromfile(tmp_path / "xin.bin", np.uint16).reshape(NL, n_tok, H)
     slots = np.fromfile(tmp_path / "slots.bin", np.int32).reshape(NL, n_tok, k)
     dense = DenseExperts(host)
-    x_in = x
+    np.testing.assert_array_equal(xin[0], x)
     for l in range(NL):
+        if l > 0:
+            xr = R.rmsnorm_bf16(R.residual_add_bf16(xin[l - 1], y[l - 1]),
+                                np.full(H, 0x3F80, np.uint16), 1e-6)
+            assert np.abs(xin[l].astype(np.int32) - xr.astype(np.int32)).max() <= 1
+        x_in = xin[l]
         ref = OracleLayer(E, S).eval(ids[l].reshape(-1), is_decode=True)
         assert ref["status"] == 0
         np.testing.assert_array_equal(slots[l].reshape(-1), ref["slots"])
@@ -65,4 +72,3 @@ def test_mock_eval_cb_two_chained_layers(cuda_device, tmp_path):
         assert np.isfinite(yl).all()
         yr = R.moe_ffn(x_in, ids[l], w[l], *dense.callables())
         assert np.abs(yl - yr).max() <= 1e-2 * float(np.abs(yr).max()), l
-        x_in = y[l]  # the chain: layer l + 1 reads layer l's output
