@@ -320,8 +320,8 @@ def run_nvmoe(a, rank, world, local_rank):
         "e2e": None if e2e_ms is None else {
             "value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
             "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
-        # per layer step: router gate + decode_front_kernel + ffn_fused (misses are copied in
-        # by the FFN), plus the final residual add
+        # per layer step: router gate (gate GEMV + top-k) + decode_front_kernel (pre-routed)
+        # + ffn_fused (misses are copied in by the FFN), plus the final residual add
         "gpu_launches": a.steps * (3 * L + 1),
         "roofline": {"bound": "hbm", "kernel": "ffn_fused (the fused expert kernel of one layer)",
                      "achieved": round(achieved, 1),
@@ -471,9 +471,9 @@ def run_ep(a, rank, world, local_rank):
         "e2e": None if e2e_ms is None else {
             "value": round(B * L * world / (e2e_ms / 1e3), 1), "unit": UNIT,
             "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
-        # per layer: router gate, top-k, two dispatch kernels, decode front, ffn_fused, combine
-        # (NCCL's all-to-all kernels not counted), plus the final residual add
-        "gpu_launches": a.steps * (7 * L + 1),
+        # per layer: router gate (with the top-k), two dispatch kernels, decode front,
+        # ffn_fused, combine (NCCL's all-to-all kernels not counted), plus the final residual add
+        "gpu_launches": a.steps * (6 * L + 1),
         "roofline": {"bound": "hbm", "kernel": "expert-parallel layer step (one rank's expert "
                                                "bytes per layer step / layer step time)",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",

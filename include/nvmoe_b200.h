@@ -114,6 +114,19 @@ typedef struct nvmoe_router_gate_args {
     int32_t n_tok;
     int32_t hidden;
     int32_t n_expert;
+    /* Optional router top-k in the same launch (top_k > 0): once a block of 8 tokens has all its
+     * logits, the last CTA to finish on it routes them exactly as nvmoe_router_topk does (mode,
+     * bias, norm_topk, routed_scaling alike) into out_ids / out_weights [n_tok, top_k]
+     * (contiguous).  tickets: device ints [ceil(n_tok / 8)], zero before the first call; every
+     * call leaves them zero again. */
+    int32_t top_k;
+    int32_t router_mode;
+    const float* router_bias;
+    int32_t norm_topk;
+    float routed_scaling;
+    int32_t* out_ids;
+    float* out_weights;
+    int32_t* tickets;
 } nvmoe_router_gate_args;
 
 int nvmoe_router_gate(const nvmoe_router_gate_args* args, nvmoe_stream_t stream);

@@ -224,6 +224,14 @@ class RouterGateArgs(C.Structure):
         ("n_tok", C.c_int32),
         ("hidden", C.c_int32),
         ("n_expert", C.c_int32),
+        ("top_k", C.c_int32),
+        ("router_mode", C.c_int32),
+        ("router_bias", C.c_void_p),
+        ("norm_topk", C.c_int32),
+        ("routed_scaling", C.c_float),
+        ("out_ids", C.c_void_p),
+        ("out_weights", C.c_void_p),
+        ("tickets", C.c_void_p),
     ]
 
 

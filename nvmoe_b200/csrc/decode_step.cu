@@ -98,42 +98,56 @@ __host__ __device__ inline FrontSmem front_smem(int E, int S, int n, int n_ent) 
 }
 
 // Token rows -> f16 and the shared-expert gate, one warp per token (no block barrier).  The
-// row's loads are issued in batches of 8 x 16 bytes per lane before any of them is used.
+// row's loads are issued in batches of 8 x 16 bytes per lane before any of them is used; the
+// conversion is packed (two values per instruction) and each mode has its own loop, so little
+// code runs: this kernel's code is cold in the instruction cache at every launch.
+__device__ __forceinline__ __half2 bf16x2_to_half2(uint32_t v) {
+    return __floats2half2_rn(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
 __device__ __forceinline__ void front_convert_token(const FfnParams& P, int t, int lane) {
     const int H = P.pool.hidden;
     const uint16_t* xr = P.x + (int64_t)t * P.x_stride;
     __half* x16 = wsp<__half>(P, P.L.x16) + (int64_t)t * H;
-    float dot = 0.f, amax = 0.f;
     constexpr int kBatch = 8;
-    for (int i0 = lane * 8; i0 < H; i0 += 256 * kBatch) {
-        uint4 v[kBatch];
+    if (!P.use_fp4) {
+        for (int i0 = lane * 8; i0 < H; i0 += 256 * kBatch) {
+            uint4 v[kBatch];
 #pragma unroll
-        for (int b = 0; b < kBatch; ++b) {
-            const int i = i0 + b * 256;
-            v[b] = i < H ? *reinterpret_cast<const uint4*>(xr + i) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) {
-            const int i = i0 + b * 256;
-            if (i >= H) break;
-            const uint16_t* e = reinterpret_cast<const uint16_t*>(&v[b]);
-            __align__(16) __half o[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float f = bf16_bits_to_f32(e[k]);
-                o[k] = __float2half_rn(f);
-                amax = fmaxf(amax, fabsf(f));
-                if (P.shared_gate) dot = fmaf(f, bf16_bits_to_f32(P.shared_gate[i + k]), dot);
+            for (int b = 0; b < kBatch; ++b) {
+                const int i = i0 + b * 256;
+                v[b] = i < H ? *reinterpret_cast<const uint4*>(xr + i) : make_uint4(0, 0, 0, 0);
             }
-            if (!P.use_fp4) *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) {
+                const int i = i0 + b * 256;
+                if (i >= H) break;
+                __half2 o[4] = {bf16x2_to_half2(v[b].x), bf16x2_to_half2(v[b].y),
+                                bf16x2_to_half2(v[b].z), bf16x2_to_half2(v[b].w)};
+                *reinterpret_cast<uint4*>(x16 + i) = *reinterpret_cast<const uint4*>(o);
+            }
         }
-    }
-    if (P.use_fp4) {  // the row's FP4 term exponent
+    } else {  // the row's FP4 term exponent
+        float amax = 0.f;
+#pragma unroll 1
+        for (int i = lane * 2; i < H; i += 64) {
+            const uint32_t v = *reinterpret_cast<const uint32_t*>(xr + i);
+            amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(v << 16)),
+                                     fabsf(__uint_as_float(v & 0xffff0000u))));
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (lane == 0) wsp<int>(P, P.L.xk)[t] = fp4_row_exp(amax);
     }
     if (P.shared_gate) {
+        float dot = 0.f;
+#pragma unroll 1
+        for (int i = lane * 2; i < H; i += 64) {
+            const uint32_t v = *reinterpret_cast<const uint32_t*>(xr + i);
+            const uint32_t g = *reinterpret_cast<const uint32_t*>(P.shared_gate + i);
+            dot = fmaf(__uint_as_float(v << 16), __uint_as_float(g << 16), dot);
+            dot = fmaf(__uint_as_float(v & 0xffff0000u), __uint_as_float(g & 0xffff0000u), dot);
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
         if (lane == 0) wsp<float>(P, P.L.sg)[t] = 1.0f / (1.0f + expf(-dot));

@@ -145,12 +145,12 @@ __device__ __forceinline__ void row_select(const float* __restrict__ lr, int n, 
     // all loads first (clamped in-row addresses), so they are in flight together
     uint32_t key[PL];
 #pragma unroll
-    for (int i = 0; i < PL; ++i) key[i] = __float_as_uint(lr[min(i * 32 + lane, n - 1)]);
+    for (int i = 0; i < PL; ++i) key[i] = __float_as_uint(__ldcg(lr + min(i * 32 + lane, n - 1)));
     if (mode != NVMOE_ROUTER_SOFTMAX) {
         // sigmoid score plus the selection bias
 #pragma unroll
         for (int i = 0; i < PL; ++i) {
-            const float b = bias ? bias[min(i * 32 + lane, n - 1)] : 0.0f;
+            const float b = bias ? __ldcg(bias + min(i * 32 + lane, n - 1)) : 0.0f;
             key[i] = __float_as_uint(1.0f / (1.0f + expf(-__uint_as_float(key[i]))) + b);
         }
     }
@@ -206,7 +206,7 @@ __device__ __forceinline__ void router_topk_warp(const float* __restrict__ lr, i
         if (mode == NVMOE_ROUTER_SOFTMAX && my_key != 0x007FFFFFu) {
             my_val = __uint_as_float((my_key & 0x80000000u) ? (my_key & 0x7fffffffu) : ~my_key);
         } else {
-            const float l = lr[my_id];
+            const float l = __ldcg(lr + my_id);
             my_val = (mode == NVMOE_ROUTER_SOFTMAX) ? l : 1.0f / (1.0f + expf(-l));
         }
     }
@@ -217,7 +217,7 @@ __device__ __forceinline__ void router_topk_warp(const float* __restrict__ lr, i
     float full_denom = 0.f;
     if (mode == NVMOE_ROUTER_SOFTMAX && !norm_topk) {
         for (int e = lane; e < n_expert; e += 32) {
-            const float l = lr[e];
+            const float l = __ldcg(lr + e);
             if (l == l) full_denom += expf(l - first_val);
         }
 #pragma unroll
@@ -231,14 +231,12 @@ __device__ __forceinline__ void router_topk_warp(const float* __restrict__ lr, i
     } else {
         w = mine ? my_val : 0.f;
     }
-    // sum of the picks in pick order (lane 0 first), identical on every lane; the shuffles are
-    // independent and issue back to back
+    // sum of the picks in pick order (lane 0 first), identical on every lane (a loop: this code
+    // runs once per row, cold in the instruction cache, where fetching an unrolled copy costs
+    // more than the loop)
     float sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-        const float v = __shfl_sync(0xffffffffu, w, j);
-        if (j < top_k) sum += v;
-    }
+#pragma unroll 1
+    for (int j = 0; j < top_k; ++j) sum += __shfl_sync(0xffffffffu, w, j);
     if (mode == NVMOE_ROUTER_SOFTMAX) {
         const float denom = norm_topk ? sum : full_denom;
         w = w / denom * scaling;

@@ -16,8 +16,10 @@
 // tail).  After the wait each warp normalises one token of the block into shared memory (CTAs
 // of the first row block also store h and x); then warp w dots its row with the block's tokens
 // of parity w / 4, two tokens at a time.  The gate matrix is read from HBM once; the token rows
-// are re-read from L2 by each row block.
+// are re-read from L2 by each row block.  With the fused top-k, each CTA counts itself done on
+// its token block (fence, then a ticket); the last one routes the block's tokens, a warp each.
 #include "common.cuh"
+#include "router_device.cuh"
 
 #include <algorithm>
 
@@ -128,9 +130,8 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_
     }
     if (!a.gate_weight) return;
     __syncthreads();
-    if (!has_row) return;
     // tokens of this warp's parity, two at a time (four independent accumulation chains)
-    for (int i = warp >> 2; i < nt; i += 4) {
+    for (int i = warp >> 2; has_row && i < nt; i += 4) {
         const int i2 = i + 2 < nt ? i + 2 : i;
         float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
@@ -163,6 +164,25 @@ __global__ void __launch_bounds__(kGateThreads) router_gate_kernel(nvmoe_router_
                     a.logit_bias ? __fadd_rn(r1, b) : r1;
         }
     }
+    if (a.top_k <= 0) return;
+    // fused top-k: the last CTA done on this token block routes it
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int done = atomicAdd(a.tickets + blockIdx.y, 1);
+        s_last = done == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = warp; i < nt; i += kGateWarps) {
+        const int t = t0 + i;
+        router_topk_warp(a.logits + (int64_t)t * a.logits_row_stride, a.n_expert, a.top_k,
+                         a.router_mode, a.router_bias, a.norm_topk, a.routed_scaling,
+                         a.out_ids + (int64_t)t * a.top_k, a.out_weights + (int64_t)t * a.top_k);
+    }
+    if (threadIdx.x == 0) a.tickets[blockIdx.y] = 0;  // ready for the next call
 }
 
 template <int NCH>
@@ -199,6 +219,11 @@ extern "C" int nvmoe_router_gate(const nvmoe_router_gate_args* a, nvmoe_stream_t
         !rows_ok(a->resid_out, a->resid_out_row_stride) ||
         !rows_ok(a->x_out, a->x_out_row_stride) || !rows_ok(a->gate_weight, a->gate_row_stride) ||
         !rows_ok(a->norm_weight, 0))
+        return NVMOE_ERR_INVALID_ARG;
+    if (a->top_k > 0 &&
+        (!a->gate_weight || a->top_k > kMaxTopK || a->top_k > a->n_expert ||
+         a->n_expert > kMaxExperts || !a->out_ids || !a->out_weights || !a->tickets ||
+         (a->router_mode != NVMOE_ROUTER_SOFTMAX && a->router_mode != NVMOE_ROUTER_SIGMOID_BIAS)))
         return NVMOE_ERR_INVALID_ARG;
     if (a->n_tok == 0) return NVMOE_OK;
     // every CTA reads resid / delta while CTA 0 writes resid_out and x_out: no overlap allowed

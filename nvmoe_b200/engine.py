@@ -196,7 +196,11 @@ class MoEStack:
         b = {"h": torch.empty((L, n_tok, H), dtype=torch.bfloat16, device=d),
              "xn": torch.empty((L, n_tok, H), dtype=torch.bfloat16, device=d),
              "logits": torch.empty((L, n_tok, E), dtype=torch.float32, device=d),
-             "y": torch.empty((L, n_tok, H), dtype=torch.bfloat16, device=d)}
+             "y": torch.empty((L, n_tok, H), dtype=torch.bfloat16, device=d),
+             # the router's picks, written by the gate launch itself (fused top-k)
+             "ids": torch.empty((L, n_tok, c.top_k), dtype=torch.int32, device=d),
+             "w": torch.empty((L, n_tok, c.top_k), dtype=torch.float32, device=d),
+             "tickets": torch.zeros(((n_tok + 7) // 8,), dtype=torch.int32, device=d)}
         b["plans"] = [
             ops.DecodeLayerPlan(self.pools[l], self.tables[l], self.misses_sets[l % 2], n_tok,
                                 c.top_k, shared=self.shared[l], refill=self.banks[l],
@@ -214,7 +218,9 @@ class MoEStack:
                 delta=b["y"][l - 1] if l >= 1 else None,
                 resid_out=b["h"][l] if l >= 1 else None, norm_weight=self.norm_w[l],
                 eps=self.eps, x_out=b["xn"][l],
-                logit_bias=None if self.logit_bias is None else self.logit_bias[l]))
+                logit_bias=None if self.logit_bias is None else self.logit_bias[l],
+                route=(c.top_k, b["ids"][l], b["w"][l], b["tickets"], c.router, self._bias(l),
+                       True, c.routed_scaling)))
         b["gates"] = gates
         self._chain[n_tok] = b
         return b
@@ -224,7 +230,8 @@ class MoEStack:
             h_0 = x;  per layer l: h_l = h_{l-1} + y_{l-1} (l >= 1), xn_l = RMSNorm_l(h_l),
             logits_l = xn_l . gate_l^T + bias_l, y_l = MoE_l(xn_l) (router top-k, slot remap,
             refill, expert FFN, shared expert);  out = h_{L-1} + y_{L-1}.
-        Per layer two calls: nvmoe_router_gate, then nvmoe_decode_layer, which waits for it."""
+        Per layer two calls: nvmoe_router_gate (which also routes: fused top-k), then
+        nvmoe_decode_layer on the routed ids, which waits for it."""
         n = x.shape[0]
         b = self.chain_buffers(n)
         L = self.cfg.n_layers
@@ -239,7 +246,7 @@ class MoEStack:
             else:
                 ga.resid = b["h"][l - 1].data_ptr()
             _lib.check(lib.nvmoe_router_gate(C.byref(ga), s), "nvmoe_router_gate")
-            b["plans"][l](b["xn"][l], b["logits"][l], b["y"][l])
+            b["plans"][l].routed(b["xn"][l], b["ids"][l], b["w"][l], b["y"][l])
         fin = ops.router_gate_args(x if L == 1 else b["h"][L - 1], None, None,
                                    delta=b["y"][L - 1], resid_out=out)
         _lib.check(lib.nvmoe_router_gate(C.byref(fin), s), "nvmoe_router_gate")

@@ -120,7 +120,7 @@ class EPMoEStack:
     The rank keeps, per layer, a slot pool and slot tables over its per = E / world routed
     experts plus its copy of the shared expert (local id per), a pinned host tier of those
     per + 1 experts, and the replicated router gates.  One layer step for n_tok home tokens:
-        nvmoe_router_gate -> nvmoe_router_topk -> nvmoe_ep_dispatch
+        nvmoe_router_gate (with its fused top-k) -> nvmoe_ep_dispatch
         -> exchange (all-to-all of world equal segments)
         -> nvmoe_decode_layer, pre-routed, over the world * n_tok received rows (top_k + 1
            entries each: remap, refill from the host tier, expert FFN)
@@ -164,6 +164,7 @@ class EPMoEStack:
         self.y = z(L, n_tok, H, dt=torch.bfloat16)
         self.ids = z(n_tok, k, dt=torch.int32)
         self.w = z(n_tok, k, dt=torch.float32)
+        self.tickets = torch.zeros(((n_tok + 7) // 8,), dtype=torch.int32, device=d)
         self.send = torch.zeros((world, n_tok, self.row), dtype=torch.uint8, device=d)
         self.recv = torch.zeros((world, n_tok, self.row), dtype=torch.uint8, device=d)
         self.slot_of = z(n_tok, world, dt=torch.int32)
@@ -187,7 +188,8 @@ class EPMoEStack:
                 delta=self.y[l - 1] if l >= 1 else None,
                 resid_out=self.h[l] if l >= 1 else None, norm_weight=st.norm_w[l], eps=eps,
                 x_out=self.xn[l],
-                logit_bias=None if st.logit_bias is None else st.logit_bias[l]))
+                logit_bias=None if st.logit_bias is None else st.logit_bias[l],
+                route=(k, self.ids, self.w, self.tickets, "softmax", None, True, 1.0)))
         self._np = np
 
     # ------------------------------------------------------------ cache state
@@ -207,7 +209,7 @@ class EPMoEStack:
 
     # ------------------------------------------------------------ one layer, in phases
     def phase_dispatch(self, l: int, x: torch.Tensor) -> None:
-        """Router gate (residual add, RMSNorm, gate GEMV), top-k and the dispatch pack of layer
+        """Router gate (residual add, RMSNorm, gate GEMV, top-k) and the dispatch pack of layer
         l; x is the stack's input tokens (read by layers 0 and 1)."""
         from . import _lib, ops
         import ctypes as C
@@ -215,7 +217,6 @@ class EPMoEStack:
         if l <= 1:
             ga.resid, ga.resid_row_stride = x.data_ptr(), x.stride(0)
         _lib.check(_lib.lib().nvmoe_router_gate(C.byref(ga), ops._stream()), "nvmoe_router_gate")
-        ops.router_topk(self.logits[l], self.cfg.top_k, out_ids=self.ids, out_weights=self.w)
         ops.ep_dispatch(self.xn[l], self.ids, self.w, self.cfg.n_experts, self.world, self.rank,
                         self.send, self.slot_of, with_shared=True, status=self.status)
 

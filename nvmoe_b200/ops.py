@@ -82,20 +82,34 @@ def router_gate_args(resid: torch.Tensor, logits: torch.Tensor | None,
                      resid_out: torch.Tensor | None = None,
                      norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
                      x_out: torch.Tensor | None = None,
-                     logit_bias: torch.Tensor | None = None) -> _lib.RouterGateArgs:
-    """C arguments of nvmoe_router_gate over these tensors (bf16 rows, fp32 logits)."""
+                     logit_bias: torch.Tensor | None = None,
+                     route: "tuple | None" = None) -> _lib.RouterGateArgs:
+    """C arguments of nvmoe_router_gate over these tensors (bf16 rows, fp32 logits).  route =
+    (top_k, out_ids [n, k] int32, out_weights [n, k] fp32, tickets int32 (zeroed),
+    mode "softmax" | "sigmoid", router_bias, norm_topk, routed_scaling) fuses the top-k."""
     _require_cuda(resid, logits, gate_weight, delta, resid_out, norm_weight, x_out, logit_bias)
     n, H = resid.shape
     for t in (resid, delta, resid_out, x_out, gate_weight):
         if t is not None:
             assert t.dtype == torch.bfloat16 and t.stride(-1) == 1
     E = 0 if gate_weight is None else gate_weight.shape[0]
-    return _lib.RouterGateArgs(
+    a = _lib.RouterGateArgs(
         resid.data_ptr(), resid.stride(0), _ptr(delta), 0 if delta is None else delta.stride(0),
         _ptr(resid_out), 0 if resid_out is None else resid_out.stride(0), _ptr(norm_weight),
         float(eps), _ptr(x_out), 0 if x_out is None else x_out.stride(0), _ptr(gate_weight),
         0 if gate_weight is None else gate_weight.stride(0), _ptr(logit_bias), _ptr(logits),
         0 if logits is None else logits.stride(0), n, H, E)
+    if route is not None:
+        k, ids, w, tickets, mode, rbias, norm, scaling = route
+        assert ids.is_contiguous() and w.is_contiguous() and tickets.numel() >= (n + 7) // 8
+        a.top_k = k
+        a.router_mode = (_lib.NVMOE_ROUTER_SOFTMAX if mode == "softmax"
+                         else _lib.NVMOE_ROUTER_SIGMOID_BIAS)
+        a.router_bias = _ptr(rbias)
+        a.norm_topk = int(norm)
+        a.routed_scaling = float(scaling)
+        a.out_ids, a.out_weights, a.tickets = ids.data_ptr(), w.data_ptr(), tickets.data_ptr()
+    return a
 
 
 def router_gate(resid: torch.Tensor, gate_weight: torch.Tensor | None,
