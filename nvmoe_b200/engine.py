@@ -201,6 +201,11 @@ class MoEStack:
              "ids": torch.empty((L, n_tok, c.top_k), dtype=torch.int32, device=d),
              "w": torch.empty((L, n_tok, c.top_k), dtype=torch.float32, device=d),
              "tickets": torch.zeros(((n_tok + 7) // 8,), dtype=torch.int32, device=d)}
+        # Routing: above one token block (8 tokens) the gate launch routes its blocks in
+        # parallel (fused top-k, last CTA per block); up to 8 tokens the decode step's front
+        # kernel routes them (a warp per token, overlapped with its table loads), which measured
+        # faster than the gate launch's extra serial tail.
+        b["route_in_gate"] = n_tok > 8
         b["plans"] = [
             ops.DecodeLayerPlan(self.pools[l], self.tables[l], self.misses_sets[l % 2], n_tok,
                                 c.top_k, shared=self.shared[l], refill=self.banks[l],
@@ -220,7 +225,7 @@ class MoEStack:
                 eps=self.eps, x_out=b["xn"][l],
                 logit_bias=None if self.logit_bias is None else self.logit_bias[l],
                 route=(c.top_k, b["ids"][l], b["w"][l], b["tickets"], c.router, self._bias(l),
-                       True, c.routed_scaling)))
+                       True, c.routed_scaling) if b["route_in_gate"] else None))
         b["gates"] = gates
         self._chain[n_tok] = b
         return b
@@ -230,8 +235,8 @@ class MoEStack:
             h_0 = x;  per layer l: h_l = h_{l-1} + y_{l-1} (l >= 1), xn_l = RMSNorm_l(h_l),
             logits_l = xn_l . gate_l^T + bias_l, y_l = MoE_l(xn_l) (router top-k, slot remap,
             refill, expert FFN, shared expert);  out = h_{L-1} + y_{L-1}.
-        Per layer two calls: nvmoe_router_gate (which also routes: fused top-k), then
-        nvmoe_decode_layer on the routed ids, which waits for it."""
+        Per layer two calls: nvmoe_router_gate (which also routes batches above 8 tokens: fused
+        top-k), then nvmoe_decode_layer (routing smaller batches itself), which waits for it."""
         n = x.shape[0]
         b = self.chain_buffers(n)
         L = self.cfg.n_layers
@@ -246,7 +251,10 @@ class MoEStack:
             else:
                 ga.resid = b["h"][l - 1].data_ptr()
             _lib.check(lib.nvmoe_router_gate(C.byref(ga), s), "nvmoe_router_gate")
-            b["plans"][l].routed(b["xn"][l], b["ids"][l], b["w"][l], b["y"][l])
+            if b["route_in_gate"]:
+                b["plans"][l].routed(b["xn"][l], b["ids"][l], b["w"][l], b["y"][l])
+            else:
+                b["plans"][l](b["xn"][l], b["logits"][l], b["y"][l])
         fin = ops.router_gate_args(x if L == 1 else b["h"][L - 1], None, None,
                                    delta=b["y"][L - 1], resid_out=out)
         _lib.check(lib.nvmoe_router_gate(C.byref(fin), s), "nvmoe_router_gate")

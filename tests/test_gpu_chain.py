@@ -35,8 +35,9 @@ def _ulp_gap(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return np.abs(a.astype(np.int32) - b.astype(np.int32))
 
 
-@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("batch", [1, 8, 20])
 def test_dependent_stack_matches_oracle_stage_by_stage(cuda_device, batch):
+    """(batch 20: the gate launch routes its three token blocks itself, fused top-k)"""
     L = 3
     stack = MoEStack(StackConfig(n_layers=L), device=cuda_device, seed=31)
     f = torch.from_numpy((2.0 ** (np.arange(E) % 5 - 2.0)).astype(np.float32))
