@@ -705,22 +705,33 @@ def run_prefill(a, dev, peaks):
     ms = e0.elapsed_time(e1) / n
     flop = 6.0 * T * (k + 1) * H * I
     tf = flop / (ms / 1e3) / 1e12
-    bf16 = peaks["bf16_tflops"] if peaks else 1590.0
-    del pool, shared
+    del shared
     fp4 = os.environ.get("NVMOE_PREFILL_KERNEL", "fp4") != "f16"
+    # HBM floor of the layer: the distinct experts' banks (+ tokens in, y out)
+    n_used = int(torch.unique(ids).numel()) + 1
+    floor_bytes = n_used * pool.bytes_per_slot + 2 * T * H * 2
+    hbm = peaks["hbm_gbs"] if peaks else 6650.0
     out = {"tokens": T, "ms_per_layer": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
-           "algorithmic_tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / bf16, 4),
-           "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback"}
+           "algorithmic_tflops": round(tf, 1),
+           "hbm_floor_ms": round(floor_bytes / (hbm * 1e9) * 1e3, 4),
+           "frac_of_hbm_floor": round(floor_bytes / (hbm * 1e9) * 1e3 / ms, 4),
+           "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback"}
     if fp4:
         # the activations enter the MMA as FP4_TERMS residual NVFP4 terms: the tensor cores do
-        # FP4_TERMS x the algorithmic products; no FP4 peak is measured, 9 PFLOP/s is nominal
+        # FP4_TERMS x the algorithmic products; the FP4 peak is this GPU's measured mxf4nvf4 rate
+        # at the kernel's MMA shape (nvmoe_probe_fp4_mma), the nominal 9 PFLOP/s beside it
         mma_tf = tf * FP4_TERMS
+        fp4_peak = ops.fp4_mma_tflops(device=dev)
         out.update({"kernel": "tcgen05 kind::mxf4nvf4 block-scaled FP4 grouped GEMM (weights "
                               "unchanged from the slot banks, activations as %d NVFP4 terms)" % FP4_TERMS,
                     "mma_tflops_fp4": round(mma_tf, 1),
+                    "fp4_peak_measured_tflops": round(fp4_peak, 1),
+                    "frac_of_fp4_measured": round(mma_tf / fp4_peak, 4),
+                    "algorithmic_frac_of_fp4_measured": round(tf / fp4_peak, 4),
                     "frac_of_fp4_nominal_dense": round(mma_tf / FP4_NOMINAL_TFLOPS, 4)})
     else:
         out["kernel"] = "tcgen05 kind::f16 grouped GEMM, weights dequantised into tensor memory"
+    del pool
     return out
 
 

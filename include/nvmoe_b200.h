@@ -472,6 +472,15 @@ typedef struct nvmoe_ep_combine_args {
 } nvmoe_ep_combine_args;
 int nvmoe_ep_combine(const nvmoe_ep_combine_args* args, nvmoe_stream_t stream);
 
+/* ================================================================ diagnostics
+ * Block-scaled FP4 tensor-core throughput probe: n_ctas CTAs (at most one per SM) each issue
+ * n_iter x 8 tcgen05.mma kind::mxf4nvf4.block16 instructions of the prefill kernel's shape
+ * (M 128, N 128, K 64; 2 x 128 x 128 x 64 flops each) on zero operands, back to back; time the
+ * launch with events on `stream` for the device's FP4 MMA rate.  status (optional device int)
+ * receives NVMOE_ERR_TIMEOUT if the final completion wait gives up.  No counterpart in the
+ * reference. */
+int nvmoe_probe_fp4_mma(int n_iter, int n_ctas, int32_t* status, nvmoe_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

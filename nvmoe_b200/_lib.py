@@ -284,6 +284,7 @@ SIGNATURES = {
     "nvmoe_ep_row_bytes": (C.c_size_t, [C.c_int, C.c_int]),
     "nvmoe_ep_dispatch": (C.c_int, [C.POINTER(EpDispatchArgs), C.c_void_p]),
     "nvmoe_ep_combine": (C.c_int, [C.POINTER(EpCombineArgs), C.c_void_p]),
+    "nvmoe_probe_fp4_mma": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
 }
 
 _lock = threading.Lock()

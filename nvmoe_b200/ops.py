@@ -569,3 +569,26 @@ def ep_combine(back: torch.Tensor, slot_of: torch.Tensor, out: torch.Tensor) -> 
                            out.stride(0))
     check(lib().nvmoe_ep_combine(C.byref(a), _stream()), "nvmoe_ep_combine")
     return out
+
+
+# ------------------------------------------------------------------ diagnostics
+def fp4_mma_tflops(n_iter: int = 4096, reps: int = 3, device=None) -> float:
+    """This GPU's block-scaled FP4 MMA rate (TFLOP/s) at the prefill kernel's MMA shape
+    (nvmoe_probe_fp4_mma on every SM, CUDA events, best of reps)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    flop = float(sms) * n_iter * 8 * 2.0 * 128 * 128 * 64
+    check(lib().nvmoe_probe_fp4_mma(64, sms, st.data_ptr(), _stream()), "nvmoe_probe_fp4_mma")
+    best = 0.0
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        check(lib().nvmoe_probe_fp4_mma(n_iter, sms, st.data_ptr(), _stream()),
+              "nvmoe_probe_fp4_mma")
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, flop / (e0.elapsed_time(e1) / 1e3) / 1e12)
+    if int(st.item()) != 0:
+        raise _lib.NvmoeError(int(st.item()), "nvmoe_probe_fp4_mma")
+    return best

@@ -359,3 +359,10 @@ def test_refill_async_and_gather_byte_exact(cuda_device):
     for e, s in zip(h["miss_ids"], h["miss_slots"]):
         assert torch.equal(gpu.gate_up.data[s].cpu(), host.gate_up.data[e])
         assert torch.equal(gpu.down.scale[s].cpu(), host.down.scale[e])
+
+
+def test_fp4_mma_probe_rate_is_sane(cuda_device):
+    """nvmoe_probe_fp4_mma completes (bounded wait, status 0) and measures a block-scaled FP4
+    MMA rate between 1 and 12 PFLOP/s (B200 nominal dense FP4: 9 PFLOP/s)."""
+    tf = ops.fp4_mma_tflops(n_iter=1024, reps=2, device=cuda_device)
+    assert 1000.0 < tf < 12000.0, tf
