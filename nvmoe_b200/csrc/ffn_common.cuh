@@ -145,7 +145,6 @@ struct FfnParams {
     int32_t* status;
     int grp_tok;           // entries per token group: min(8, n_tok), at least 1
     const uint32_t* aux_table;  // the format's lookup table in device memory (IQ2_XXS grid)
-    int ypart_smem;        // 1: the down phase keeps y_part in shared memory
     int kernel;            // enum nvmoe_kernel of the call
     int use_fp4;           // 1: the block-scaled FP4 tensor-core kernel runs this call (NVFP4)
     int spare_sm;          // 1: the FFN grid leaves one SM free (for the next layer's front)
@@ -163,6 +162,51 @@ __device__ __forceinline__ float global_of(const nvmoe_matrix_bank& b, int slot)
 }
 // The same load issued where it stands (not sunk to its first use), for a value needed only at
 // the end of a long stretch of work.
+// The fields of one matrix bank of the routed pool (sh = 0) or of the shared expert's pool
+// (sh = 1), each read at its fixed place in the kernel parameters and then selected as a value
+// (selp in inline assembly, so that the choice cannot become a runtime-indexed read of the
+// parameter block, which is a memory load on the critical path of a single-lane producer).
+struct BankSel {
+    const uint8_t* data;
+    int64_t slot_stride, row_stride;
+    const uint8_t* scale;
+    int64_t scale_slot_stride, scale_row_stride;
+    const float* global_scale;
+    int64_t global_stride;
+};
+__device__ __forceinline__ int64_t sel64(int c, int64_t a, int64_t b) {  // c ? b : a
+    int64_t r;
+    asm("{ .reg .pred p; setp.ne.s32 p, %3, 0; selp.b64 %0, %2, %1, p; }"
+        : "=l"(r)
+        : "l"(a), "l"(b), "r"(c));
+    return r;
+}
+template <typename T>
+__device__ __forceinline__ T* selp_ptr(int c, T* a, T* b) {
+    return reinterpret_cast<T*>(sel64(c, reinterpret_cast<int64_t>(a), reinterpret_cast<int64_t>(b)));
+}
+__device__ __forceinline__ BankSel bank_sel(int sh, const nvmoe_matrix_bank& a,
+                                            const nvmoe_matrix_bank& b) {
+    BankSel r;
+    r.data = selp_ptr(sh, static_cast<const uint8_t*>(a.data), static_cast<const uint8_t*>(b.data));
+    r.slot_stride = sel64(sh, a.slot_stride, b.slot_stride);
+    r.row_stride = sel64(sh, a.row_stride, b.row_stride);
+    r.scale = selp_ptr(sh, static_cast<const uint8_t*>(a.scale), static_cast<const uint8_t*>(b.scale));
+    r.scale_slot_stride = sel64(sh, a.scale_slot_stride, b.scale_slot_stride);
+    r.scale_row_stride = sel64(sh, a.scale_row_stride, b.scale_row_stride);
+    r.global_scale = selp_ptr(sh, a.global_scale, b.global_scale);
+    r.global_stride = sel64(sh, a.global_stride, b.global_stride);
+    return r;
+}
+// the slot's global scale (1 without a global-scale bank), read through L2
+__device__ __forceinline__ float global_of_sel(const BankSel& b, int slot) {
+    if (!b.global_scale) return 1.0f;
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];"
+                 : "=f"(v)
+                 : "l"(b.global_scale + (int64_t)slot * b.global_stride));
+    return v;
+}
 __device__ __forceinline__ float global_of_early(const nvmoe_matrix_bank& b, int slot) {
     if (!b.global_scale) return 1.0f;
     float v;

@@ -11,15 +11,16 @@
 //           groups of <= 8 entries with complete group records (ffn_common.cuh); the fused
 //           decode front kernel does the same work in the engine path
 //   fused — persistent, one CTA per SM, warp-specialised: a producer warp streams gate_up work
-//           items (token group x 16 rows of gate and of up) and then down slabs (16 rows of a
-//           CTA's output tile for every group) with 1-D bulk copies (TMA) into two rings of
-//           shared-memory stages; 8 MMA warps dequantise A fragments in registers from the
-//           staged bytes and run m16n8k16 f16 MMAs (fp32 accumulate); an epilogue warp sums the
-//           gate_up partials of the 8 warps, stores h = silu(g) * u (f16) and publishes each
-//           finished row tile on a per-group counter; the down phase starts a group once its
-//           counter is complete, writes w * down(h) per entry into shared memory, and each CTA
-//           finally sums the entries of each token in the fixed order j = 0..k-1, shared, and
-//           stores bf16 y.  No atomics on data, deterministic.
+//           items (token group x 16 rows of gate and of up) and then down units (up to 64 rows
+//           of H of one group) with 1-D bulk copies (TMA) into two rings of shared-memory
+//           stages; 8 MMA warps dequantise A fragments in registers from the staged bytes and
+//           run m16n8k16 f16 MMAs (fp32 accumulate); an epilogue warp sums the gate_up partials
+//           of the 8 warps and stores h = silu(g) * u (f16); the down producer publishes each
+//           finished row tile on a per-group counter; a down unit starts once its group's
+//           counter is complete and writes w * down(h) per entry into y_part; after a grid-wide
+//           count of finished units every CTA sums its share of y over each token's entries in
+//           the fixed order j = 0..k-1, shared, and stores bf16 y.  No atomics on data,
+//           deterministic.
 // Only the slots that occur in slot_ids are read; every weight byte is read once per call.
 #include "common.cuh"
 #include "dequant_frag.cuh"
@@ -159,28 +160,31 @@ __device__ __forceinline__ void bulk_rows(uint8_t* dst, const uint8_t* src, int 
 
 // ------------------------------------------------------------------ 2. fused gate_up + down
 // Shared memory: [gate_up ring][resident x][down ring][red: 2 x 8 warps x 32 lanes x 8
-// floats][meta: 2 x 8 ints][y_part (optional)][mbarriers].  Once the gate_up phase has drained,
+// floats][meta: 2 x 8 ints, publication ring][mbarriers].  Once the gate_up phase has drained,
 // its ring's bytes hold further down stages.
 //   gate_up stage: [record 128 B] gate codes [16][H/2] | up codes | gate scales [16][H/16] |
 //                  up scales | x [XT][H + 8] f16 when x is staged per item (XT = the largest
 //                  group of this launch; the 8 extra halves per row only spread the rows over
 //                  the banks); resident x: [n_tok][H + 8] f16 once per CTA (n_tok <= 8)
-//   down stage   : [record 128 B] codes [16][I/2] | scales [16][I/16]
+//   down stage   : [record 128 B] codes [dn_rows][I/2] | scales [dn_rows][I/16]
 struct FusedLayout {
     int stage_gu, stage_dn;  // bytes per stage
     int nst_gu;              // gate_up ring stages
-    int nst_dn;              // down stages in their own region (a multiple of 8)
+    int nst_dn;              // down stages in their own region (a multiple of the warp groups)
     int nst_dn_ext;          // down stages carved from the gate_up ring once it has drained
+    int dn_rows;             // rows of H per down unit (64, 32 or 16: 16 per MMA warp)
     int xt;                  // x rows per gate_up stage (staged x), 0 with resident x
     int x_res;               // 1: every token row resident in shared memory, loaded once
-    int off_x, off_dn, off_red, off_meta, off_yp, off_bar, total;
+    int off_x, off_dn, off_red, off_meta, off_bar, total;
     int off_aux;             // the format's lookup table (IQ2_XXS grid)
 };
 
 __host__ __device__ inline int round128(int v) { return (v + 127) / 128 * 128; }
 
 // One 128-wide K tile of a 16-row gate + up item: rows g and g + 8 of both matrices for the
-// lane quarter q, B = the activations of the group's tokens (token g of the lane).
+// lane quarter q, B = the activations of the group's tokens (token g of the lane).  Lanes past
+// the group's tokens load some valid row: their output columns are never stored, and loads
+// without a condition keep the tile straight-line code.
 // The MMAs of consecutive steps go to kAcc independent accumulators (a single accumulator
 // chains every mma.sync on the previous one's result and leaves the warp latency-bound); the
 // accumulators are summed in a fixed order at the end of the item.
@@ -190,7 +194,7 @@ template <typename Fmt>
 __device__ __forceinline__ void gate_up_tile(const uint8_t* gcode, const uint8_t* ucode,
                                              const uint8_t* gsc, const uint8_t* usc, int cb,
                                              int sb, const uint32_t* aux, const __half* xs,
-                                             bool has_tok, int k0,
+                                             int k0,
                                              int g, int q, float (&accg)[kAcc][4],
                                              float (&accu)[kAcc][4]) {
     typename Fmt::Row ga, gb, ua, ub;
@@ -200,8 +204,7 @@ __device__ __forceinline__ void gate_up_tile(const uint8_t* gcode, const uint8_t
     Fmt::load_smem(ub, ucode + (g + 8) * cb, usc + (g + 8) * sb, k0, q, aux);
 #pragma unroll
     for (int s2 = 0; s2 < Fmt::kSteps; s2 += 2) {
-        const uint4 xb = has_tok ? *reinterpret_cast<const uint4*>(xs + k0 + Fmt::kofs(q, s2))
-                                 : make_uint4(0, 0, 0, 0);
+        const uint4 xb = *reinterpret_cast<const uint4*>(xs + k0 + Fmt::kofs(q, s2));
 #pragma unroll
         for (int ss = 0; ss < 2; ++ss) {
             uint32_t ag[4], au[4];
@@ -247,25 +250,51 @@ __device__ __forceinline__ void fold_acc(float (&acc)[kAcc][4]) {
         for (int v = 0; v < 4; ++v) acc[0][v] += acc[a][v];
 }
 
-// h fragments of one K tile for token row hrow (null: no token -> zeros), in the order of the
-// format's step pairs, read through L2 (h is written by other CTAs of this grid).
+// h fragments of one K tile for token row hrow, in the order of the format's step pairs, read
+// through L2 (h is written by other CTAs of this grid).
 template <typename Fmt>
 __device__ __forceinline__ void load_h_tile(const __half* hrow, int k0, int q,
                                             uint4 (&hb)[Fmt::kSteps / 2]) {
 #pragma unroll
     for (int i = 0; i < Fmt::kSteps / 2; ++i)
-        hb[i] = hrow ? __ldcg(reinterpret_cast<const uint4*>(hrow + k0 + Fmt::kofs(q, 2 * i)))
-                     : make_uint4(0, 0, 0, 0);
+        hb[i] = __ldcg(reinterpret_cast<const uint4*>(hrow + k0 + Fmt::kofs(q, 2 * i)));
 }
 
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
     int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
-    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
+__device__ __forceinline__ void red_relaxed_gpu_add(int* p, int v) {
+    asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_cta(int* p, int v) {
+    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta(const int* p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_relaxed_cta(const int* p) {
+    int v;
+    asm volatile("ld.relaxed.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+
+// Publication of finished h row tiles.  The epilogue warp stores a gate_up item's h rows and
+// hands the item's group to the down producer warp through a ring in shared memory (release /
+// acquire at CTA scope); the down producer publishes everything handed over so far with one
+// gpu-scope fence and one relaxed count per item.  The fence waits until the stores have
+// reached L2 (about a microsecond under the weight stream), so it runs on the warp that is not
+// on the gate_up critical path, and it covers every item stored meanwhile.
+//   pub[0] items handed over, pub[1] items published, pub[2] items the epilogue finished with
+//   (-1 while it runs), pub[4 + i % kPubRing] the group of item i
+constexpr int kPubRing = 32;
+constexpr int kPubInts = 4 + kPubRing;
 
 // Bounded wait until the group's h rows are complete (all I/16 gate/up row tiles stored).
 
@@ -291,29 +320,40 @@ __device__ __forceinline__ void shfl_record(int4 (&dst)[kDescInts / 4],
 }
 
 constexpr int kCW = kConsumerWarps;       // MMA warps
+// Hardware warp of each role: the 8 MMA warps are warps 0-7 (index mw = warp), then the
+// control warps.
 constexpr int kProdGU = kCW;              // bulk-copy producer of the gate_up items
 constexpr int kEpiWarp = kCW + 1;         // gate/up cross-warp sum + SwiGLU + h store
-constexpr int kProdDN = kCW + 2;          // bulk-copy producer of the down slabs
+constexpr int kProdDN = kCW + 2;          // bulk-copy producer of the down units; publisher
 constexpr int kRefillWarp = kCW + 3;      // copies this call's misses in from the host tier
 constexpr int kFusedThreads = (kCW + 4) * 32;
 
 // Persistent expert FFN, one CTA per SM.  CTA c runs
 //   gate_up items c, c + G, ... (item = token group x 16 rows of gate and of up, full K = H),
-//   then down row tiles r = G - 1 - c, 2G - 1 - c, ... (16 rows of y over every group, K = I).
+//   then down units c, c + G, ... (unit = dn_rows rows of H of one group, K = I), numbered
+//   group-major so that the groups whose h completes first come first, then its share of y.
 // Roles: two producer warps stream the two phases' weights into their rings (down weights do
 // not depend on h, so they are in flight while gate_up runs); the 8 MMA warps split K of a
 // gate_up item (TPW tiles each, straight-line code) and hand their partial sums to the
 // epilogue warp through a 2-deep ring, so they never wait for the cross-warp sum; the epilogue
-// warp stores h and counts the group's finished row tiles (release); a down MMA warp owns whole
-// groups and starts a group once its count is complete (acquire).
+// warp stores h and hands the item to the down producer warp, which counts the group's
+// finished row tiles (fence, then relaxed counts); a down MMA warp owns whole groups and starts
+// a group once its count is complete (acquire).
 template <typename Fmt, int TPW, int TD>
 __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, FusedLayout FL) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int H = P.pool.hidden, I = P.pool.inter;
+    // With compile-time K tiles (TPW, TD > 0) the host has checked H = TPW x 8 warps x tile and
+    // I = TD x tile, so H, I and every row stride and offset inside a stage are constants: the
+    // tile loops then address shared memory with immediate offsets (runtime strides measured
+    // almost twice as slow in the gate_up tile).
+    const int H = TPW > 0 ? TPW * kCW * Fmt::kWarpTileK : P.pool.hidden;
+    const int I = TD > 0 ? TD * Fmt::kWarpTileK : P.pool.inter;
     const int G = gridDim.x;
     // (the down producer gives each ring stage to one lane: at most 32 stages are used)
-    const int NGU = FL.nst_gu, NDT = min(FL.nst_dn + FL.nst_dn_ext, 32);
+    const int NGU = FL.nst_gu, NDT = FL.nst_dn + FL.nst_dn_ext;
+    // down units: dn_rows rows of H of one group; its dn_rows / 16 MMA warps form a warp group
+    const int dn_rows = FL.dn_rows, wpu = dn_rows / 16, n_wg = kCW / wpu;
     uint64_t* gu_full = reinterpret_cast<uint64_t*>(smem + FL.off_bar);
     uint64_t* gu_empty = gu_full + NGU;
     uint64_t* dn_full = gu_empty + NGU;
@@ -324,9 +364,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     uint64_t* gu_drained = x_full + 1;
     float* red = reinterpret_cast<float*>(smem + FL.off_red);
     int* meta = reinterpret_cast<int*>(smem + FL.off_meta);
+    int* pub = meta + 16;
     if (tid == 0) {
+        pub[0] = 0, pub[1] = 0, pub[2] = -1;
         for (int s = 0; s < NGU; ++s) mbar_init(&gu_full[s], 1), mbar_init(&gu_empty[s], kCW);
-        for (int s = 0; s < NDT; ++s) mbar_init(&dn_full[s], 1), mbar_init(&dn_empty[s], 1);
+        for (int s = 0; s < NDT; ++s) mbar_init(&dn_full[s], 1), mbar_init(&dn_empty[s], wpu);
         for (int s = 0; s < 2; ++s) mbar_init(&red_full[s], kCW), mbar_init(&red_empty[s], 1);
         mbar_init(x_full, 1);
         mbar_init(gu_drained, kCW);
@@ -340,12 +382,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     grid_dep_wait();
     grid_dep_launch();
 
-    const int tiles_i = I / 16, n_dn = H / 16;
+    const int tiles_i = I / 16, nb = H / dn_rows;
     const int cbg = Fmt::code_bytes(H), sbg = Fmt::scale_bytes(H);
     const int cbd = Fmt::code_bytes(I), sbd = Fmt::scale_bytes(I);
     const int og_uc = kStageHdr + 16 * cbg, og_gs = kStageHdr + 32 * cbg;
     const int og_us = og_gs + 16 * sbg, og_x = og_us + 16 * sbg;
-    const int od_sc = kStageHdr + 16 * cbd;
+    const int od_sc = kStageHdr + dn_rows * cbd;
     const int xrow = H * 2 + kXPad;  // bytes between x rows in shared memory
     const __half* x16 = wsp<__half>(P, P.L.x16);
     __half* h16 = wsp<__half>(P, P.L.h16);
@@ -399,31 +441,29 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                         }
                         hdr[GD_RT] = item % tiles_i;
                         hdr[GD_GID] = item / tiles_i;
-                        const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
+                        const int sh = hdr[GD_POOL];
+                        const BankSel bg = bank_sel(sh, P.pool.gate, P.shared.gate);
+                        const BankSel bu = bank_sel(sh, P.pool.up, P.shared.up);
                         const int slot = hdr[GD_SLOT], nt = hdr[GD_NT];
                         const int64_t r0 = (int64_t)(item % tiles_i) * 16;
                         mbar_arrive_expect_tx(
                             &gu_full[st],
                             (uint32_t)(32 * cbg + 32 * sbg + (FL.x_res ? 0 : nt * H * 2)));
                         bulk_rows(stg + kStageHdr,
-                                  (const uint8_t*)pool.gate.data + slot * pool.gate.slot_stride +
-                                      r0 * pool.gate.row_stride,
-                                  16, cbg, pool.gate.row_stride, &gu_full[st]);
+                                  bg.data + slot * bg.slot_stride + r0 * bg.row_stride, 16, cbg,
+                                  bg.row_stride, &gu_full[st]);
                         bulk_rows(stg + og_uc,
-                                  (const uint8_t*)pool.up.data + slot * pool.up.slot_stride +
-                                      r0 * pool.up.row_stride,
-                                  16, cbg, pool.up.row_stride, &gu_full[st]);
+                                  bu.data + slot * bu.slot_stride + r0 * bu.row_stride, 16, cbg,
+                                  bu.row_stride, &gu_full[st]);
                         if (sbg > 0) {  // formats with a separate scale bank
                             bulk_rows(stg + og_gs,
-                                      (const uint8_t*)pool.gate.scale +
-                                          slot * pool.gate.scale_slot_stride +
-                                          r0 * pool.gate.scale_row_stride,
-                                      16, sbg, pool.gate.scale_row_stride, &gu_full[st]);
+                                      bg.scale + slot * bg.scale_slot_stride +
+                                          r0 * bg.scale_row_stride,
+                                      16, sbg, bg.scale_row_stride, &gu_full[st]);
                             bulk_rows(stg + og_us,
-                                      (const uint8_t*)pool.up.scale +
-                                          slot * pool.up.scale_slot_stride +
-                                          r0 * pool.up.scale_row_stride,
-                                      16, sbg, pool.up.scale_row_stride, &gu_full[st]);
+                                      bu.scale + slot * bu.scale_slot_stride +
+                                          r0 * bu.scale_row_stride,
+                                      16, sbg, bu.scale_row_stride, &gu_full[st]);
                         }
                         if (!FL.x_res)
                             for (int n = 0; n < nt; ++n)
@@ -439,10 +479,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     }
 
     if (warp == kProdDN) {
-        // down slabs: for each of this CTA's row tiles, every group's 16 rows; use j of the ring
-        // is (row tile j / n_groups, group j % n_groups) in stage j % NDT.  Lane i owns stage i
-        // and runs its uses i, i + NDT, ... as a state machine of its own, polled without
-        // blocking (a lane that waited in a loop of its own would hold the others back):
+        // down units: unit j of this CTA is u = blockIdx.x + j G (group u / nb, rows
+        // [dn_rows (u % nb), + dn_rows) of H) in stage j % NDT.  Lane i owns stage i and runs its
+        // units i, i + NDT, ... as a state machine of its own, polled without blocking (a lane
+        // that waited in a loop of its own would hold the others back):
         //   the gate_up ring drained (stages in its bytes) -> stage free -> missed slot's banks
         //   in -> rows requested (expect_tx, bulk copies) -> the group's h complete: down global
         //   scale and shared-expert gates into the stage's record copy, arrive (the MMA warp
@@ -450,50 +490,67 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
         enum { S_DRAIN, S_FREE, S_REFILL, S_ISSUE, S_H, S_DONE };
         const int n_groups = __ldcg(hdr_g + HDR_N_GROUPS);
         const float* sgate = (P.has_shared && P.shared_gate) ? wsp<float>(P, P.L.sg) : nullptr;
-        const int rt0 = G - 1 - (int)blockIdx.x;
-        const int n_rt = rt0 < n_dn ? (n_dn - 1 - rt0) / G + 1 : 0;
-        const int total = n_rt * n_groups;
+        const int n_units = n_groups * nb;
+        const int total = (int)blockIdx.x < n_units ? (n_units - 1 - (int)blockIdx.x) / G + 1 : 0;
+        auto group_of = [&](int jj) { return ((int)blockIdx.x + jj * G) / nb; };
         int j = lane;
         int state = (lane >= NDT || j >= total) ? S_DONE : (lane >= FL.nst_dn ? S_DRAIN : S_FREE);
         uint8_t* stg = dn_stage(lane < NDT ? lane : 0);
         int* hdr = reinterpret_cast<int*>(stg);
         int4 r[kDescInts / 4];
-        if (state != S_DONE) load_record(P, j % n_groups, r);
+        if (state != S_DONE) load_record(P, group_of(j), r);
         float dgl = 1.f;
         bool ok = true;
-        for (uint32_t w = 0; __any_sync(0xffffffffu, state != S_DONE); ++w) {
-            if (w == (1u << 24)) {  // about a second: give up
-                if (state != S_DONE) {
+        unsigned backoff = 32;
+        int published = 0;
+        bool pub_open = lane == 0;  // lane 0 publishes the epilogue's items until it finishes
+        for (uint32_t w = 0; __any_sync(0xffffffffu, state != S_DONE || pub_open); ++w) {
+            if (w == (1u << 24)) {  // a few seconds: give up
+                if (state != S_DONE || pub_open) {
                     report_timeout(P);
                     ok = false;
                 }
                 break;
             }
+            const int state0 = state;
+            bool moved = false;
+            if (pub_open) {
+                const int fin = ld_acquire_cta(pub + 2);  // (read before the count)
+                const int handed = ld_acquire_cta(pub);
+                if (handed > published) {
+                    fence_acq_rel_gpu();
+                    for (int i = published; i < handed; ++i)
+                        red_relaxed_gpu_add(done + pub[4 + i % kPubRing], 1);
+                    published = handed;
+                    st_release_cta(pub + 1, published);
+                    moved = true;
+                }
+                if (fin >= 0 && published >= fin) pub_open = false;
+            }
             if (state == S_DRAIN && mbar_test_wait(gu_drained, 0)) state = S_FREE;
             if (state == S_FREE && mbar_test_wait(&dn_empty[lane], ((j / NDT) & 1) ^ 1)) {
                 copy_record(hdr, r);
-                hdr[GD_GID] = j % n_groups;
+                hdr[GD_GID] = group_of(j);
                 state = hdr[GD_MISS] > 0 ? S_REFILL : S_ISSUE;
             }
             if (state == S_REFILL && refill_ready(P, hdr[GD_MISS] - 1, 1)) state = S_ISSUE;
             if (state == S_ISSUE) {
-                const nvmoe_expert_pool& pool = hdr[GD_POOL] ? P.shared : P.pool;
+                const BankSel bd = bank_sel(hdr[GD_POOL], P.pool.down, P.shared.down);
                 const int slot = hdr[GD_SLOT];
-                const int64_t r0 = (int64_t)(rt0 + (j / n_groups) * G) * 16;
-                dgl = global_of_early(pool.down, slot);
-                mbar_expect_tx(&dn_full[lane], (uint32_t)(16 * (cbd + sbd)));
-                bulk_rows(stg + kStageHdr,
-                          (const uint8_t*)pool.down.data + slot * pool.down.slot_stride +
-                              r0 * pool.down.row_stride,
-                          16, cbd, pool.down.row_stride, &dn_full[lane]);
+                const int64_t r0 = (int64_t)(((int)blockIdx.x + j * G) % nb) * dn_rows;
+                dgl = global_of_sel(bd, slot);
+                mbar_expect_tx(&dn_full[lane], (uint32_t)(dn_rows * (cbd + sbd)));
+                bulk_rows(stg + kStageHdr, bd.data + slot * bd.slot_stride + r0 * bd.row_stride,
+                          dn_rows, cbd, bd.row_stride, &dn_full[lane]);
                 if (sbd > 0)
                     bulk_rows(stg + od_sc,
-                              (const uint8_t*)pool.down.scale + slot * pool.down.scale_slot_stride +
-                                  r0 * pool.down.scale_row_stride,
-                              16, sbd, pool.down.scale_row_stride, &dn_full[lane]);
+                              bd.scale + slot * bd.scale_slot_stride + r0 * bd.scale_row_stride,
+                              dn_rows, sbd, bd.scale_row_stride, &dn_full[lane]);
                 state = S_H;
             }
-            if (state == S_H && ld_acquire_gpu(done + j % n_groups) >= tiles_i) {
+            // (relaxed polls; the acquire is one fence once the count is complete)
+            if (state == S_H && ld_relaxed_gpu(done + group_of(j)) >= tiles_i) {
+                fence_acq_rel_gpu();
                 hdr[GD_DGLOB] = __float_as_int(dgl);
                 if (hdr[GD_POOL] && sgate) {
                     const int nt = hdr[GD_NT];
@@ -504,11 +561,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 j += NDT;
                 state = S_DONE;
                 if (j < total) {
-                    load_record(P, j % n_groups, r);  // (used once the stage is free again)
+                    load_record(P, group_of(j), r);  // (used once the stage is free again)
                     state = S_FREE;
                 }
             }
-            if (w > 8) __nanosleep(32);
+            // back off while no lane moves (most of the gate_up phase: every lane waits for h)
+            if (__any_sync(0xffffffffu, state != state0 || moved)) {
+                backoff = 32;
+            } else if (w > 8) {
+                __nanosleep(backoff);
+                backoff = min(2 * backoff, 256);
+            }
         }
         (void)ok;
         return;
@@ -518,7 +581,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     const int n_gu = n_groups * tiles_i;
 
     if (warp == kEpiWarp) {
-        // ---- gate_up epilogue: sum the 8 warps' partials in warp order, h = silu(g) * u
+        // ---- gate_up epilogue: sum the 8 warps' partials in warp order, h = silu(g) * u, then
+        // hand the item to the down producer for publication
         int it = 0;
         for (int item = blockIdx.x; item < n_gu; item += G, ++it) {
             const int rs = it & 1;
@@ -549,12 +613,30 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                         __float2half_rn(silu(sg[v] * gglob) * (su[v] * uglob));
             }
             __syncwarp();
-            if (lane == 0) red_release_gpu_add(done + gid, 1);
+            int ring_ok = 1;
+            if (lane == 0) {
+                // a free ring entry: the publisher is less than kPubRing items behind
+                for (uint32_t i = 0; it - ld_relaxed_cta(pub + 1) >= kPubRing; ++i) {
+                    if (i == (1u << 22)) {
+                        report_timeout(P);
+                        ring_ok = 0;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+                if (ring_ok) {
+                    pub[4 + it % kPubRing] = gid;
+                    st_release_cta(pub, it + 1);  // (orders the warp's h stores before it)
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, ring_ok, 0)) break;
         }
+        if (lane == 0) st_release_cta(pub + 2, it);
         return;
     }
 
-    // ---------------- MMA warps
+    // ---------------- MMA warps (mw = 0..7, ctid = this thread's index among the MMA threads)
+    const int mw = warp, ctid = tid;
     const int g = lane >> 2, q = lane & 3;
     bool ok = true;
     {
@@ -577,26 +659,27 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 mv[0] = hdr[GD_E0], mv[1] = hdr[GD_NT], mv[2] = hdr[GD_RT], mv[3] = hdr[GD_GID];
                 {  // the slot's global scales from the pool itself: a refill between the
                    // grouping and this kernel may have replaced the slot's expert
-                    const nvmoe_expert_pool& pl = hdr[GD_POOL] ? P.shared : P.pool;
-                    mv[4] = __float_as_int(global_of_early(pl.gate, hdr[GD_SLOT]));
-                    mv[5] = __float_as_int(global_of_early(pl.up, hdr[GD_SLOT]));
+                    const int sh = hdr[GD_POOL], slot = hdr[GD_SLOT];
+                    mv[4] = __float_as_int(global_of_sel(bank_sel(sh, P.pool.gate, P.shared.gate), slot));
+                    mv[5] = __float_as_int(global_of_sel(bank_sel(sh, P.pool.up, P.shared.up), slot));
                 }
                 const bool has_tok = g < mv[1];
-                // B rows: the resident row of the lane's token, or the staged row g
-                const uint8_t* xb = FL.x_res ? smem + FL.off_x + (has_tok ? hdr[GD_TOK + g] : 0) * xrow
-                                             : stg + og_x + g * xrow;
+                // B rows: the resident row of the lane's token, or the staged row g (lanes
+                // without a token: the row of the group's first token)
+                const uint8_t* xb = FL.x_res ? smem + FL.off_x + hdr[GD_TOK + (has_tok ? g : 0)] * xrow
+                                             : stg + og_x + (has_tok ? g : 0) * xrow;
                 const __half* xs = reinterpret_cast<const __half*>(xb);
                 if constexpr (TPW > 0) {
 #pragma unroll
                     for (int t = 0; t < TPW; ++t)
                         gate_up_tile<Fmt>(stg + kStageHdr, stg + og_uc, stg + og_gs, stg + og_us,
-                                          cbg, sbg, aux, xs, has_tok, (warp * TPW + t) * Fmt::kWarpTileK,
+                                          cbg, sbg, aux, xs, (mw * TPW + t) * Fmt::kWarpTileK,
                                           g, q, accg, accu);
                 } else {
                     const int kw = H / kCW;
-                    for (int k0 = warp * kw; k0 < (warp + 1) * kw; k0 += Fmt::kWarpTileK)
+                    for (int k0 = mw * kw; k0 < (mw + 1) * kw; k0 += Fmt::kWarpTileK)
                         gate_up_tile<Fmt>(stg + kStageHdr, stg + og_uc, stg + og_gs, stg + og_us,
-                                          cbg, sbg, aux, xs, has_tok, k0, g, q, accg, accu);
+                                          cbg, sbg, aux, xs, k0, g, q, accg, accu);
                 }
             }
             __syncwarp();
@@ -608,10 +691,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 report_timeout(P);
                 ok = false;
             }
-            float4* rw = reinterpret_cast<float4*>(red + ((rs * kCW + warp) * 32 + lane) * 8);
+            float4* rw = reinterpret_cast<float4*>(red + ((rs * kCW + mw) * 32 + lane) * 8);
             rw[0] = make_float4(accg[0][0], accg[0][1], accg[0][2], accg[0][3]);
             rw[1] = make_float4(accu[0][0], accu[0][1], accu[0][2], accu[0][3]);
-            if (warp == 0 && lane < 6) {
+            if (mw == 0 && lane < 6) {
                 // lane i stores field i (selects, not an indexed register array)
                 int v = mv[0];
                 v = lane == 1 ? mv[1] : v;
@@ -629,82 +712,99 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
         if (lane == 0) mbar_arrive(gu_drained);
     }
 
-    // ---- down: warp w owns the ring uses j = w, w + 8, ... (one use = one group of a row tile)
-    float* ypart = P.ypart_smem ? reinterpret_cast<float*>(smem + FL.off_yp)
-                                : wsp<float>(P, P.L.ypart);
-    const int ypstride = P.ypart_smem ? 16 : H;  // floats between entries
+    // ---- down: unit j of this CTA (u = blockIdx.x + j G: group u / nb, rows [dn_rows (u % nb),
+    // + dn_rows) of H) goes to warp group j % n_wg, whose warp wsl takes the unit's rows
+    // [16 wsl, 16 wsl + 16).  The ring has a multiple of n_wg stages, so each stage is always
+    // consumed by the same warp group, in order: a warp is never a whole phase ahead of a
+    // stage's barrier (parity would alias).  Each entry's rows go to y_part [entry][H] (fp32).
+    float* ypart = wsp<float>(P, P.L.ypart);
     const int* ent_of = wsp<int>(P, P.L.ent_of);
     const int K1 = P.top_k + 1;
-    int j = 0;
-    for (int rt = G - 1 - (int)blockIdx.x; rt < n_dn; rt += G) {
-        const int ypcol = P.ypart_smem ? 0 : rt * 16;
-        for (int grp = 0; grp < n_groups; ++grp, ++j) {
-            // use j of the down ring goes to warp j % 8 and the ring has a multiple of 8 stages,
-            // so each stage is always consumed by the same warp, in order: a warp is never a
-            // whole phase ahead of a stage's barrier (parity would alias)
-            if (j % kCW != warp) continue;
-            const int st = j % NDT;
-            if (ok && !mbar_wait_bounded(&dn_full[st], (j / NDT) & 1)) {
-                report_timeout(P);
-                ok = false;
-            }
-            __syncwarp();
-            float acc[kAcc][4] = {};
-            int e0 = 0, nt = 0;
-            float dglob = 0.f, w_lo = 0.f, w_hi = 0.f;
-            if (ok) {  // (the producer released the stage after the group's h was complete and
-                       // put the down global scale and, for the shared expert, the gates into it)
-                const uint8_t* stg = dn_stage(st);
-                const int* hdr = reinterpret_cast<const int*>(stg);
-                e0 = hdr[GD_E0], nt = hdr[GD_NT];
-                dglob = __int_as_float(hdr[GD_DGLOB]);
-                w_lo = __int_as_float(hdr[GD_W + 2 * q]);
-                w_hi = __int_as_float(hdr[GD_W + 2 * q + 1]);
-                const __half* hrow = g < nt ? h16 + (int64_t)(e0 + g) * I : nullptr;
-                if constexpr (TD > 0) {
-                    uint4 hb[TD][Fmt::kSteps / 2];
+    const int wgi = mw / wpu, wsl = mw % wpu;
+    const int n_units = n_groups * nb;
+    const int n_local = (int)blockIdx.x < n_units ? (n_units - 1 - (int)blockIdx.x) / G + 1 : 0;
+    for (int j = wgi; j < n_local; j += n_wg) {
+        const int st = j % NDT;
+        if (ok && !mbar_wait_bounded(&dn_full[st], (j / NDT) & 1)) {
+            report_timeout(P);
+            ok = false;
+        }
+        __syncwarp();
+        float acc[kAcc][4] = {};
+        int e0 = 0, nt = 0;
+        float dglob = 0.f, w_lo = 0.f, w_hi = 0.f;
+        if (ok) {  // (the producer released the stage after the group's h was complete and put
+                   // the down global scale and, for the shared expert, the gates into it)
+            const uint8_t* stg = dn_stage(st);
+            const int* hdr = reinterpret_cast<const int*>(stg);
+            e0 = hdr[GD_E0], nt = hdr[GD_NT];
+            dglob = __int_as_float(hdr[GD_DGLOB]);
+            w_lo = __int_as_float(hdr[GD_W + 2 * q]);
+            w_hi = __int_as_float(hdr[GD_W + 2 * q + 1]);
+            const uint8_t* code = stg + kStageHdr + wsl * 16 * cbd;
+            const uint8_t* sc = stg + od_sc + wsl * 16 * sbd;
+            // (lanes past the group's entries read entry 0's row; their columns are not stored)
+            const __half* hrow = h16 + (int64_t)(e0 + (g < nt ? g : 0)) * I;
+            if constexpr (TD > 0) {
+                uint4 hb[TD][Fmt::kSteps / 2];
 #pragma unroll
-                    for (int t = 0; t < TD; ++t)
-                        load_h_tile<Fmt>(hrow, t * Fmt::kWarpTileK, q, hb[t]);
+                for (int t = 0; t < TD; ++t) load_h_tile<Fmt>(hrow, t * Fmt::kWarpTileK, q, hb[t]);
 #pragma unroll
-                    for (int t = 0; t < TD; ++t)
-                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, aux, hb[t],
-                                       t * Fmt::kWarpTileK, g, q, acc);
-                } else {
-                    for (int k0 = 0; k0 < I; k0 += Fmt::kWarpTileK) {
-                        uint4 hb[Fmt::kSteps / 2];
-                        load_h_tile<Fmt>(hrow, k0, q, hb);
-                        down_tile<Fmt>(stg + kStageHdr, stg + od_sc, cbd, sbd, aux, hb, k0, g, q,
-                                       acc);
-                    }
+                for (int t = 0; t < TD; ++t)
+                    down_tile<Fmt>(code, sc, cbd, sbd, aux, hb[t], t * Fmt::kWarpTileK, g, q, acc);
+            } else {
+                for (int k0 = 0; k0 < I; k0 += Fmt::kWarpTileK) {
+                    uint4 hb[Fmt::kSteps / 2];
+                    load_h_tile<Fmt>(hrow, k0, q, hb);
+                    down_tile<Fmt>(code, sc, cbd, sbd, aux, hb, k0, g, q, acc);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dn_empty[st]);
-            fold_acc(acc);
-            // C fragment: rows g, g+8; entries 2q, 2q+1 of the group
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dn_empty[st]);
+        fold_acc(acc);
+        // C fragment: rows g, g+8; entries 2q, 2q+1 of the group
+        const int row0 = (((int)blockIdx.x + j * G) % nb) * dn_rows + wsl * 16;
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-                const int row = g + ((v >> 1) << 3);
-                const int n = 2 * q + (v & 1);
-                if (n < nt)
-                    ypart[(int64_t)(e0 + n) * ypstride + ypcol + row] =
-                        acc[0][v] * dglob * ((v & 1) ? w_hi : w_lo);
-            }
+        for (int v = 0; v < 4; ++v) {
+            const int row = g + ((v >> 1) << 3);
+            const int n = 2 * q + (v & 1);
+            if (n < nt)
+                ypart[(int64_t)(e0 + n) * H + row0 + row] =
+                    acc[0][v] * dglob * ((v & 1) ? w_hi : w_lo);
         }
-        named_bar_sync(1, kConsumers);
-        // y rows of this tile: the entries of each token summed in the order j = 0..k-1, shared
-        // (no groups: an upstream error or no valid entry, y = 0 without reading the entry map)
-        for (int idx = tid; idx < P.n_tok * 16; idx += kConsumers) {
-            const int t = idx >> 4, r = idx & 15;
-            float sum = 0.f;
-            for (int jj = 0; jj < (n_groups > 0 ? K1 : 0); ++jj) {
-                const int e = ent_of[t * K1 + jj];
-                if (e >= 0) sum += ypart[(int64_t)e * ypstride + ypcol + r];
+    }
+    // every unit of the grid done (a count over all CTAs; the grid is resident, one CTA per SM):
+    // this CTA's y_part stores, then its count (fence, relaxed add); wait for the total
+    named_bar_sync(1, kConsumers);
+    int* dn_done = wsp<int>(P, P.L.phase);  // (reset by the grouping before this kernel)
+    if (ctid == 0) {
+        fence_acq_rel_gpu();
+        red_relaxed_gpu_add(dn_done, n_local);
+        bool fin = false;
+        for (uint32_t i = 0; i < (1u << 22); ++i) {
+            if (ld_relaxed_gpu(dn_done) >= n_units) {
+                fin = true;
+                break;
             }
-            P.y[(int64_t)t * P.y_stride + rt * 16 + r] = f32_to_bf16_bits(sum);
+            __nanosleep(i < 64 ? 32 : 256);
         }
-        named_bar_sync(1, kConsumers);  // y_part is reused by the next row tile
+        if (!fin) report_timeout(P);
+        fence_acq_rel_gpu();
+    }
+    named_bar_sync(1, kConsumers);
+    // y: this CTA's share of the (token, row) outputs, each token's entries summed in the order
+    // j = 0..k-1, shared (no groups: an upstream error or no valid entry, y = 0 without reading
+    // the entry map)
+    const int n_out = P.n_tok * H;
+    for (int idx = (int)blockIdx.x * kConsumers + ctid; idx < n_out; idx += G * kConsumers) {
+        const int t = idx / H, r = idx - t * H;
+        float sum = 0.f;
+        for (int jj = 0; jj < (n_groups > 0 ? K1 : 0); ++jj) {
+            const int e = __ldg(ent_of + t * K1 + jj);
+            if (e >= 0) sum += __ldcg(ypart + (int64_t)e * H + r);
+        }
+        P.y[(int64_t)t * P.y_stride + r] = f32_to_bf16_bits(sum);
     }
 }
 
@@ -763,29 +863,33 @@ int launch_fmt(FfnParams& P, cudaStream_t st) {
     const int xrow = H * 2 + kXPad;
     FL.stage_gu = round128(kStageHdr + 32 * Fmt::code_bytes(H) + 32 * Fmt::scale_bytes(H) +
                            FL.xt * xrow);
-    FL.stage_dn = round128(kStageHdr + 16 * (Fmt::code_bytes(I) + Fmt::scale_bytes(I)));
+    // down units of 64, 32 or 16 rows of H (16 per MMA warp): the largest whose stage stays
+    // within 20 KB.  Fewer, larger bulk copies: every copy costs the single-lane producer a
+    // fixed issue time, and 16-row units made the down phase issue-bound (2 copies per 4.6 KB).
+    const int row_dn = Fmt::code_bytes(I) + Fmt::scale_bytes(I);
+    FL.dn_rows = 64;
+    while (FL.dn_rows > 16 && kStageHdr + FL.dn_rows * row_dn > 20 * 1024) FL.dn_rows /= 2;
+    if (H % FL.dn_rows) return NVMOE_ERR_UNSUPPORTED;
+    const int n_wg = kCW / (FL.dn_rows / 16);  // warp groups; down stage counts are multiples
+    FL.stage_dn = round128(kStageHdr + FL.dn_rows * row_dn);
     const int x_bytes = FL.x_res ? round128(std::max(1, P.n_tok) * xrow) : 0;
-    const int red_bytes = 2 * kCW * 32 * 8 * 4, meta_bytes = 2 * 8 * 4;
+    const int red_bytes = 2 * kCW * 32 * 8 * 4, meta_bytes = round128((16 + kPubInts) * 4);
     const int bar_bytes = 8 * (2 * 4 + 2 * 64 + 6) + 64;
     const int aux_bytes = round128(Fmt::kAuxBytes);
-    const int yp_bytes = round128(P.L.n_ent_max * 16 * 4);
     const int fixed = red_bytes + meta_bytes + bar_bytes + x_bytes + aux_bytes;
-    // y_part in shared memory when it leaves room for 2 gate_up and 8 down stages
-    P.ypart_smem = (fixed + yp_bytes + 2 * FL.stage_gu + kCW * FL.stage_dn <= kSmemCap) ? 1 : 0;
-    const int avail = kSmemCap - fixed - (P.ypart_smem ? yp_bytes : 0);
-    // down stage counts are multiples of the 8 MMA warps (see the down phase)
-    FL.nst_gu = std::min(4, (avail - kCW * FL.stage_dn) / FL.stage_gu);
+    const int avail = kSmemCap - fixed;
+    FL.nst_gu = std::min(4, (avail - n_wg * FL.stage_dn) / FL.stage_gu);
     // (one stage only for the widest items, e.g. bf16 rows: loads then do not overlap the math)
     if (FL.nst_gu < 1) return NVMOE_ERR_UNSUPPORTED;
-    FL.nst_dn = std::min(32, (avail - FL.nst_gu * FL.stage_gu) / FL.stage_dn) / kCW * kCW;
-    if (FL.nst_dn < kCW) return NVMOE_ERR_UNSUPPORTED;
-    FL.nst_dn_ext = std::min(32, FL.nst_gu * FL.stage_gu / FL.stage_dn) / kCW * kCW;
+    FL.nst_dn = std::min(32, (avail - FL.nst_gu * FL.stage_gu) / FL.stage_dn) / n_wg * n_wg;
+    if (FL.nst_dn < n_wg) return NVMOE_ERR_UNSUPPORTED;
+    FL.nst_dn_ext =
+        std::min(32 - FL.nst_dn, FL.nst_gu * FL.stage_gu / FL.stage_dn) / n_wg * n_wg;
     FL.off_x = FL.nst_gu * FL.stage_gu;
     FL.off_dn = FL.off_x + x_bytes;
     FL.off_red = FL.off_dn + FL.nst_dn * FL.stage_dn;
     FL.off_meta = FL.off_red + red_bytes;
-    FL.off_yp = FL.off_meta + meta_bytes;
-    FL.off_aux = FL.off_yp + (P.ypart_smem ? yp_bytes : 0);
+    FL.off_aux = FL.off_meta + meta_bytes;
     FL.off_bar = FL.off_aux + aux_bytes;
     FL.total = FL.off_bar + 8 * (2 * FL.nst_gu + 2 * (FL.nst_dn + FL.nst_dn_ext) + 6);
     // compile-time K tiles per MMA warp (gate_up) and per down slab where the shape has an
