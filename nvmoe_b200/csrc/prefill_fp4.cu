@@ -171,7 +171,7 @@ __host__ __device__ inline Pf4Layout pf4_layout(int n_tok, int top_k, int H, int
     L.ximg = take((size_t)L.max_tiles * L.ksg * kImg);
     L.himg = take((size_t)L.max_tiles * L.ksd * kImg);
     L.h32 = take(4 * (size_t)L.n_ent_max * I);
-    L.ypart = take(4 * (size_t)L.n_ent_max * H);
+    L.ypart = take(2 * (size_t)L.n_ent_max * H);  // bf16 per-entry partials
     L.total = o;
     return L;
 }
@@ -623,7 +623,7 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
         // entries 16 hh .. 16 hh + 15 (a column group of 4 terms each)
         const int r = 32 * (warp & 3) + lane, hh = warp >> 2, i0 = 16 * hh;
         float* h32 = qws<float>(P, P.L.h32);
-        float* ypart = qws<float>(P, P.L.ypart);
+        uint16_t* ypart = qws<uint16_t>(P, P.L.ypart);
         for (int k = 0; k < my_units && ok; ++k) {
             const int b = k % kInfoN, u = c + k * G, sub = u % UPT;
             if (!wait_bar(&info_full[b], (k / kInfoN) & 1, abort)) {
@@ -677,9 +677,12 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
                     h32[(int64_t)(eb + e) * I + sub * 128 + r] = silu(a * f * ga) * (bb * f * gb);
                 } else {
                     const float f = fp4_exp2(-in.eexp[e]) * in.efac[e] * ga;
-                    float* yp = ypart + (int64_t)(eb + e) * H + sub * 256 + r;
-                    yp[0] = a * f;
-                    yp[128] = bb * f;
+                    // (bf16 partials: half the bytes of the largest write and read of the
+                    // layer; each is within 2^-9 of the fp32 partial, and the sum and the
+                    // output rounding stay as before)
+                    uint16_t* yp = ypart + (int64_t)(eb + e) * H + sub * 256 + r;
+                    yp[0] = f32_to_bf16_bits(a * f);
+                    yp[128] = f32_to_bf16_bits(bb * f);
                 }
             };
 #pragma unroll
@@ -702,11 +705,12 @@ __global__ void __launch_bounds__(kGThreads, 1) pf4_gemm(const __grid_constant__
     }
 }
 
-// y[t] = sum_j y_part[ent_of[t, j]] in the order j = 0..k-1, shared; 4 columns per thread.
+// y[t] = sum_j y_part[ent_of[t, j]] (bf16 partials, fp32 sum) in the order j = 0..k-1, shared;
+// 4 columns per thread.
 __global__ void pf4_combine(const __grid_constant__ Pf4Params P) {
     const int H = P.pool.hidden, K1 = P.top_k + 1;
     const int* ent_of = qws<int>(P, P.L.ent_of);
-    const float* yp = qws<float>(P, P.L.ypart);
+    const uint16_t* yp = qws<uint16_t>(P, P.L.ypart);
     const int64_t n4 = (int64_t)P.n_tok * (H / 4);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -715,8 +719,9 @@ __global__ void pf4_combine(const __grid_constant__ Pf4Params P) {
         for (int j = 0; j < K1; ++j) {
             const int e = ent_of[t * K1 + j];
             if (e < 0) continue;
-            const float4 v = *reinterpret_cast<const float4*>(yp + (int64_t)e * H + cc);
-            s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
+            const uint2 v = *reinterpret_cast<const uint2*>(yp + (int64_t)e * H + cc);
+            s.x += __uint_as_float(v.x << 16), s.y += __uint_as_float(v.x & 0xffff0000u);
+            s.z += __uint_as_float(v.y << 16), s.w += __uint_as_float(v.y & 0xffff0000u);
         }
         uint2 o;
         o.x = (uint32_t)f32_to_bf16_bits(s.x) | ((uint32_t)f32_to_bf16_bits(s.y) << 16);
