@@ -153,6 +153,7 @@ __device__ __forceinline__ void bulk_rows(uint8_t* dst, const uint8_t* src, int 
     if (stride == row_bytes) {
         bulk_g2s_stream(dst, src, (uint32_t)(rows * row_bytes), bar, pol);
     } else {
+#pragma unroll 1
         for (int r = 0; r < rows; ++r)
             bulk_g2s_stream(dst + r * row_bytes, src + r * stride, (uint32_t)row_bytes, bar, pol);
     }
@@ -189,6 +190,8 @@ __host__ __device__ inline int round128(int v) { return (v + 127) / 128 * 128; }
 // chains every mma.sync on the previous one's result and leaves the warp latency-bound); the
 // accumulators are summed in a fixed order at the end of the item.
 constexpr int kAcc = 8;
+// entries per token (top-k + the shared expert) whose partials the final sum loads at once
+constexpr int kSumK = 12;
 
 template <typename Fmt>
 __device__ __forceinline__ void gate_up_tile(const uint8_t* gcode, const uint8_t* ucode,
@@ -308,17 +311,6 @@ __device__ __forceinline__ void load_record(const FfnParams& P, int grp, int4 (&
 #pragma unroll
     for (int k = 0; k < kDescInts / 4; ++k) r[k] = __ldcg(src + k);
 }
-__device__ __forceinline__ void shfl_record(int4 (&dst)[kDescInts / 4],
-                                            const int4 (&src)[kDescInts / 4], int lane) {
-#pragma unroll
-    for (int k = 0; k < kDescInts / 4; ++k) {
-        dst[k].x = __shfl_sync(0xffffffffu, src[k].x, lane);
-        dst[k].y = __shfl_sync(0xffffffffu, src[k].y, lane);
-        dst[k].z = __shfl_sync(0xffffffffu, src[k].z, lane);
-        dst[k].w = __shfl_sync(0xffffffffu, src[k].w, lane);
-    }
-}
-
 constexpr int kCW = kConsumerWarps;       // MMA warps
 // Hardware warp of each role: the 8 MMA warps are warps 0-7 (index mw = warp), then the
 // control warps.
@@ -413,20 +405,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
         const int n_gu = n_groups * tiles_i;
         if (FL.x_res && lane == 0 && n_gu > (int)blockIdx.x) {
             mbar_arrive_expect_tx(x_full, (uint32_t)(P.n_tok * H * 2));
+#pragma unroll 1
             for (int t = 0; t < P.n_tok; ++t)
                 bulk_g2s(smem + FL.off_x + t * xrow, x16 + (int64_t)t * H, (uint32_t)(H * 2), x_full);
         }
         bool ok = true;
         int it = 0;
+#pragma unroll 1
         for (int base = blockIdx.x; base < n_gu && ok; base += 32 * G) {
             const int mine = base + lane * G;
             if (base != (int)blockIdx.x && mine < n_gu) load_record(P, mine / tiles_i, rec);
             const int n_here = min(32, (n_gu - base + G - 1) / G);
+            // Lane i holds item i's record and issues it (no shuffles of the record); the loop
+            // is not unrolled, so every item runs the same short stretch of code, which stays in
+            // the instruction cache (unrolled copies were cold on every item, and their fetches,
+            // not the weight stream, paced the gate_up phase).
+#pragma unroll 1
             for (int i = 0; i < n_here; ++i, ++it) {
-                int4 r[kDescInts / 4];
-                shfl_record(r, rec, i);
-                if (lane == 0) {
-                    const int item = base + i * G;
+                if (lane == i) {
+                    const int* rv = reinterpret_cast<const int*>(rec);
+                    const int item = mine;
                     const int st = it % NGU;
                     if (!mbar_wait_bounded(&gu_empty[st], ((it / NGU) & 1) ^ 1)) {
                         report_timeout(P);
@@ -434,18 +432,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                     } else {
                         uint8_t* stg = smem + (size_t)st * FL.stage_gu;
                         int* hdr = reinterpret_cast<int*>(stg);
-                        copy_record(hdr, r);
-                        if (hdr[GD_MISS] > 0 && !refill_wait(P, hdr[GD_MISS] - 1, 0)) {
+                        copy_record(hdr, rec);
+                        const int miss = rv[GD_MISS];
+                        if (miss > 0 && !refill_wait(P, miss - 1, 0)) {
                             report_timeout(P);
                             ok = false;
                         }
-                        hdr[GD_RT] = item % tiles_i;
+                        const int rt = item % tiles_i;
+                        hdr[GD_RT] = rt;
                         hdr[GD_GID] = item / tiles_i;
-                        const int sh = hdr[GD_POOL];
+                        const int sh = rv[GD_POOL];
                         const BankSel bg = bank_sel(sh, P.pool.gate, P.shared.gate);
                         const BankSel bu = bank_sel(sh, P.pool.up, P.shared.up);
-                        const int slot = hdr[GD_SLOT], nt = hdr[GD_NT];
-                        const int64_t r0 = (int64_t)(item % tiles_i) * 16;
+                        const int slot = rv[GD_SLOT], nt = rv[GD_NT];
+                        const int64_t r0 = (int64_t)rt * 16;
                         mbar_arrive_expect_tx(
                             &gu_full[st],
                             (uint32_t)(32 * cbg + 32 * sbg + (FL.x_res ? 0 : nt * H * 2)));
@@ -466,12 +466,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                                       16, sbg, bu.scale_row_stride, &gu_full[st]);
                         }
                         if (!FL.x_res)
+#pragma unroll 1
                             for (int n = 0; n < nt; ++n)
                                 bulk_g2s(stg + og_x + n * xrow, x16 + (int64_t)hdr[GD_TOK + n] * H,
                                          (uint32_t)(H * 2), &gu_full[st]);
                     }
                 }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
+                ok = __shfl_sync(0xffffffffu, ok, i);
                 if (!ok) break;
             }
         }
@@ -519,6 +520,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 const int handed = ld_acquire_cta(pub);
                 if (handed > published) {
                     fence_acq_rel_gpu();
+#pragma unroll 1
                     for (int i = published; i < handed; ++i)
                         red_relaxed_gpu_add(done + pub[4 + i % kPubRing], 1);
                     published = handed;
@@ -554,6 +556,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 hdr[GD_DGLOB] = __float_as_int(dgl);
                 if (hdr[GD_POOL] && sgate) {
                     const int nt = hdr[GD_NT];
+#pragma unroll 1
                     for (int k = 0; k < nt; ++k)
                         hdr[GD_W + k] = __float_as_int(__ldcg(sgate + hdr[GD_TOK + k]));
                 }
@@ -657,8 +660,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                 const uint8_t* stg = smem + (size_t)st * FL.stage_gu;
                 const int* hdr = reinterpret_cast<const int*>(stg);
                 mv[0] = hdr[GD_E0], mv[1] = hdr[GD_NT], mv[2] = hdr[GD_RT], mv[3] = hdr[GD_GID];
-                {  // the slot's global scales from the pool itself: a refill between the
-                   // grouping and this kernel may have replaced the slot's expert
+                if (mw == 0) {  // (only warp 0 hands them on) the slot's global scales from
+                                // the pool itself: a refill between the grouping and this
+                                // kernel may have replaced the slot's expert
                     const int sh = hdr[GD_POOL], slot = hdr[GD_SLOT];
                     mv[4] = __float_as_int(global_of_sel(bank_sel(sh, P.pool.gate, P.shared.gate), slot));
                     mv[5] = __float_as_int(global_of_sel(bank_sel(sh, P.pool.up, P.shared.up), slot));
@@ -670,7 +674,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
                                              : stg + og_x + (has_tok ? g : 0) * xrow;
                 const __half* xs = reinterpret_cast<const __half*>(xb);
                 if constexpr (TPW > 0) {
-#pragma unroll
+                    // (one tile body: the warp's K tiles run through the same code)
+#pragma unroll 1
                     for (int t = 0; t < TPW; ++t)
                         gate_up_tile<Fmt>(stg + kStageHdr, stg + og_uc, stg + og_gs, stg + og_us,
                                           cbg, sbg, aux, xs, (mw * TPW + t) * Fmt::kWarpTileK,
@@ -797,12 +802,28 @@ __global__ void __launch_bounds__(kFusedThreads, 1) ffn_fused(FfnParams P, Fused
     // j = 0..k-1, shared (no groups: an upstream error or no valid entry, y = 0 without reading
     // the entry map)
     const int n_out = P.n_tok * H;
+    const int k1 = n_groups > 0 ? K1 : 0;
     for (int idx = (int)blockIdx.x * kConsumers + ctid; idx < n_out; idx += G * kConsumers) {
         const int t = idx / H, r = idx - t * H;
         float sum = 0.f;
-        for (int jj = 0; jj < (n_groups > 0 ? K1 : 0); ++jj) {
-            const int e = __ldg(ent_of + t * K1 + jj);
-            if (e >= 0) sum += __ldcg(ypart + (int64_t)e * H + r);
+        if (k1 <= kSumK) {
+            // every entry index first, then every partial: two round trips to L2 in all, not
+            // two per entry (dependent pairs made the slowest CTAs' sums the kernel's tail)
+            int e[kSumK];
+            float v[kSumK];
+#pragma unroll
+            for (int jj = 0; jj < kSumK; ++jj) e[jj] = jj < k1 ? __ldg(ent_of + t * K1 + jj) : -1;
+#pragma unroll
+            for (int jj = 0; jj < kSumK; ++jj)
+                v[jj] = e[jj] >= 0 ? __ldcg(ypart + (int64_t)e[jj] * H + r) : 0.f;
+#pragma unroll
+            for (int jj = 0; jj < kSumK; ++jj)
+                if (e[jj] >= 0) sum += v[jj];
+        } else {
+            for (int jj = 0; jj < k1; ++jj) {
+                const int e = __ldg(ent_of + t * K1 + jj);
+                if (e >= 0) sum += __ldcg(ypart + (int64_t)e * H + r);
+            }
         }
         P.y[(int64_t)t * P.y_stride + r] = f32_to_bf16_bits(sum);
     }
