@@ -344,6 +344,34 @@ int nvmoe_host_tier_resolve(nvmoe_host_tier* tier, const int32_t* unique_ids,
  * each host slot [host_slots] (-1: free).  Either pointer may be NULL. */
 int nvmoe_host_tier_tables(const nvmoe_host_tier* tier, int32_t* host_slot_of_id,
                            int32_t* id_in_host_slot);
+/* The tier's counts since it was created: misses it served from a host slot (host_hits) and
+ * misses that had to be loaded from the backing store (host_misses), over every resolve call.
+ * (eval_cb's st->host_hits / st->host_misses, scripts/moe_cache_probe.cpp:727-734.)  Either
+ * pointer may be NULL. */
+int nvmoe_host_tier_stats(const nvmoe_host_tier* tier, int64_t* host_hits, int64_t* host_misses);
+
+/* ================================================================ cache counters
+ * eval_cb's GPU-tier statistics (scripts/moe_cache_probe.cpp:253-256): distinct ids found in
+ * the slot pool or copied in (:662-671), matched callbacks (:995), the same restricted to decode
+ * steps, and the bytes copied into the slot pool.  The host tier keeps its own counts
+ * (nvmoe_host_tier_stats).  Lives in device memory, zeroed by the caller. */
+typedef struct nvmoe_cache_stats {
+    int64_t calls;              /* remap calls counted (eval_cb's callback_hits)            */
+    int64_t decode_calls;       /* calls with is_decode                                    */
+    int64_t gpu_hits;           /* distinct ids already in the slot pool                   */
+    int64_t gpu_misses;         /* distinct ids copied into the slot pool                  */
+    int64_t decode_gpu_hits;    /* gpu_hits of decode calls                                */
+    int64_t decode_gpu_misses;  /* gpu_misses of decode calls                              */
+    int64_t refill_bytes;       /* gpu_misses x bytes per expert                           */
+    int64_t error_calls;        /* calls whose miss list reported an error (not counted)   */
+} nvmoe_cache_stats;
+
+/* Adds one remap call's GPU-tier counts to stats on the device, in stream order after the call
+ * that wrote the miss list: counts[0] distinct ids, counts[1] misses, counts[2] status (the
+ * nvmoe_miss_list.counts of nvmoe_remap or nvmoe_decode_layer).  No host synchronisation, so it
+ * can sit in a captured step.  A call whose status is an error only increments error_calls. */
+int nvmoe_cache_stats_add(nvmoe_cache_stats* stats, const int32_t* counts, int is_decode,
+                          int64_t bytes_per_expert, nvmoe_stream_t stream);
 
 /* ================================================================ R5: pinned-host refill
  * One bank of an expert row in both tiers: slot s of the device pool starts at

@@ -204,6 +204,13 @@ class EpCombineArgs(C.Structure):
     ]
 
 
+class CacheStats(C.Structure):
+    """nvmoe_cache_stats (the device buffer is an int64 tensor of the same layout)."""
+    _fields_ = [(n, C.c_int64) for n in (
+        "calls", "decode_calls", "gpu_hits", "gpu_misses", "decode_gpu_hits",
+        "decode_gpu_misses", "refill_bytes", "error_calls")]
+
+
 class RouterGateArgs(C.Structure):
     _fields_ = [
         ("resid", C.c_void_p),
@@ -274,6 +281,10 @@ SIGNATURES = {
     "nvmoe_host_tier_resolve": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                           C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "nvmoe_host_tier_tables": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "nvmoe_host_tier_stats": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64),
+                                        C.POINTER(C.c_int64)]),
+    "nvmoe_cache_stats_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int64,
+                                        C.c_void_p]),
     "nvmoe_refill_async": (C.c_int, [C.POINTER(RefillBank), C.c_int, C.c_void_p, C.c_void_p,
                                      C.c_int, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                      C.c_void_p]),

@@ -211,6 +211,7 @@ struct nvmoe_host_tier {
     std::vector<int32_t> id_in;    // expert in host slot h, -1: free
     nvmoe::SegmentedLru lru;
     std::unordered_set<int64_t> active;  // the step's distinct ids (reused)
+    int64_t host_hits = 0, host_misses = 0;  // misses served by a host slot / loaded
 };
 
 extern "C" {
@@ -247,6 +248,7 @@ int nvmoe_host_tier_resolve(nvmoe_host_tier* t, const int32_t* unique_ids,
             t->lru.touch(r);
             host_slot_out[m] = hs;
             load_out[m] = 0;
+            ++t->host_hits;
             continue;
         }
         int32_t ns;
@@ -265,6 +267,7 @@ int nvmoe_host_tier_resolve(nvmoe_host_tier* t, const int32_t* unique_ids,
         t->lru.insert_new(r);
         host_slot_out[m] = ns;
         load_out[m] = 1;  // the caller fills host slot ns from the backing store
+        ++t->host_misses;
     }
     return NVMOE_OK;
 }
@@ -276,6 +279,13 @@ int nvmoe_host_tier_tables(const nvmoe_host_tier* t, int32_t* host_slot_of_id,
         std::copy(t->slot_of.begin(), t->slot_of.end(), host_slot_of_id);
     if (id_in_host_slot)
         std::copy(t->id_in.begin(), t->id_in.end(), id_in_host_slot);
+    return NVMOE_OK;
+}
+
+int nvmoe_host_tier_stats(const nvmoe_host_tier* t, int64_t* host_hits, int64_t* host_misses) {
+    if (!t) return NVMOE_ERR_INVALID_ARG;
+    if (host_hits) *host_hits = t->host_hits;
+    if (host_misses) *host_misses = t->host_misses;
     return NVMOE_OK;
 }
 

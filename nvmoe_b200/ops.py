@@ -411,6 +411,34 @@ def moe_ffn_prefill(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor
     return out
 
 
+# ------------------------------------------------------------------ cache counters
+STATS_FIELDS = tuple(n for n, _ in _lib.CacheStats._fields_)
+
+
+class CacheStatsGPU:
+    """nvmoe_cache_stats in device memory: eval_cb's GPU-tier counters
+    (scripts/moe_cache_probe.cpp:253-256, :662-671, :995), accumulated in stream order from the
+    miss lists of remap / decode layer calls, without a host round trip."""
+
+    def __init__(self, device="cuda"):
+        self.buf = torch.zeros(len(STATS_FIELDS), dtype=torch.int64, device=device)
+
+    def add(self, misses: "MissListGPU", is_decode: bool, bytes_per_expert: int,
+            stream=None) -> None:
+        check(lib().nvmoe_cache_stats_add(self.buf.data_ptr(), misses.counts.data_ptr(),
+                                          1 if is_decode else 0, int(bytes_per_expert),
+                                          _stream(stream)), "nvmoe_cache_stats_add")
+
+    def reset(self) -> None:
+        self.buf.zero_()
+
+    def read(self) -> dict:
+        d = dict(zip(STATS_FIELDS, self.buf.cpu().tolist()))
+        refs = d["gpu_hits"] + d["gpu_misses"]
+        d["gpu_hit_rate"] = d["gpu_hits"] / refs if refs else 0.0
+        return d
+
+
 # ------------------------------------------------------------------ R5 refill
 def refill_banks(gpu: ExpertWeights, host: ExpertWeights) -> list[_lib.RefillBank]:
     """One RefillBank per FTW bank (codes, scales, global) of gate_up and down."""

@@ -48,6 +48,13 @@ class HostTier:
               "nvmoe_host_tier_resolve")
         return hs[:m.size], ld[:m.size]
 
+    def stats(self) -> tuple[int, int]:
+        """(host hits, host misses) over every resolve call (nvmoe_host_tier_stats)."""
+        hh, hm = C.c_int64(0), C.c_int64(0)
+        check(lib().nvmoe_host_tier_stats(self.h, C.byref(hh), C.byref(hm)),
+              "nvmoe_host_tier_stats")
+        return hh.value, hm.value
+
     def tables(self):
         a = np.empty(self.n_expert, np.int32)
         b = np.empty(self.host_slots, np.int32)

@@ -63,7 +63,8 @@ def test_struct_layouts_match_a_c_compiler(tmp_path):
                "nvmoe_decode_args": _lib.DecodeArgs,
                "nvmoe_router_gate_args": _lib.RouterGateArgs,
                "nvmoe_ep_dispatch_args": _lib.EpDispatchArgs,
-               "nvmoe_ep_combine_args": _lib.EpCombineArgs}
+               "nvmoe_ep_combine_args": _lib.EpCombineArgs,
+               "nvmoe_cache_stats": _lib.CacheStats}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nvmoe_b200.h"',
              'int main(void) {']
     for cname, py in mirrors.items():

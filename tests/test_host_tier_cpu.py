@@ -44,3 +44,6 @@ def test_host_tier_matches_oracle(E, S, HS, B, k):
     np.testing.assert_array_equal(a, ea)
     np.testing.assert_array_equal(b, eb)
     assert loads > HS and hits > 0  # the host tier filled up and then evicted
+    # its counters are eval_cb's st->host_hits / st->host_misses (moe_cache_probe.cpp:727-734):
+    # the oracle's host-to-slot copies and backing-store loads of the same steps
+    assert tier.stats() == (hits, loads)
