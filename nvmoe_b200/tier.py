@@ -90,10 +90,14 @@ class BoundedTierStack:
     like the synthetic weights).  Eager: the host reads each layer step's miss list."""
 
     def __init__(self, cfg, host_slots: int, backing: ExpertWeights | None = None,
-                 device="cuda", seed: int = 0, protected_ratio: float = 0.8):
+                 device="cuda", seed: int = 0, protected_ratio: float = 0.8, loader=None):
+        """loader: where host-tier misses are read from instead of `backing` (an object with
+        load_into(layer, expert, host_banks, host_slot), e.g. loaders.FtwModel or
+        loaders.InterleavedSidecar); `backing` still gives the pools' shapes."""
         from .engine import MoEStack
         from .formats import random_experts
         self.cfg, self.host_slots = cfg, host_slots
+        self.loader = loader
         self.device = d = torch.device(device)
         self.backing = backing if backing is not None else random_experts(
             cfg.quant, cfg.n_experts, cfg.hidden, cfg.inter, seed=seed)
@@ -133,7 +137,11 @@ class BoundedTierStack:
         return self._buf[n]
 
     def _load(self, l: int, expert: int, host_slot: int) -> None:
-        """Backing store -> pinned host slot (the stand-in for the NVMe read)."""
+        """Backing store -> pinned host slot (the stand-in for the NVMe read): a read from the
+        model's files when the stack has a loader, else a copy from the in-memory store."""
+        if self.loader is not None:
+            self.loader.load_into(l, expert, _bank_tensors(self.host[l]), host_slot)
+            return
         for dst, src in zip(_bank_tensors(self.host[l]), _bank_tensors(self.backing)):
             dst[host_slot].copy_(src[expert])
 

@@ -9,7 +9,9 @@ import numpy as np
 import pytest
 import torch
 
+from nvmoe_b200 import loaders
 from nvmoe_b200.engine import StackConfig
+from nvmoe_b200.formats import random_experts
 from nvmoe_b200.synth import layer_log_bias
 from nvmoe_b200.tier import BoundedTierStack
 from oracle import ref_numpy as R
@@ -19,10 +21,19 @@ from tests.helpers import DenseExperts, bf16_bits, within
 pytestmark = pytest.mark.gpu
 
 
-def test_bounded_host_tier_stack_matches_oracle(cuda_device):
+@pytest.mark.parametrize("source", ["memory", "ftw_files"])
+def test_bounded_host_tier_stack_matches_oracle(cuda_device, source, tmp_path):
+    """source "ftw_files": host-tier misses are read from an FTW model directory on disk
+    (loaders.FtwModel, every layer holding the same experts as the in-memory store)."""
     L, E, k, H, I, S, HS, B = 2, 64, 4, 2048, 512, 16, 24, 4
     cfg = StackConfig(n_layers=L, n_experts=E, top_k=k, hidden=H, inter=I, cache_size=S)
-    stack = BoundedTierStack(cfg, HS, device=cuda_device, seed=91)
+    backing = random_experts("nvfp4", E, H, I, seed=91)
+    loader = None
+    if source == "ftw_files":
+        loaders.write_ftw(str(tmp_path), [backing] * L, n_shards=3)
+        loader = loaders.FtwModel(str(tmp_path))
+    stack = BoundedTierStack(cfg, HS, backing=backing, device=cuda_device, seed=91,
+                             loader=loader)
     bias = layer_log_bias(L, E, 1.1, seed=6)
     stack.init_router(logit_bias=bias, seed=92)
     orc = [OracleLayer(E, S, host_cache_size=HS) for _ in range(L)]
