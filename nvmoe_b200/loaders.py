@@ -106,7 +106,7 @@ class FtwModel:
             if row.numel() * row.element_size() != len(buf):
                 raise ValueError(f"{bank}: host slot holds {row.numel() * row.element_size()} "
                                  f"bytes, the file's row {len(buf)}")
-            row.view(torch.uint8).reshape(-1).copy_(torch.frombuffer(bytearray(buf),
+            row.reshape(-1).view(torch.uint8).copy_(torch.frombuffer(bytearray(buf),
                                                                      dtype=torch.uint8))
 
     def experts(self, layer: int, ids) -> ExpertWeights:
@@ -221,7 +221,7 @@ class InterleavedSidecar:
             if row.numel() * row.element_size() != len(buf):
                 raise ValueError(f"host slot holds {row.numel() * row.element_size()} bytes, "
                                  f"the file's rows {len(buf)}")
-            row.view(torch.uint8).reshape(-1).copy_(torch.frombuffer(bytearray(buf),
+            row.reshape(-1).view(torch.uint8).copy_(torch.frombuffer(bytearray(buf),
                                                                      dtype=torch.uint8))
 
 

@@ -13,7 +13,7 @@ from nvmoe_b200.formats import random_experts
 
 
 def _same(a, b):
-    return torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+    return torch.equal(a.reshape(-1).view(torch.uint8), b.reshape(-1).view(torch.uint8))
 
 
 def test_ftw_round_trip_across_shards(tmp_path):
@@ -45,6 +45,12 @@ def test_ftw_round_trip_across_shards(tmp_path):
            w.down.scale, w.down.glob.reshape(-1, 1))
     for h, s in zip(host, src):
         assert _same(h[3], s[9]) and not h[:3].any()
+    # the host tier's own banks: global scales one fp32 per slot ([S], as the pools keep them)
+    from nvmoe_b200.tier import _bank_tensors, _empty_like_slots
+    tier_banks = _bank_tensors(_empty_like_slots(w, 5, pin=False))
+    m.load_into(2, 4, tier_banks, 2)
+    for h, s in zip(tier_banks, _bank_tensors(w)):
+        assert _same(h[2], s[4])
     with pytest.raises(IndexError):
         m.read_row(0, "down_packed", E)
     m.close()
