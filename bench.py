@@ -800,6 +800,48 @@ def cpu_oracle_sample(batch: int, seconds: float, layers_cap: int = 48):
                                      f"dequant + fp32 FFN, torch/BLAS threads={cores})"
 
 
+def reference_host_code(batch: int, seconds: float = 1.5, n_expert: int = 512, top_k: int = 10,
+                        cache_size: int = 128) -> dict:
+    """The reference's own host code for the step this library moves to the device, timed on
+    the host cores: eval_cb's remap + host-tier block (scripts/moe_cache_probe.cpp:627-753,
+    955-970, compiled from the reference tree into oracle/_ref by oracle/Makefile) over
+    Zipf(1.1)-routed decode steps of the benchmark's shape.  Routing is drawn before the timed
+    loop; one call per layer step, through a preallocated-buffer binding."""
+    import ctypes as C
+    import numpy as np
+    try:
+        from oracle import ref_numpy as R
+        from oracle.native import RefEvalCb
+        from nvmoe_b200.synth import layer_log_bias, router_logits
+        ref = RefEvalCb(n_expert, cache_size, 0, host_cache_size=n_expert)
+    except (OSError, ImportError) as e:  # the reference build is not on this machine
+        return {"unavailable": f"oracle/_ref not loadable ({type(e).__name__})"}
+    rng = np.random.default_rng(17)
+    bias = layer_log_bias(1, n_expert, 1.1, seed=0)[0]
+    steps = [np.ascontiguousarray(R.router_topk_softmax(router_logits(batch, bias, rng),
+                                                         top_k)[0].reshape(-1), np.int32)
+             for _ in range(256)]
+    n = batch * top_k
+    bufs = [np.empty(n, np.int32) for _ in range(7)] + [np.zeros(1, np.int32), np.zeros(1, np.int32)]
+    out, hg, hh, li, lg, lh, _, nh, nl = bufs
+    fn, h = ref.L.ref_evalcb_step, ref.h
+    for ids in steps[:32]:  # warm: the pool fills with the hot experts
+        fn(h, ids, batch, top_k, 1, out, hg, hh, nh, li, lg, lh, nl)
+    count, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for ids in steps:
+            fn(h, ids, batch, top_k, 1, out, hg, hh, nh, li, lg, lh, nl)
+        count += len(steps)
+    dt = time.perf_counter() - t0
+    return {"eval_cb_remap_us_per_layer_step": round(1e6 * dt / count, 3), "cores": 1,
+            "steps": count,
+            "what": f"the reference's eval_cb remap + host-tier block (moe_cache_probe.cpp:"
+                    f"627-753,955-970) per layer step, {n_expert} experts, top-{top_k}, "
+                    f"{cache_size} slots, batch {batch}, one host thread (ctypes call "
+                    f"overhead included); on the GPU this step runs inside the decode front "
+                    f"kernel"}
+
+
 def run_reference(a):
     """Reference arm: the CPU implementation of the path (oracle port; the reference's own FFN
     lives in FreeToken / ggml, which are not in the reference tree) on the host cores."""
@@ -817,7 +859,8 @@ def run_reference(a):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (oracle port)",
         "data": "synthetic (seeded)", "config": config_dict(a, 1),
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores,
-                         "kind": "port", "sample": desc},
+                         "kind": "port", "sample": desc,
+                         "reference_host_code": reference_host_code(a.batch)},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -854,10 +897,11 @@ def main():
     else:
         line = run_nvmoe(a, rank, world, local_rank)
     if rank == 0:
-        if not a.no_cpu:
+        if not a.no_cpu and world == 1:
             v, cores, desc = cpu_oracle_sample(a.batch, a.cpu_baseline_seconds)
             line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": cores,
-                                    "kind": "port", "sample": desc}
+                                    "kind": "port", "sample": desc,
+                                    "reference_host_code": reference_host_code(a.batch)}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
