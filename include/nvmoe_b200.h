@@ -350,6 +350,40 @@ int nvmoe_host_tier_tables(const nvmoe_host_tier* tier, int32_t* host_slot_of_id
  * pointer may be NULL. */
 int nvmoe_host_tier_stats(const nvmoe_host_tier* tier, int64_t* host_hits, int64_t* host_misses);
 
+/* ================================================================ (f)3 tail pruning
+ * eval_cb's decode-time "two-tier cost-aware expert pruning" (scripts/moe_cache_probe.cpp:
+ * 523-625) on the device, between the router top-k and the remap: per token row, picks in
+ * neither tier whose share of the row's weight is below nvme_thresh (or whose row already has
+ * min_mass of its weight resident), and, with host_thresh > 0, picks only in the host tier below
+ * host_thresh, are replaced from the last pick backwards by the row's first slot-resident
+ * expert (else the expert of the pool's first occupied slot) with weight 0, keeping at least
+ * min_keep picks and min_mass of the weight; the weights are then scaled back to their total.
+ * ids / weights [n_tok][top_k] are rewritten in place (row strides in elements).  Like the
+ * reference, nothing happens unless nvme_thresh > 0, n_tok * top_k <= 4096 and a slot is
+ * occupied; rows with an id outside [0, n_expert) are left as they are.  pruned (device, [2],
+ * optional) gains the decode calls' picks pruned from the backing-store tier and from the host
+ * tier (eval_cb's decode_pruned_nvme / decode_pruned_host). */
+typedef struct nvmoe_prune_args {
+    int32_t* ids;
+    int64_t ids_row_stride;
+    float* weights;
+    int64_t weights_row_stride;
+    int32_t n_tok;
+    int32_t top_k;
+    const int32_t* slot_of_real;       /* [n_expert]: slot or -1 (this layer's table)         */
+    const int32_t* host_slot_of_real;  /* [n_expert]: host slot or -1; NULL: no host tier       */
+    const int32_t* real_in_slot;       /* [cache_size]: expert in each slot or -1              */
+    int32_t cache_size;
+    int32_t n_expert;
+    float nvme_thresh;
+    float host_thresh;
+    float min_mass;
+    int32_t min_keep;
+    int32_t is_decode;
+    int32_t* pruned;
+} nvmoe_prune_args;
+int nvmoe_prune_tail(const nvmoe_prune_args* args, nvmoe_stream_t stream);
+
 /* ================================================================ cache counters
  * eval_cb's GPU-tier statistics (scripts/moe_cache_probe.cpp:253-256): distinct ids found in
  * the slot pool or copied in (:662-671), matched callbacks (:995), the same restricted to decode

@@ -211,6 +211,29 @@ class CacheStats(C.Structure):
         "decode_gpu_misses", "refill_bytes", "error_calls")]
 
 
+class PruneArgs(C.Structure):
+    """nvmoe_prune_args."""
+    _fields_ = [
+        ("ids", C.c_void_p),
+        ("ids_row_stride", C.c_int64),
+        ("weights", C.c_void_p),
+        ("weights_row_stride", C.c_int64),
+        ("n_tok", C.c_int32),
+        ("top_k", C.c_int32),
+        ("slot_of_real", C.c_void_p),
+        ("host_slot_of_real", C.c_void_p),
+        ("real_in_slot", C.c_void_p),
+        ("cache_size", C.c_int32),
+        ("n_expert", C.c_int32),
+        ("nvme_thresh", C.c_float),
+        ("host_thresh", C.c_float),
+        ("min_mass", C.c_float),
+        ("min_keep", C.c_int32),
+        ("is_decode", C.c_int32),
+        ("pruned", C.c_void_p),
+    ]
+
+
 class RouterGateArgs(C.Structure):
     _fields_ = [
         ("resid", C.c_void_p),
@@ -285,6 +308,7 @@ SIGNATURES = {
                                         C.POINTER(C.c_int64)]),
     "nvmoe_cache_stats_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int64,
                                         C.c_void_p]),
+    "nvmoe_prune_tail": (C.c_int, [C.POINTER(PruneArgs), C.c_void_p]),
     "nvmoe_refill_async": (C.c_int, [C.POINTER(RefillBank), C.c_int, C.c_void_p, C.c_void_p,
                                      C.c_int, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                      C.c_void_p]),

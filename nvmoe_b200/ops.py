@@ -411,6 +411,26 @@ def moe_ffn_prefill(pool: ExpertWeights, x: torch.Tensor, slot_ids: torch.Tensor
     return out
 
 
+# ------------------------------------------------------------------ (f)3 tail pruning
+def prune_tail(ids: torch.Tensor, weights: torch.Tensor, table: "SlotTableGPU",
+               nvme_thresh: float, host_thresh: float = 0.0, min_keep: int = 6,
+               min_mass: float = 0.95, host_slot_of_real: torch.Tensor | None = None,
+               is_decode: bool = True, pruned: torch.Tensor | None = None) -> None:
+    """eval_cb's tail pruning (scripts/moe_cache_probe.cpp:523-625) of ids [n, k] (int32) and
+    weights [n, k] (fp32) in place, against this layer's slot table (and the host tier's map
+    host_slot_of_real [E], if any); see nvmoe_prune_tail.  pruned: int32 [2] device counters."""
+    _require_cuda(ids, weights)
+    assert ids.dtype == torch.int32 and weights.dtype == torch.float32
+    assert ids.stride(1) == 1 and weights.stride(1) == 1 and ids.shape == weights.shape
+    n, k = ids.shape
+    args = _lib.PruneArgs(ids.data_ptr(), ids.stride(0), weights.data_ptr(), weights.stride(0),
+                          n, k, table.slot_of_real.data_ptr(), _ptr(host_slot_of_real),
+                          table.real_in_slot.data_ptr(), table.cache_size, table.n_expert,
+                          nvme_thresh, host_thresh, min_mass, min_keep, 1 if is_decode else 0,
+                          _ptr(pruned))
+    check(lib().nvmoe_prune_tail(C.byref(args), _stream()), "nvmoe_prune_tail")
+
+
 # ------------------------------------------------------------------ cache counters
 STATS_FIELDS = tuple(n for n, _ in _lib.CacheStats._fields_)
 

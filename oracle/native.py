@@ -265,3 +265,32 @@ class RefEvalCb:
         d = np.empty(1, np.uint32)
         self.L.ref_evalcb_tables(self.h, a, b, c, d)
         return a, b, c, int(d[0])
+
+
+REF_PRUNE_SO = HERE / "_ref" / "libref_prune.so"
+
+
+def ref_prune(ids, w, slot_of_real, host_slot_of_real, real_in_slot, nvme_thresh, host_thresh,
+              min_keep, min_mass, is_decode=True):
+    """The reference's own tail-pruning block (scripts/moe_cache_probe.cpp:523-625) compiled into
+    oracle/_ref/libref_prune.so by oracle/Makefile; same interface as ref_numpy.prune_tail (the
+    reference always has a host tier map: None becomes all -1)."""
+    if not REF_PRUNE_SO.exists():
+        raise FileNotFoundError(str(REF_PRUNE_SO))
+    L = C.CDLL(str(REF_PRUNE_SO))
+    fn = L.ref_prune
+    fn.restype = None
+    ids = np.ascontiguousarray(ids, np.int32).copy()
+    w = np.ascontiguousarray(w, np.float32).copy()
+    n, k = ids.shape
+    sor = np.ascontiguousarray(slot_of_real, np.int32)
+    hs = (np.full(len(sor), -1, np.int32) if host_slot_of_real is None
+          else np.ascontiguousarray(host_slot_of_real, np.int32))
+    ris = np.ascontiguousarray(real_in_slot, np.int32)
+    pn, ph = C.c_long(0), C.c_long(0)
+    fn(C.c_int(len(sor)), C.c_int(len(ris)), sor.ctypes.data_as(C.c_void_p),
+       hs.ctypes.data_as(C.c_void_p), ris.ctypes.data_as(C.c_void_p),
+       ids.ctypes.data_as(C.c_void_p), w.ctypes.data_as(C.c_void_p), C.c_int(n), C.c_int(k),
+       C.c_float(nvme_thresh), C.c_float(host_thresh), C.c_int(min_keep), C.c_float(min_mass),
+       C.c_int(1 if is_decode else 0), C.byref(pn), C.byref(ph))
+    return ids, w, pn.value, ph.value

@@ -236,3 +236,69 @@ def router_gate_logits(x_bits: np.ndarray, w_bits: np.ndarray,
     if bias is not None:
         lg = lg + np.asarray(bias, np.float64)
     return lg.astype(np.float32)
+
+
+def prune_tail(ids, w, slot_of_real, host_slot_of_real, real_in_slot, nvme_thresh, host_thresh,
+               min_keep, min_mass, is_decode=True):
+    """eval_cb's two-tier cost-aware tail pruning (scripts/moe_cache_probe.cpp:523-625) of ids /
+    weights [n, k], restated with fp32 scalar arithmetic in the reference's order.  Returns the
+    new ids, weights and the (backing-store, host) picks pruned in decode calls.  host_slot_of_real
+    None: no host tier."""
+    f32 = np.float32
+    ids = np.array(ids, np.int32, copy=True)
+    w = np.array(w, np.float32, copy=True)
+    n, k = ids.shape
+    pn = ph = 0
+    if not f32(nvme_thresh) > 0 or n * k > 4096:
+        return ids, w, 0, 0
+    occupied = [int(r) for r in real_in_slot if r != -1]
+    if not occupied:
+        return ids, w, 0, 0
+    resident_real = occupied[0]
+    in_gpu = lambda r: slot_of_real[r] != -1  # noqa: E731
+    in_host = lambda r: host_slot_of_real is not None and host_slot_of_real[r] != -1  # noqa: E731
+    for row in range(n):
+        if ((ids[row] < 0) | (ids[row] >= len(slot_of_real))).any():
+            continue
+        total = f32(0)
+        for i in range(k):
+            total = f32(total + w[row, i])
+        if not total > f32(1e-6):
+            continue
+        gpu_res, in_mem = -1, f32(0)
+        for i in range(k):
+            r = ids[row, i]
+            if in_gpu(r) and gpu_res == -1:
+                gpu_res = int(r)
+            if in_gpu(r) or in_host(r):
+                in_mem = f32(in_mem + f32(w[row, i] / total))
+        alias = gpu_res if gpu_res != -1 else resident_real
+        remaining, kept, modified = f32(1), k, False
+        for j in range(k - 1, -1, -1):
+            if kept <= min_keep:
+                break
+            r = ids[row, j]
+            if in_gpu(r):
+                continue
+            rel = f32(w[row, j] / total)
+            if in_host(r):
+                if f32(host_thresh) > 0 and rel < f32(host_thresh) and \
+                        f32(remaining - rel) >= f32(min_mass):
+                    w[row, j], ids[row, j] = 0, alias
+                    remaining, kept, modified = f32(remaining - rel), kept - 1, True
+                    ph += 1 if is_decode else 0
+                continue
+            should = rel < f32(nvme_thresh) or in_mem >= f32(min_mass)
+            if should and f32(remaining - rel) >= f32(min_mass):
+                w[row, j], ids[row, j] = 0, alias
+                remaining, kept, modified = f32(remaining - rel), kept - 1, True
+                pn += 1 if is_decode else 0
+        if modified:
+            new_total = f32(0)
+            for i in range(k):
+                new_total = f32(new_total + w[row, i])
+            if new_total > f32(1e-6):
+                fac = f32(total / new_total)
+                for i in range(k):
+                    w[row, i] = f32(w[row, i] * fac)
+    return ids, w, pn, ph

@@ -64,7 +64,7 @@ def test_struct_layouts_match_a_c_compiler(tmp_path):
                "nvmoe_router_gate_args": _lib.RouterGateArgs,
                "nvmoe_ep_dispatch_args": _lib.EpDispatchArgs,
                "nvmoe_ep_combine_args": _lib.EpCombineArgs,
-               "nvmoe_cache_stats": _lib.CacheStats}
+               "nvmoe_cache_stats": _lib.CacheStats, "nvmoe_prune_args": _lib.PruneArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nvmoe_b200.h"',
              'int main(void) {']
     for cname, py in mirrors.items():
