@@ -14,6 +14,8 @@ GPU tests never read the reference at run time.
   remap_traces.npz  — seeded routing traces and the CPU oracle's slot maps / miss lists
                       (oracle/remap_lru.c, a restatement of moe_cache_probe.cpp:eval_cb).
   router_golden.npz — seeded logits and the oracle's top-k ids / weights.
+  glm_router_golden.npz — seeded logits and selection biases routed by the reference's own GLM
+                      router (nvme_offload_cache.py:2980-3089), imported with stub modules.
 """
 from __future__ import annotations
 
@@ -215,6 +217,58 @@ def router_golden() -> dict:
     return out
 
 
+def glm_router_reference(ref: Path) -> dict:
+    """Seeded logits routed by the reference's own GLM router (patched_route of
+    install_glm5_pruning_patch, nvme-moe-bench/nvme_offload_cache.py:2980-3089), with a stand-in
+    Glm5NextSparseBlock whose gate is the identity (so F.linear(hidden, gate) returns the logits
+    unchanged) and a top-k override one below the block's top_k (the patched path, not the
+    unpatched FreeToken route it falls back to)."""
+    import os
+
+    import torch
+    _stub_reference_imports()
+
+    class Glm5NextSparseBlock:  # the class the patch wraps (FreeToken, not installed)
+        def _route(self, hidden_states):
+            raise RuntimeError("the unpatched FreeToken route is not available")
+
+    for name in ("freetoken.models", "freetoken.models.glm5_next", "freetoken.server"):
+        sys.modules[name] = types.ModuleType(name)
+    moe = types.ModuleType("freetoken.models.glm5_next.moe")
+    moe.Glm5NextSparseBlock = Glm5NextSparseBlock
+    sys.modules["freetoken.models.glm5_next.moe"] = moe
+    args = types.ModuleType("freetoken.server.args")
+    args.parse_args = lambda *a, **k: None
+    sys.modules["freetoken.server.args"] = args
+    sys.path.insert(0, str(ref / "nvme-moe-bench"))
+    import nvme_offload_cache as noc  # the reference module
+    noc.install_glm5_pruning_patch()
+    route = Glm5NextSparseBlock._route
+    os.environ.pop("FREETOKEN_ROUTER_MIN_PROB", None)
+    os.environ.pop("FREETOKEN_GLM_ROUTER_MIN_PROB", None)
+    rng = np.random.default_rng(11)
+    out = {}
+    for name, E, k, n, norm, scale in (("glm_a", 288, 8, 64, True, 2.5),
+                                       ("glm_b", 256, 8, 16, False, 1.0),
+                                       ("glm_c", 64, 4, 32, True, 1.0)):
+        logits = rng.standard_normal((n, E)).astype(np.float32)
+        bias = (rng.standard_normal(E) * 0.1).astype(np.float32)
+        os.environ["FREETOKEN_TOPK_OVERRIDE"] = str(k)
+        block = types.SimpleNamespace(
+            top_k=k + 1, n_group=1, norm_topk_prob=norm, routed_scaling_factor=scale,
+            gate=types.SimpleNamespace(weight=torch.eye(E, dtype=torch.float32)),
+            e_score_correction_bias=torch.from_numpy(bias))
+        w, ids = route(block, torch.from_numpy(logits))
+        out[f"{name}_meta"] = np.array([E, k, n, int(norm)], np.int32)
+        out[f"{name}_scale"] = np.array([scale], np.float32)
+        out[f"{name}_logits"] = logits
+        out[f"{name}_bias"] = bias
+        out[f"{name}_ids"] = ids.numpy().astype(np.int32)
+        out[f"{name}_w"] = w.numpy().astype(np.float32)
+    os.environ.pop("FREETOKEN_TOPK_OVERRIDE", None)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -224,6 +278,7 @@ def main() -> None:
     np.savez_compressed(HERE / "dequant_golden.npz", **dequant_golden())
     np.savez_compressed(HERE / "remap_traces.npz", **remap_traces())
     np.savez_compressed(HERE / "router_golden.npz", **router_golden())
+    np.savez_compressed(HERE / "glm_router_golden.npz", **glm_router_reference(ref))
     for p in sorted(HERE.glob("*.*")):
         print(f"{p.name:24s} {p.stat().st_size:8d} B")
 

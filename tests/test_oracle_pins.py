@@ -129,3 +129,16 @@ def test_torch_nvfp4_dequant_equals_numpy_restatement():
     nan = np.isnan(a)
     np.testing.assert_array_equal(nan, np.isnan(b))  # scale bytes 0x7F / 0xFF (NaN payloads vary)
     np.testing.assert_array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
+
+
+@pytest.mark.parametrize("case", ["glm_a", "glm_b", "glm_c"])
+def test_glm_router_oracle_matches_the_reference_router(case):
+    """The oracle's sigmoid + selection-bias router against the reference's own GLM router
+    (nvme_offload_cache.py:2980-3089, run by tests/golden/make_golden.py): the same experts in
+    the same order; weights within 2e-6 relative (torch's row sum may add in another order)."""
+    g = np.load(GOLD / "glm_router_golden.npz")
+    E, k, n, norm = (int(v) for v in g[f"{case}_meta"])
+    ids, w, _ = R.router_topk_sigmoid_bias(g[f"{case}_logits"], k, g[f"{case}_bias"],
+                                           bool(norm), float(g[f"{case}_scale"][0]))
+    np.testing.assert_array_equal(ids, g[f"{case}_ids"])
+    np.testing.assert_allclose(w, g[f"{case}_w"], rtol=2e-6, atol=0)
