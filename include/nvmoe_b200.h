@@ -358,7 +358,7 @@ int nvmoe_host_tier_stats(const nvmoe_host_tier* tier, int64_t* host_hits, int64
  * host_thresh, are replaced from the last pick backwards by the row's first slot-resident
  * expert (else the expert of the pool's first occupied slot) with weight 0, keeping at least
  * min_keep picks and min_mass of the weight; the weights are then scaled back to their total.
- * ids / weights [n_tok][top_k] are rewritten in place (row strides in elements).  Like the
+ * ids / weights [n_tok][top_k] (top_k <= 32) are rewritten in place (row strides in elements).  Like the
  * reference, nothing happens unless nvme_thresh > 0, n_tok * top_k <= 4096 and a slot is
  * occupied; rows with an id outside [0, n_expert) are left as they are.  pruned (device, [2],
  * optional) gains the decode calls' picks pruned from the backing-store tier and from the host

@@ -87,9 +87,18 @@ class FtwModel:
         self.n_experts = self.loc[(layers[0], FTW_BANKS[0])].n_rows
 
     def close(self) -> None:
-        for fd in self.fds.values():
+        for fd in getattr(self, "fds", {}).values():
             os.close(fd)
         self.fds = {}
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        self.close()
 
     def read_row(self, layer: int, bank: str, expert: int) -> bytes:
         lc = self.loc[(layer, bank)]
@@ -187,20 +196,29 @@ class InterleavedSidecar:
         try:
             hdr = _pread_exact(self.fd, RPK_HEADER_BYTES, 0)
         except OSError:
-            os.close(self.fd)
+            self.close()
             raise ValueError(f"{path}: shorter than the 4096-byte NVMOERPK header") from None
         magic, version, n_layers, n_experts, _ = _RPK_HEAD.unpack_from(hdr, 0)
         if magic != RPK_MAGIC or version != RPK_VERSION or n_layers > RPK_MAX_LAYERS:
-            os.close(self.fd)
+            self.close()
             raise ValueError(f"{path}: not an NVMOERPK v{RPK_VERSION} file")
         self.n_layers, self.n_experts = n_layers, n_experts
         self.layers = [RpkLayer(*_RPK_LAYER.unpack_from(hdr, _RPK_HEAD.size + i * _RPK_LAYER.size))
                        for i in range(n_layers)]
 
     def close(self) -> None:
-        if self.fd >= 0:
+        if getattr(self, "fd", -1) >= 0:
             os.close(self.fd)
             self.fd = -1
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        self.close()
 
     def read_expert(self, layer: int, expert: int) -> tuple[bytes, bytes, bytes]:
         """(gate, up, down) rows of one expert."""
