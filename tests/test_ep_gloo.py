@@ -1,4 +1,4 @@
-"""Expert-parallel dispatch / combine (nvmoe_b200.ep.ep_layer) on 2 gloo ranks (CPU): every
+"""Expert-parallel dispatch / combine (nvmoe_b200.ep.ep_layer) on 2 and 4 gloo ranks (CPU): every
 rank's output equals the single-process MoE over all experts, with uneven pair counts, a rank
 that receives no pairs, and the shared expert.  The local expert step is a torch stand-in
 (y = w * x @ W_e) so only the host-side partitioning and exchange are under test."""
@@ -62,18 +62,20 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_ep_layer_two_ranks_matches_single_process():
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_layer_ranks_match_single_process(world):
+    """2 and 4 ranks (4: two ranks receive nothing in the skewed case)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in procs)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for r in range(2):
+    for r in range(world):
         assert max(res[r]) < 1e-4, res
 
 
